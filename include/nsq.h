@@ -1,0 +1,148 @@
+/*
+ * nsq.h -- C ABI of libnsq, the B200 (sm_100a) GGUF block-quantized
+ * dequant + matmul library.
+ *
+ * It replaces the Vulkan dequant/matmul dispatch of NodeStor's engine
+ * (nodestor/crates/nodestor-vulkan).  Paths below are relative to the
+ * reference project root.
+ *
+ * Conventions
+ *   - Weights W are GGUF-native: N rows of K weights, each row a run of
+ *     quant blocks along K, exactly the bytes of a GGUF tensor (ggml ne0 = K).
+ *     ggml_type is the GGUF/ggml type id: 2 = Q4_0, 8 = Q8_0, 12 = Q4_K,
+ *     14 = Q6_K.  The weight pointer must be 16-byte aligned (GGUF tensor
+ *     data is 32-byte aligned in the file; cudaMalloc gives 256).
+ *   - q6k_layout selects the meaning of Q6_K bytes: NSQ_Q6K_GGML (what
+ *     llama.cpp writes) or NSQ_Q6K_NODESTOR (the element mapping of the
+ *     reference shader nodestor/crates/nodestor-vulkan/shaders/
+ *     dequant_q6k.comp:50-99).  Ignored for the other types.
+ *   - The matmul semantic is y[M x N] = x[M x K] . W^T (y[m,n] = sum_k
+ *     x[m,k] W[n,k]); the reference's operator takes B = W^T as a [K x N]
+ *     f32 matrix (crates/nodestor-vulkan/shaders/matmul.comp:10-16).
+ *   - All pointers are device pointers owned by the caller.  Calls are
+ *     asynchronous on `stream` (a cudaStream_t; NULL = legacy default
+ *     stream) and allocate no device memory; scratch is passed explicitly.
+ *   - Every entry point returns an NSQ_* status and never aborts.  Argument
+ *     errors are detected on the host before any launch.
+ */
+#ifndef NSQ_H
+#define NSQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NSQ_VERSION 10000 /* 1.0.0 */
+
+/* status codes (mapped to NodeStorError variants by the host wrapper:
+   crates/nodestor-core/src/error.rs:1-38) */
+#define NSQ_OK 0
+#define NSQ_ERR_TYPE 1      /* unsupported ggml_type, q6k_layout or out dtype */
+#define NSQ_ERR_SHAPE 2     /* K not a multiple of the block, M/N/K out of range */
+#define NSQ_ERR_ALIGN 3     /* pointer alignment violated */
+#define NSQ_ERR_NULL 4      /* required pointer is NULL */
+#define NSQ_ERR_CUDA 5      /* CUDA launch/runtime error */
+#define NSQ_ERR_NCCL 6      /* NCCL error in a sharded call */
+#define NSQ_ERR_TIMEOUT 7   /* a bounded device-side wait gave up */
+#define NSQ_ERR_WORKSPACE 8 /* workspace missing or too small */
+#define NSQ_ERR_DEVICE 9    /* current device is not sm_100 */
+
+#define NSQ_TYPE_Q4_0 2
+#define NSQ_TYPE_Q8_0 8
+#define NSQ_TYPE_Q4_K 12
+#define NSQ_TYPE_Q6_K 14
+
+#define NSQ_Q6K_GGML 0
+#define NSQ_Q6K_NODESTOR 1
+
+#define NSQ_OUT_F32 0
+#define NSQ_OUT_BF16 1
+
+/* Largest M accepted by the decode GEMV (batch 1..16). */
+#define NSQ_GEMV_MAX_M 16
+
+/* Library version (NSQ_VERSION). */
+int nsq_version(void);
+
+/* Text of a status code; static storage. */
+const char *nsq_strerror(int status);
+
+/* Bytes of one quant block and weights per block for a ggml type
+ * (0 for unsupported types).  Replaces calculate_tensor_size /
+ * QuantFormat::block_size_bytes (crates/nodestor-formats/src/gguf.rs:288-304,
+ * crates/nodestor-inference/src/dequant/mod.rs:65-85), which have no Q4_K /
+ * Q6_K entries and size Q8_0 at 36 B per 32 weights instead of 34. */
+int64_t nsq_block_bytes(int ggml_type);
+int64_t nsq_block_weights(int ggml_type);
+
+/* Reads and optionally clears the device-side status word that bounded
+ * waits inside kernels set (NSQ_ERR_TIMEOUT).  Synchronises the device. */
+int nsq_device_status(int clear);
+
+/*
+ * Dequantize n_elems weights (a whole number of blocks) to f32 or bf16.
+ * f32 results are bit-exact to the reference's dequant:
+ *   Q8_0  crates/nodestor-inference/src/dequant/q8_0.rs:14-28
+ *   Q4_K  crates/nodestor-inference/src/dequant/q4_k.rs:56-131
+ *   Q4_0  crates/nodestor-vulkan/shaders/dequant_q4.comp:40-61
+ *   Q6_K  crates/nodestor-vulkan/shaders/dequant_q6k.comp:50-99 (NODESTOR)
+ * with IEEE fp16 scales (dequant/mod.rs:234-260).  bf16 is the f32 value
+ * rounded to nearest-even.  Replaces DequantDispatcher::dequantize
+ * (dequant/mod.rs:142-191) and the never-dispatched dequant pipelines
+ * (crates/nodestor-vulkan/src/pipeline.rs:160-214, 1220-1252).
+ */
+int nsq_dequant(const void *w, int ggml_type, int q6k_layout, int out_dtype, void *out,
+                int64_t n_elems, void *stream);
+
+/*
+ * Decode GEMV, batch M in 1..16: y[M x N] f32 = x[M x K] f32 . W^T,
+ * fp32 output within 1e-3 relative error of the reference composition
+ * cpu_matmul_f32(x, transpose(dequant(W))) (crates/nodestor-vulkan/src/
+ * pipeline.rs:1256-1268).  Replaces VulkanEngine::matmul
+ * (crates/nodestor-vulkan/src/lib.rs:117-122) on quantized weights and the
+ * TensorOp::Matmul{quantized} dispatch (src/operator_registry.rs:246-259).
+ *
+ * Activations are first split into per-32 scaled int16 limbs in `workspace`
+ * (nsq_gemv_workspace_size bytes, 16-byte aligned); the GEMV itself
+ * accumulates exact integer dot products per 32 weights and combines them
+ * in fp32.
+ */
+size_t nsq_gemv_workspace_size(int64_t M, int64_t K);
+int nsq_gemv(const void *w, int ggml_type, int q6k_layout, const float *x, float *y, int64_t M,
+             int64_t N, int64_t K, void *workspace, size_t workspace_bytes, void *stream);
+
+/* The two halves of nsq_gemv, so that projections sharing one activation
+ * (q|k|v, gate|up) prepare it once: */
+int nsq_prepare_activations(const float *x, int64_t M, int64_t K, void *workspace,
+                            size_t workspace_bytes, void *stream);
+int nsq_gemv_prepared(const void *w, int ggml_type, int q6k_layout, const void *workspace,
+                      float *y, int64_t M, int64_t N, int64_t K, void *stream);
+
+/*
+ * Prefill GEMM on tcgen05 tensor cores: y[M x N] bf16 = x[M x K] bf16 . W^T,
+ * weights dequantized to bf16 in shared memory, fp32 accumulation in TMEM.
+ * Within 2e-2 relative error of the reference composition on the same
+ * (bf16-valued) inputs.  x must be 16-byte aligned with K % 64 == 0; y must
+ * be 16-byte aligned.  Same reference operator as nsq_gemv, for M > 16.
+ */
+int nsq_gemm_bf16(const void *w, int ggml_type, int q6k_layout, const void *x_bf16, void *y_bf16,
+                  int64_t M, int64_t N, int64_t K, void *stream);
+
+/*
+ * Dense f32 matmul with the reference operator's own layout:
+ * C[M x N] = A[M x K] . B[K x N], all row-major f32
+ * (crates/nodestor-vulkan/shaders/matmul.comp:27-68,
+ * crates/nodestor-vulkan/src/lib.rs:117-122).  For the unquantized (F32)
+ * weights the reference engine also routes through `matmul`.
+ */
+int nsq_matmul_f32(const float *a, const float *b, float *c, int64_t M, int64_t K, int64_t N,
+                   void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NSQ_H */

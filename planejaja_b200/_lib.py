@@ -1,0 +1,86 @@
+"""ctypes binding of libnsq.so (the C ABI in include/nsq.h).
+
+The library is built in-tree (planejaja_b200/libnsq.so) by
+`python -m planejaja_b200.build` or `make -C planejaja_b200/csrc`.  There is
+no fallback: if the shared library is missing or fails to load, every
+compute call raises NsqError.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libnsq.so")
+
+OK = 0
+ERR_TYPE = 1
+ERR_SHAPE = 2
+ERR_ALIGN = 3
+ERR_NULL = 4
+ERR_CUDA = 5
+ERR_NCCL = 6
+ERR_TIMEOUT = 7
+ERR_WORKSPACE = 8
+ERR_DEVICE = 9
+
+OUT_F32 = 0
+OUT_BF16 = 1
+GEMV_MAX_M = 16
+
+# (name, restype, argtypes) for every symbol declared in include/nsq.h
+_vp, _i64, _int, _sz = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_size_t
+SIGNATURES = [
+    ("nsq_version", _int, []),
+    ("nsq_strerror", ctypes.c_char_p, [_int]),
+    ("nsq_block_bytes", _i64, [_int]),
+    ("nsq_block_weights", _i64, [_int]),
+    ("nsq_device_status", _int, [_int]),
+    ("nsq_dequant", _int, [_vp, _int, _int, _int, _vp, _i64, _vp]),
+    ("nsq_gemv_workspace_size", _sz, [_i64, _i64]),
+    ("nsq_gemv", _int, [_vp, _int, _int, _vp, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),
+    ("nsq_prepare_activations", _int, [_vp, _i64, _i64, _vp, _sz, _vp]),
+    ("nsq_gemv_prepared", _int, [_vp, _int, _int, _vp, _vp, _i64, _i64, _i64, _vp]),
+    ("nsq_gemm_bf16", _int, [_vp, _int, _int, _vp, _vp, _i64, _i64, _i64, _vp]),
+    ("nsq_matmul_f32", _int, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+]
+
+
+class NsqError(RuntimeError):
+    def __init__(self, status: int, what: str = ""):
+        self.status = status
+        msg = strerror(status) if _lib_or_none() is not None else f"status {status}"
+        super().__init__(f"{what}: {msg} (status {status})" if what else f"{msg} (status {status})")
+
+
+_lib = None
+_load_error = None
+
+
+def _lib_or_none():
+    return _lib
+
+
+def load():
+    """Load libnsq.so once; raises NsqError-like RuntimeError if absent."""
+    global _lib, _load_error
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(f"libnsq.so not built (expected at {LIB_PATH}); run `python -m planejaja_b200.build`")
+    L = ctypes.CDLL(LIB_PATH)
+    for name, res, args in SIGNATURES:
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def strerror(status: int) -> str:
+    return load().nsq_strerror(status).decode()
+
+
+def check(status: int, what: str = "") -> None:
+    if status != OK:
+        raise NsqError(status, what)

@@ -1,0 +1,208 @@
+// api.cu -- the extern "C" entry points of libnsq (declared in include/nsq.h).
+//
+// Every entry point validates its arguments on the host (types, shapes,
+// alignment, workspace size, device) and returns an NSQ_* status before
+// launching anything; CUDA launch errors become NSQ_ERR_CUDA.  Nothing here
+// allocates device memory.
+#include <mutex>
+
+#include "nsq_common.cuh"
+
+namespace nsq {
+__device__ int g_device_status = 0;
+
+cudaError_t launch_dequant(const uint8_t* w, int type, int layout, int out_dtype, void* out, int64_t n_elems,
+                           cudaStream_t st, int num_sms);
+cudaError_t launch_prepare_x(const float* x, XGroup* xg, int64_t M, int64_t K, cudaStream_t st, int num_sms);
+int run_gemv(const uint8_t* w, int type, int layout, const XGroup* xg, float* y, int64_t M, int64_t N, int64_t K,
+             cudaStream_t st, int num_sms);
+int run_gemm_bf16(const uint8_t* w, int type, int layout, const void* x, void* y, int64_t M, int64_t N, int64_t K,
+                  cudaStream_t st, int num_sms);
+cudaError_t launch_matmul_f32(const float* a, const float* b, float* c, int64_t M, int64_t K, int64_t N,
+                              cudaStream_t st);
+
+struct DevInfo {
+  int num_sms = 0;
+  int cc_major = 0;
+};
+
+static DevInfo dev_info() {
+  static std::mutex mu;
+  static DevInfo cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return DevInfo{};
+  std::lock_guard<std::mutex> lk(mu);
+  if (cache[dev].num_sms == 0) {
+    int sms = 0, major = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return DevInfo{};
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return DevInfo{};
+    cache[dev].num_sms = sms;
+    cache[dev].cc_major = major;
+  }
+  return cache[dev];
+}
+
+static bool type_ok(int t) {
+  return t == NSQ_TYPE_Q4_0 || t == NSQ_TYPE_Q8_0 || t == NSQ_TYPE_Q4_K || t == NSQ_TYPE_Q6_K;
+}
+
+static int check_device(DevInfo& di) {
+  di = dev_info();
+  if (di.num_sms == 0) return NSQ_ERR_CUDA;
+  if (di.cc_major != 10) return NSQ_ERR_DEVICE;
+  return NSQ_OK;
+}
+
+static int check_weights(const void* w, int type, int layout, int64_t K) {
+  if (!type_ok(type)) return NSQ_ERR_TYPE;
+  if (type == NSQ_TYPE_Q6_K && layout != NSQ_Q6K_GGML && layout != NSQ_Q6K_NODESTOR) return NSQ_ERR_TYPE;
+  if (!w) return NSQ_ERR_NULL;
+  if (reinterpret_cast<uintptr_t>(w) & 15) return NSQ_ERR_ALIGN;
+  const int64_t qk = nsq_block_weights(type);
+  if (K <= 0 || K % qk) return NSQ_ERR_SHAPE;
+  return NSQ_OK;
+}
+
+}  // namespace nsq
+
+using namespace nsq;
+
+extern "C" {
+
+int nsq_version(void) { return NSQ_VERSION; }
+
+const char* nsq_strerror(int status) {
+  switch (status) {
+    case NSQ_OK: return "ok";
+    case NSQ_ERR_TYPE: return "unsupported ggml type, Q6_K layout or output dtype";
+    case NSQ_ERR_SHAPE: return "bad shape (K not a multiple of the block size, or M/N/K out of range)";
+    case NSQ_ERR_ALIGN: return "pointer alignment violated";
+    case NSQ_ERR_NULL: return "required pointer is NULL";
+    case NSQ_ERR_CUDA: return "CUDA error";
+    case NSQ_ERR_NCCL: return "NCCL error";
+    case NSQ_ERR_TIMEOUT: return "device-side wait timed out";
+    case NSQ_ERR_WORKSPACE: return "workspace missing or too small";
+    case NSQ_ERR_DEVICE: return "current device is not sm_100";
+    default: return "unknown status";
+  }
+}
+
+int64_t nsq_block_bytes(int ggml_type) {
+  switch (ggml_type) {
+    case NSQ_TYPE_Q4_0: return 18;
+    case NSQ_TYPE_Q8_0: return 34;
+    case NSQ_TYPE_Q4_K: return 144;
+    case NSQ_TYPE_Q6_K: return 210;
+    default: return 0;
+  }
+}
+
+int64_t nsq_block_weights(int ggml_type) {
+  switch (ggml_type) {
+    case NSQ_TYPE_Q4_0:
+    case NSQ_TYPE_Q8_0: return 32;
+    case NSQ_TYPE_Q4_K:
+    case NSQ_TYPE_Q6_K: return 256;
+    default: return 0;
+  }
+}
+
+int nsq_device_status(int clear) {
+  int v = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess) return NSQ_ERR_CUDA;
+  if (cudaMemcpyFromSymbol(&v, g_device_status, sizeof(int)) != cudaSuccess) return NSQ_ERR_CUDA;
+  if (clear) {
+    const int z = 0;
+    if (cudaMemcpyToSymbol(g_device_status, &z, sizeof(int)) != cudaSuccess) return NSQ_ERR_CUDA;
+  }
+  return v;
+}
+
+int nsq_dequant(const void* w, int ggml_type, int q6k_layout, int out_dtype, void* out, int64_t n_elems,
+                void* stream) {
+  if (out_dtype != NSQ_OUT_F32 && out_dtype != NSQ_OUT_BF16) return NSQ_ERR_TYPE;
+  const int64_t qk = nsq_block_weights(ggml_type);
+  int rc = check_weights(w, ggml_type, q6k_layout, qk ? qk : 1);
+  if (rc) return rc;
+  if (n_elems < 0 || n_elems % qk) return NSQ_ERR_SHAPE;
+  if (!out) return NSQ_ERR_NULL;
+  if (reinterpret_cast<uintptr_t>(out) & (out_dtype == NSQ_OUT_F32 ? 3 : 1)) return NSQ_ERR_ALIGN;
+  DevInfo di;
+  if ((rc = check_device(di))) return rc;
+  if (n_elems == 0) return NSQ_OK;
+  cudaError_t e = launch_dequant(static_cast<const uint8_t*>(w), ggml_type, q6k_layout, out_dtype, out, n_elems,
+                                 static_cast<cudaStream_t>(stream), di.num_sms);
+  return e == cudaSuccess ? NSQ_OK : NSQ_ERR_CUDA;
+}
+
+size_t nsq_gemv_workspace_size(int64_t M, int64_t K) {
+  if (M <= 0 || K <= 0 || K % 32) return 0;
+  return (size_t)(M * (K / 32)) * sizeof(XGroup);
+}
+
+int nsq_prepare_activations(const float* x, int64_t M, int64_t K, void* workspace, size_t workspace_bytes,
+                            void* stream) {
+  if (M < 1 || M > NSQ_GEMV_MAX_M || K <= 0 || K % 32) return NSQ_ERR_SHAPE;
+  if (!x || !workspace) return x ? NSQ_ERR_WORKSPACE : NSQ_ERR_NULL;
+  if (reinterpret_cast<uintptr_t>(x) & 3) return NSQ_ERR_ALIGN;
+  if (reinterpret_cast<uintptr_t>(workspace) & 15) return NSQ_ERR_ALIGN;
+  if (workspace_bytes < nsq_gemv_workspace_size(M, K)) return NSQ_ERR_WORKSPACE;
+  DevInfo di;
+  int rc = check_device(di);
+  if (rc) return rc;
+  cudaError_t e = launch_prepare_x(x, static_cast<XGroup*>(workspace), M, K, static_cast<cudaStream_t>(stream),
+                                   di.num_sms);
+  return e == cudaSuccess ? NSQ_OK : NSQ_ERR_CUDA;
+}
+
+int nsq_gemv_prepared(const void* w, int ggml_type, int q6k_layout, const void* workspace, float* y, int64_t M,
+                      int64_t N, int64_t K, void* stream) {
+  int rc = check_weights(w, ggml_type, q6k_layout, K);
+  if (rc) return rc;
+  if (M < 1 || M > NSQ_GEMV_MAX_M || N < 1) return NSQ_ERR_SHAPE;
+  if (!workspace) return NSQ_ERR_WORKSPACE;
+  if (!y) return NSQ_ERR_NULL;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 15) || (reinterpret_cast<uintptr_t>(y) & 3)) return NSQ_ERR_ALIGN;
+  DevInfo di;
+  if ((rc = check_device(di))) return rc;
+  return run_gemv(static_cast<const uint8_t*>(w), ggml_type, q6k_layout, static_cast<const XGroup*>(workspace), y,
+                  M, N, K, static_cast<cudaStream_t>(stream), di.num_sms);
+}
+
+int nsq_gemv(const void* w, int ggml_type, int q6k_layout, const float* x, float* y, int64_t M, int64_t N,
+             int64_t K, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_weights(w, ggml_type, q6k_layout, K);
+  if (rc) return rc;
+  if (M < 1 || M > NSQ_GEMV_MAX_M || N < 1) return NSQ_ERR_SHAPE;
+  if (!y) return NSQ_ERR_NULL;
+  if ((rc = nsq_prepare_activations(x, M, K, workspace, workspace_bytes, stream))) return rc;
+  return nsq_gemv_prepared(w, ggml_type, q6k_layout, workspace, y, M, N, K, stream);
+}
+
+int nsq_gemm_bf16(const void* w, int ggml_type, int q6k_layout, const void* x_bf16, void* y_bf16, int64_t M,
+                  int64_t N, int64_t K, void* stream) {
+  int rc = check_weights(w, ggml_type, q6k_layout, K);
+  if (rc) return rc;
+  if (M < 1 || N < 1 || K % 64) return NSQ_ERR_SHAPE;
+  if (M > (int64_t)1 << 24 || N > (int64_t)1 << 24) return NSQ_ERR_SHAPE;
+  if (!x_bf16 || !y_bf16) return NSQ_ERR_NULL;
+  if ((reinterpret_cast<uintptr_t>(x_bf16) & 15) || (reinterpret_cast<uintptr_t>(y_bf16) & 15)) return NSQ_ERR_ALIGN;
+  DevInfo di;
+  if ((rc = check_device(di))) return rc;
+  return run_gemm_bf16(static_cast<const uint8_t*>(w), ggml_type, q6k_layout, x_bf16, y_bf16, M, N, K,
+                       static_cast<cudaStream_t>(stream), di.num_sms);
+}
+
+int nsq_matmul_f32(const float* a, const float* b, float* c, int64_t M, int64_t K, int64_t N, void* stream) {
+  if (M < 1 || K < 1 || N < 1) return NSQ_ERR_SHAPE;
+  if (!a || !b || !c) return NSQ_ERR_NULL;
+  if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) | reinterpret_cast<uintptr_t>(c)) & 3)
+    return NSQ_ERR_ALIGN;
+  DevInfo di;
+  int rc = check_device(di);
+  if (rc) return rc;
+  cudaError_t e = launch_matmul_f32(a, b, c, M, K, N, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? NSQ_OK : NSQ_ERR_CUDA;
+}
+
+}  // extern "C"

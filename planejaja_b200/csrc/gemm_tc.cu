@@ -1,0 +1,463 @@
+// gemm_tc.cu -- prefill GEMM on 5th-generation tensor cores (tcgen05).
+//
+//   y[M x N] (bf16) = x[M x K] (bf16) . W^T,   W: N rows of GGUF blocks
+//
+// "Swap-AB" tiling: the weights are the UMMA M side (128 rows of W per CTA),
+// the tokens the UMMA N side (TOK = 128 or 256 per CTA), so D = W_tile .
+// x_tile^T is a [128 x TOK] fp32 accumulator in tensor memory (TOK columns).
+// K advances in blocks of 64 (one 128-byte swizzle atom of bf16).
+//
+// Warp roles (384 threads):
+//   warp 0      : TMA producer -- one thread loads the x tile [TOK x 64]
+//                 (2-D tiled bulk tensor copy, 128B swizzle) per K block.
+//   warp 1      : allocates TMEM; one thread issues 4 tcgen05.mma
+//                 (kind::f16, bf16 inputs, fp32 accumulate, K = 16 each)
+//                 per K block and commits them to the stage's "empty"
+//                 barrier, and finally to the accumulator barrier.
+//   warps 4..11 : dequant producers -- 2 threads per W row turn the GGUF
+//                 blocks of the K block into bf16 and store them in the
+//                 same 128B-swizzled K-major layout TMA uses; then the
+//                 epilogue: tcgen05.ld of the accumulator, bf16 convert,
+//                 store to y.
+// Stages form a 4-deep ring guarded by mbarriers.  Every wait is bounded
+// (%globaltimer); a wait that gives up records NSQ_ERR_TIMEOUT and the
+// kernel winds down instead of hanging.
+//
+// Weights are dequantized with the same formulas (and roundings) as the
+// standalone dequant, then rounded to bf16.  The reference computes the
+// contraction in f32 (crates/nodestor-vulkan/src/pipeline.rs:1256-1268);
+// the bf16 operands here bound the error at about 2^-8 relative per term,
+// checked at a 2e-2 tolerance.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "nsq_common.cuh"
+
+namespace nsq {
+
+constexpr int GEMM_BM = 128;   // W rows per CTA (UMMA M)
+constexpr int GEMM_BK = 64;    // K per stage (bf16: 128 bytes per row)
+constexpr int GEMM_STAGES = 4;
+constexpr int GEMM_THREADS = 384;
+constexpr int GEMM_DQ_WARP0 = 4;  // first dequant / epilogue warp
+constexpr int GEMM_DQ_THREADS = 256;
+
+// ---------------------------------------------------------------------------
+// tcgen05 / TMA PTX wrappers
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_ld_32x32b_x32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+        "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+        "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// UMMA shared-memory descriptor: K-major, 128B swizzle, 8-row groups 1024 B
+// apart (SBO), LBO unused (1), descriptor version 1.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr & 0x3FFFF) >> 4);  // start address
+  d |= (uint64_t)1 << 16;                       // LBO (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;             // SBO
+  d |= (uint64_t)1 << 46;                       // version
+  d |= (uint64_t)2 << 61;                       // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor, kind::f16: D f32, A = B = bf16, both K-major.
+__host__ __device__ constexpr uint32_t umma_idesc_bf16(int m, int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+// ---------------------------------------------------------------------------
+// Dequant of 32 weights of one row for one 64-wide K block, as bf16 pairs in
+// K order.  chunk[i] (i < 4) is the 16-byte chunk index (0..7) of the 64-wide
+// row segment that pair-group i (8 bf16) belongs to.
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t ldg_u16(const uint8_t* p) {
+  return __ldg(reinterpret_cast<const unsigned short*>(p));
+}
+
+template <int TYPE, int LAYOUT>
+__device__ __forceinline__ void dequant_row_kblock(const uint8_t* __restrict__ row, int kb, int h, uint32_t (&out)[16],
+                                                   int (&chunk)[4]) {
+  float v[32];
+  if constexpr (TYPE == NSQ_TYPE_Q4_K) {
+    const int b = kb >> 2, p = kb & 3;
+    const uint8_t* blk = row + (int64_t)b * 144;
+    const uint4 hdr = __ldg(reinterpret_cast<const uint4*>(blk));
+    const uint4 q = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 32 * p + 16 * h));
+    const float d = h2f((uint16_t)(hdr.x & 0xFFFF)), dmin = h2f((uint16_t)(hdr.x >> 16));
+    uint32_t sc[2], mn[2];
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      const int j = 2 * p + s;
+      if (j < 4) {
+        sc[s] = (hdr.y >> (8 * j)) & 63;
+        mn[s] = (hdr.z >> (8 * j)) & 63;
+      } else {
+        const int sh = 8 * (j - 4);
+        const uint32_t b2 = (hdr.w >> sh) & 0xFF, b0 = (hdr.y >> sh) & 0xFF, b1 = (hdr.z >> sh) & 0xFF;
+        sc[s] = (b2 & 0xF) | ((b0 >> 6) << 4);
+        mn[s] = (b2 >> 4) | ((b1 >> 6) << 4);
+      }
+    }
+    const float d1 = __fmul_rn(d, (float)sc[0]), m1 = __fmul_rn(dmin, (float)mn[0]);
+    const float d2 = __fmul_rn(d, (float)sc[1]), m2 = __fmul_rn(dmin, (float)mn[1]);
+    const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const uint32_t byte = (qw[i >> 2] >> (8 * (i & 3))) & 0xFF;
+      v[i] = __fsub_rn(__fmul_rn(d1, (float)(byte & 0xF)), m1);
+      v[16 + i] = __fsub_rn(__fmul_rn(d2, (float)(byte >> 4)), m2);
+    }
+    chunk[0] = 2 * h; chunk[1] = 2 * h + 1; chunk[2] = 4 + 2 * h; chunk[3] = 5 + 2 * h;
+  } else if constexpr (TYPE == NSQ_TYPE_Q6_K) {
+    const int b = kb >> 2, q = kb & 3;
+    const uint8_t* blk = row + (int64_t)b * 210;
+    const float d = h2f((uint16_t)ldg_u16(blk + 208));
+    if constexpr (LAYOUT == NSQ_Q6K_NODESTOR) {
+      // elements e = 64q + 32h + l: ql[e>>1], qh[e>>2], scale byte [e>>4]
+      const uint8_t* ql = blk + 32 * q + 16 * h;
+      const uint8_t* qh = blk + 128 + 16 * q + 8 * h;
+      const uint32_t s01 = ldg_u16(blk + 192 + 4 * q + 2 * h);
+      const float sa = __fmul_rn(d, (float)((int)(s01 & 0xFF) - 128) / 64.0f);
+      const float sb = __fmul_rn(d, (float)((int)(s01 >> 8) - 128) / 64.0f);
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        const uint32_t l2 = ldg_u16(ql + 2 * t);  // elements 4t .. 4t+3
+        const uint32_t hb = (t & 1) ? (ldg_u16(qh + (t & ~1)) >> 8) : (ldg_u16(qh + t) & 0xFF);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const uint32_t lo = (l2 >> (4 * e)) & 0xF;  // byte e>>1, nibble e&1
+          const uint32_t hi = (hb >> (2 * e)) & 3;
+          const int qq = (int)(lo | (hi << 4)) - 32;
+          v[4 * t + e] = __fmul_rn(t < 4 ? sa : sb, (float)qq);
+        }
+      }
+    } else {
+      // ggml: n = q>>1, group j = 2(q&1) + h; ql[64n + 32h + l] nibble (q&1),
+      // qh[32n + l] bits 2j, scale int8 sc[8n + l/16 + 2j]
+      const int n = q >> 1, j = 2 * (q & 1) + h, nib = q & 1;
+      const uint8_t* ql = blk + 64 * n + 32 * h;
+      const uint8_t* qh = blk + 128 + 32 * n;
+      const uint32_t s01 = ldg_u16(blk + 192 + 8 * n + 2 * j);
+      const float sa = __fmul_rn(d, (float)(int8_t)(s01 & 0xFF));
+      const float sb = __fmul_rn(d, (float)(int8_t)(s01 >> 8));
+#pragma unroll
+      for (int t = 0; t < 16; ++t) {
+        const uint32_t l2 = ldg_u16(ql + 2 * t), h2 = ldg_u16(qh + 2 * t);
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const uint32_t lo = ((l2 >> (8 * e)) >> (4 * nib)) & 0xF;
+          const uint32_t hi = ((h2 >> (8 * e)) >> (2 * j)) & 3;
+          const int qq = (int)(lo | (hi << 4)) - 32;
+          v[2 * t + e] = __fmul_rn(t < 8 ? sa : sb, (float)qq);
+        }
+      }
+    }
+    chunk[0] = 4 * h; chunk[1] = 4 * h + 1; chunk[2] = 4 * h + 2; chunk[3] = 4 * h + 3;
+  } else if constexpr (TYPE == NSQ_TYPE_Q4_0) {
+    const uint8_t* blk = row + (int64_t)(2 * kb + h) * 18;
+    const float d = h2f((uint16_t)ldg_u16(blk));
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      const uint32_t b2 = ldg_u16(blk + 2 + 2 * t);
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const uint32_t byte = (b2 >> (8 * e)) & 0xFF;
+        v[2 * t + e] = __fmul_rn((float)((int)(byte & 0xF) - 8), d);
+        v[16 + 2 * t + e] = __fmul_rn((float)((int)(byte >> 4) - 8), d);
+      }
+    }
+    chunk[0] = 4 * h; chunk[1] = 4 * h + 1; chunk[2] = 4 * h + 2; chunk[3] = 4 * h + 3;
+  } else {  // Q8_0
+    const uint8_t* blk = row + (int64_t)(2 * kb + h) * 34;
+    const float d = h2f((uint16_t)ldg_u16(blk));
+#pragma unroll
+    for (int t = 0; t < 16; ++t) {
+      const uint32_t b2 = ldg_u16(blk + 2 + 2 * t);
+      v[2 * t] = __fmul_rn(d, (float)(int8_t)(b2 & 0xFF));
+      v[2 * t + 1] = __fmul_rn(d, (float)(int8_t)(b2 >> 8));
+    }
+    chunk[0] = 4 * h; chunk[1] = 4 * h + 1; chunk[2] = 4 * h + 2; chunk[3] = 4 * h + 3;
+  }
+#pragma unroll
+  for (int i = 0; i < 16; ++i) out[i] = pack_bf16(v[2 * i], v[2 * i + 1]);
+}
+
+// ---------------------------------------------------------------------------
+struct GemmParams {
+  const uint8_t* w;
+  __nv_bfloat16* y;
+  int64_t M, N, K, RB;
+};
+
+template <int TYPE, int LAYOUT, int TOK>
+__global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap xmap,
+                                                                   const GemmParams p) {
+  constexpr uint32_t W_STAGE = GEMM_BM * 128;  // bytes
+  constexpr uint32_t X_STAGE = TOK * 128;
+  constexpr uint32_t IDESC = umma_idesc_bf16(GEMM_BM, TOK);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* w_sm = smem;
+  uint8_t* x_sm = smem + GEMM_STAGES * W_STAGE;
+  uint64_t* full = reinterpret_cast<uint64_t*>(x_sm + GEMM_STAGES * X_STAGE);
+  uint64_t* empty = full + GEMM_STAGES;
+  uint64_t* accum = empty + GEMM_STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  __shared__ int s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t n0 = (int64_t)blockIdx.x * GEMM_BM;
+  const int m0 = (int)blockIdx.y * TOK;
+  const int KB = (int)(p.K / GEMM_BK);
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    for (int s = 0; s < GEMM_STAGES; ++s) {
+      mbar_init(&full[s], 1 + GEMM_DQ_THREADS / 32);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum, 1);
+    fence_mbar_init();
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TOK);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_d = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int kb = 0; kb < KB; ++kb) {
+        const int s = kb % GEMM_STAGES;
+        const uint32_t par = (uint32_t)((kb / GEMM_STAGES) & 1);
+        if (!mbar_wait_bounded(&empty[s], par ^ 1)) {
+          s_abort = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&full[s], X_STAGE);
+        tma_load_2d(x_sm + s * X_STAGE, &xmap, kb * GEMM_BK, m0, &full[s]);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t w_base = smem_u32(w_sm), x_base = smem_u32(x_sm);
+      bool ok = true;
+      for (int kb = 0; kb < KB; ++kb) {
+        const int s = kb % GEMM_STAGES;
+        const uint32_t par = (uint32_t)((kb / GEMM_STAGES) & 1);
+        if (!mbar_wait_bounded(&full[s], par)) {
+          s_abort = 1;
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < GEMM_BK / 16; ++kk) {
+          const uint64_t ad = umma_desc_sw128(w_base + s * W_STAGE + kk * 32);
+          const uint64_t bd = umma_desc_sw128(x_base + s * X_STAGE + kk * 32);
+          tc_mma_bf16(tmem_d, ad, bd, IDESC, (kb | kk) != 0 ? 1u : 0u);
+        }
+        tc_commit(&empty[s]);
+      }
+      if (ok) tc_commit(accum);
+    }
+  } else if (warp >= GEMM_DQ_WARP0) {
+    const int t = threadIdx.x - GEMM_DQ_WARP0 * 32;  // 0..255
+    const int r = t >> 1, h = t & 1;
+    const int64_t grow = n0 + r;
+    const uint8_t* rowp = p.w + (grow < p.N ? grow : 0) * p.RB;
+    bool ok = true;
+    for (int kb = 0; kb < KB; ++kb) {
+      const int s = kb % GEMM_STAGES;
+      const uint32_t par = (uint32_t)((kb / GEMM_STAGES) & 1);
+      uint32_t pk[16];
+      int chunk[4];
+      if (grow < p.N) {
+        dequant_row_kblock<TYPE, LAYOUT>(rowp, kb, h, pk, chunk);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pk[i] = 0u;
+        chunk[0] = 4 * h; chunk[1] = 4 * h + 1; chunk[2] = 4 * h + 2; chunk[3] = 4 * h + 3;
+      }
+      if (!mbar_wait_bounded(&empty[s], par ^ 1)) {
+        s_abort = 1;
+        ok = false;
+        break;
+      }
+      uint8_t* dst = w_sm + s * W_STAGE + r * 128;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int c = chunk[i] ^ (r & 7);
+        *reinterpret_cast<uint4*>(dst + c * 16) = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full[s]);
+    }
+    // epilogue
+    if (ok && mbar_wait_bounded(accum, 0)) {
+      tc_fence_after();
+      const int q = warp & 3;
+      const int half = (warp - GEMM_DQ_WARP0) >> 2;
+      const int64_t n = n0 + 32 * q + lane;
+#pragma unroll 1
+      for (int c0 = half * (TOK / 2); c0 < (half + 1) * (TOK / 2); c0 += 32) {
+        uint32_t v[32];
+        tc_ld_32x32b_x32(tmem_d + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
+        if (n < p.N) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int64_t m = (int64_t)m0 + c0 + j;
+            if (m < p.M) p.y[m * p.N + n] = __float2bfloat16_rn(__uint_as_float(v[j]));
+          }
+        }
+      }
+    } else {
+      s_abort = 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_d, TOK);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+template <int TOK>
+static size_t gemm_smem_bytes() {
+  return 1024 + (size_t)GEMM_STAGES * (GEMM_BM * 128 + TOK * 128) + (2 * GEMM_STAGES + 1) * 8 + 16;
+}
+
+template <int TYPE, int LAYOUT, int TOK>
+static int launch_gemm_t(const CUtensorMap& map, const GemmParams& p, cudaStream_t st) {
+  auto kern = gemm_tc_kernel<TYPE, LAYOUT, TOK>;
+  const size_t smem = gemm_smem_bytes<TOK>();
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return NSQ_ERR_CUDA;
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  dim3 grid((unsigned)((p.N + GEMM_BM - 1) / GEMM_BM), (unsigned)((p.M + TOK - 1) / TOK));
+  if (grid.y > 65535) return NSQ_ERR_SHAPE;
+  kern<<<grid, GEMM_THREADS, smem, st>>>(map, p);
+  return cudaGetLastError() == cudaSuccess ? NSQ_OK : NSQ_ERR_CUDA;
+}
+
+template <int TYPE, int LAYOUT>
+static int run_gemm_t(const CUtensorMap& map128, const CUtensorMap& map256, const GemmParams& p, cudaStream_t st) {
+  if (p.M <= 128) return launch_gemm_t<TYPE, LAYOUT, 128>(map128, p, st);
+  return launch_gemm_t<TYPE, LAYOUT, 256>(map256, p, st);
+}
+
+static int encode_xmap(CUtensorMap* map, const void* x, int64_t M, int64_t K, int box_rows) {
+  auto enc = get_encode_fn();
+  if (!enc) return NSQ_ERR_CUDA;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
+  cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  cuuint32_t box[2] = {(cuuint32_t)GEMM_BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? NSQ_OK : NSQ_ERR_CUDA;
+}
+
+int run_gemm_bf16(const uint8_t* w, int type, int layout, const void* x, void* y, int64_t M, int64_t N, int64_t K,
+                  cudaStream_t st, int /*num_sms*/) {
+  if (K % GEMM_BK) return NSQ_ERR_SHAPE;
+  GemmParams p{};
+  p.w = w;
+  p.y = static_cast<__nv_bfloat16*>(y);
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.RB = (K / nsq_block_weights(type)) * nsq_block_bytes(type);
+  alignas(64) CUtensorMap map{};
+  const int tok = M <= 128 ? 128 : 256;
+  int rc = encode_xmap(&map, x, M, K, tok);
+  if (rc) return rc;
+  switch (type) {
+    case NSQ_TYPE_Q4_0: return run_gemm_t<NSQ_TYPE_Q4_0, 0>(map, map, p, st);
+    case NSQ_TYPE_Q8_0: return run_gemm_t<NSQ_TYPE_Q8_0, 0>(map, map, p, st);
+    case NSQ_TYPE_Q4_K: return run_gemm_t<NSQ_TYPE_Q4_K, 0>(map, map, p, st);
+    case NSQ_TYPE_Q6_K:
+      if (layout == NSQ_Q6K_NODESTOR) return run_gemm_t<NSQ_TYPE_Q6_K, NSQ_Q6K_NODESTOR>(map, map, p, st);
+      return run_gemm_t<NSQ_TYPE_Q6_K, NSQ_Q6K_GGML>(map, map, p, st);
+    default: return NSQ_ERR_TYPE;
+  }
+}
+
+}  // namespace nsq

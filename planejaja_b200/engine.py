@@ -1,0 +1,160 @@
+"""Host-side mirror of the reference engine's matmul / dequant operators.
+
+`CudaEngine` keeps the shape of NodeStor's `VulkanEngine`
+(nodestor/crates/nodestor-vulkan/src/lib.rs:38-271) for the hot path:
+
+  upload(bytes)                 -> device buffer       (lib.rs:221-224)
+  download_f32(buf)             -> host f32 array      (lib.rs:236-239)
+  matmul(a, b, m, k, n)         -> C = A[m,k] . B[k,n] (lib.rs:117-122, dense f32)
+  matmul_quant(x, w, t, m, k, n)-> y = x . W^T over GGUF blocks (the quantized
+                                   branch of TensorOp::Matmul,
+                                   src/operator_registry.rs:43-49, 246-259)
+  dequant(w, t, n)              -> f32 / bf16 weights (DequantDispatcher::dequantize,
+                                   crates/nodestor-inference/src/dequant/mod.rs:142-191)
+
+Device memory, streams and the output buffers come from PyTorch; every
+computation is a call into libnsq.so.  Like the reference, calls are
+synchronous by default (the reference waits for queue idle after every
+dispatch, src/pipeline.rs:486-487); pass `sync=False` to stay asynchronous on
+the current CUDA stream.  Errors raise NsqError (the reference returns
+NodeStorError, crates/nodestor-core/src/error.rs:1-38).
+
+Kernel choice for matmul_quant: M <= 16 uses the decode GEMV (fp32
+activations and output); larger M uses the tcgen05 prefill GEMM (bf16
+operands, fp32 accumulate, bf16 output widened back to f32).  The
+environment variable NSQ_MATMUL_PATH=gemv|gemm forces one of them.
+"""
+from __future__ import annotations
+
+import os
+from typing import Optional
+
+import numpy as np
+import torch
+
+from . import _lib
+from .formats import FORMATS, Q6K_GGML, fmt
+from ._lib import NsqError, check
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+class CudaEngine:
+    """Engine facade over libnsq for one CUDA device."""
+
+    def __init__(self, device: int | str | torch.device = 0):
+        if not torch.cuda.is_available():
+            raise NsqError(_lib.ERR_DEVICE, "no CUDA device")
+        self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
+        self.lib = _lib.load()
+        self._ws: Optional[torch.Tensor] = None
+
+    # ---- buffers ---------------------------------------------------------
+    def upload(self, data) -> torch.Tensor:
+        """Copy host bytes (bytes / numpy array) to a new device uint8 buffer."""
+        arr = np.frombuffer(data, np.uint8) if isinstance(data, (bytes, bytearray, memoryview)) else \
+            np.ascontiguousarray(data).view(np.uint8).reshape(-1)
+        return torch.from_numpy(arr.copy()).to(self.device)
+
+    def upload_f32(self, data) -> torch.Tensor:
+        return torch.as_tensor(np.ascontiguousarray(data, np.float32)).to(self.device)
+
+    def download_f32(self, buf: torch.Tensor) -> np.ndarray:
+        return buf.detach().float().cpu().numpy()
+
+    def workspace(self, nbytes: int) -> torch.Tensor:
+        """Scratch for prepared activations; grown outside the hot calls."""
+        if self._ws is None or self._ws.numel() < nbytes:
+            self._ws = torch.empty(max(nbytes, 1 << 16), dtype=torch.uint8, device=self.device)
+        return self._ws
+
+    def _stream(self) -> int:
+        return _stream_handle(self.device)
+
+    def _sync(self, sync: bool):
+        if sync:
+            torch.cuda.synchronize(self.device)
+
+    # ---- operators ---------------------------------------------------------
+    def dequant(self, w: torch.Tensor, ggml_type: int, n_elems: int, out_dtype: str = "f32",
+                q6k_layout: int = Q6K_GGML, out: Optional[torch.Tensor] = None, sync: bool = True) -> torch.Tensor:
+        od = _lib.OUT_F32 if out_dtype == "f32" else _lib.OUT_BF16
+        if out is None:
+            out = torch.empty(n_elems, dtype=torch.float32 if od == _lib.OUT_F32 else torch.bfloat16,
+                              device=self.device)
+        check(self.lib.nsq_dequant(_ptr(w), ggml_type, q6k_layout, od, _ptr(out), n_elems, self._stream()),
+              "nsq_dequant")
+        self._sync(sync)
+        return out
+
+    def gemv(self, w: torch.Tensor, ggml_type: int, x: torch.Tensor, n: int, k: int,
+             q6k_layout: int = Q6K_GGML, y: Optional[torch.Tensor] = None, sync: bool = True) -> torch.Tensor:
+        m = x.numel() // k
+        if y is None:
+            y = torch.empty((m, n), dtype=torch.float32, device=self.device)
+        wsb = self.lib.nsq_gemv_workspace_size(m, k)
+        ws = self.workspace(wsb)
+        check(self.lib.nsq_gemv(_ptr(w), ggml_type, q6k_layout, _ptr(x), _ptr(y), m, n, k, _ptr(ws), ws.numel(),
+                                self._stream()), "nsq_gemv")
+        self._sync(sync)
+        return y
+
+    def prepare(self, x: torch.Tensor, k: int, ws: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Prepare activations once for several GEMVs (q|k|v, gate|up)."""
+        m = x.numel() // k
+        nbytes = self.lib.nsq_gemv_workspace_size(m, k)
+        if ws is None:
+            ws = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+        check(self.lib.nsq_prepare_activations(_ptr(x), m, k, _ptr(ws), ws.numel(), self._stream()),
+              "nsq_prepare_activations")
+        return ws
+
+    def gemv_prepared(self, w: torch.Tensor, ggml_type: int, ws: torch.Tensor, m: int, n: int, k: int,
+                      q6k_layout: int = Q6K_GGML, y: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if y is None:
+            y = torch.empty((m, n), dtype=torch.float32, device=self.device)
+        check(self.lib.nsq_gemv_prepared(_ptr(w), ggml_type, q6k_layout, _ptr(ws), _ptr(y), m, n, k,
+                                         self._stream()), "nsq_gemv_prepared")
+        return y
+
+    def gemm_bf16(self, w: torch.Tensor, ggml_type: int, x: torch.Tensor, n: int, k: int,
+                  q6k_layout: int = Q6K_GGML, y: Optional[torch.Tensor] = None, sync: bool = True) -> torch.Tensor:
+        if x.dtype != torch.bfloat16:
+            raise NsqError(_lib.ERR_TYPE, "gemm_bf16 expects bf16 activations")
+        m = x.numel() // k
+        if y is None:
+            y = torch.empty((m, n), dtype=torch.bfloat16, device=self.device)
+        check(self.lib.nsq_gemm_bf16(_ptr(w), ggml_type, q6k_layout, _ptr(x), _ptr(y), m, n, k, self._stream()),
+              "nsq_gemm_bf16")
+        self._sync(sync)
+        return y
+
+    def matmul(self, a: torch.Tensor, b: torch.Tensor, m: int, k: int, n: int, sync: bool = True) -> torch.Tensor:
+        """Dense f32 C[m, n] = A[m, k] . B[k, n] (the reference operator's layout)."""
+        c = torch.empty((m, n), dtype=torch.float32, device=self.device)
+        check(self.lib.nsq_matmul_f32(_ptr(a), _ptr(b), _ptr(c), m, k, n, self._stream()), "nsq_matmul_f32")
+        self._sync(sync)
+        return c
+
+    def matmul_quant(self, x: torch.Tensor, w: torch.Tensor, ggml_type: int, m: int, k: int, n: int,
+                     q6k_layout: int = Q6K_GGML, sync: bool = True) -> torch.Tensor:
+        """y[m, n] f32 = x[m, k] . W^T with W[n, k] in GGUF blocks of `ggml_type`."""
+        if ggml_type not in FORMATS:
+            raise NsqError(_lib.ERR_TYPE, f"matmul_quant: ggml type {ggml_type}")
+        if w.numel() < fmt(ggml_type).tensor_bytes(n, k):
+            raise NsqError(_lib.ERR_SHAPE, "matmul_quant: weight buffer smaller than N*row_bytes")
+        path = os.environ.get("NSQ_MATMUL_PATH", "")
+        if path == "gemv" or (path != "gemm" and m <= _lib.GEMV_MAX_M):
+            return self.gemv(w, ggml_type, x.reshape(m, k).float().contiguous(), n, k, q6k_layout, sync=sync)
+        xb = x.reshape(m, k).to(torch.bfloat16).contiguous()
+        return self.gemm_bf16(w, ggml_type, xb, n, k, q6k_layout, sync=sync).float()
+
+    def device_status(self, clear: bool = True) -> int:
+        """NSQ_ERR_TIMEOUT if a bounded device-side wait gave up, else 0."""
+        return self.lib.nsq_device_status(1 if clear else 0)

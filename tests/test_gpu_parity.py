@@ -1,0 +1,196 @@
+"""GPU parity tests: libnsq (through its C ABI) against the CPU oracle.
+
+Bars:
+  dequant  -- bit-exact f32 (and bf16 = round-to-nearest-even of the f32 value)
+  GEMV     -- max_i |y_i - r_i| / max(|r_i|, rms(r)) <= 1e-3   (r: oracle f32)
+  GEMM     -- the same metric <= 2e-2 (bf16 operands, fp32 accumulate)
+"""
+import numpy as np
+import pytest
+import torch
+
+from planejaja_b200 import quantize as Q
+from planejaja_b200 import _lib
+from planejaja_b200.formats import FORMATS, Q4_0, Q4_K, Q6_K, Q8_0, Q6K_GGML, Q6K_NODESTOR
+
+pytestmark = pytest.mark.gpu
+
+GEMV_TOL = 1e-3
+GEMM_TOL = 2e-2
+ALL = [(Q4_0, 0), (Q8_0, 0), (Q4_K, 0), (Q6_K, Q6K_GGML), (Q6_K, Q6K_NODESTOR)]
+IDS = ["Q4_0", "Q8_0", "Q4_K", "Q6_K", "Q6_K_nodestor"]
+
+
+@pytest.fixture(scope="module")
+def eng():
+    from planejaja_b200.engine import CudaEngine
+    e = CudaEngine(0)
+    yield e
+    assert e.device_status() == 0
+
+
+def rel_err(y, r):
+    y = np.asarray(y, np.float64).reshape(-1)
+    r = np.asarray(r, np.float64).reshape(-1)
+    rms = np.sqrt(np.mean(r * r)) if r.size else 0.0
+    den = np.maximum(np.abs(r), max(rms, 1e-30))
+    return float(np.max(np.abs(y - r) / den)) if r.size else 0.0
+
+
+def bf16_round(a: np.ndarray) -> np.ndarray:
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(torch.bfloat16).float().numpy()
+
+
+# ---------------------------------------------------------------- dequant
+@pytest.mark.parametrize("tid,layout", ALL, ids=IDS)
+def test_dequant_bit_exact_random(eng, oracle, tid, layout):
+    raw = Q.synthetic_weights(96, 1024, tid, seed=11, q6k_layout=layout)
+    ref = oracle.dequant(raw, tid, layout)
+    w = eng.upload(raw)
+    out = eng.dequant(w, tid, ref.size, "f32", layout).cpu().numpy()
+    assert np.array_equal(out.view(np.uint32), ref.view(np.uint32))
+    outb = eng.dequant(w, tid, ref.size, "bf16", layout).float().cpu().numpy()
+    assert np.array_equal(outb.view(np.uint32), bf16_round(ref).view(np.uint32))
+
+
+@pytest.mark.parametrize("name,tid,layout", [("Q4_0", Q4_0, 0), ("Q8_0", Q8_0, 0), ("Q4_K", Q4_K, 0),
+                                             ("Q6_K", Q6_K, 0), ("Q6_K_NODESTOR", Q6_K, 1)])
+def test_dequant_golden_and_fuzz(eng, golden, name, tid, layout):
+    raw, ref = golden[f"{name}_raw"], golden[f"{name}_f32"]
+    out = eng.dequant(eng.upload(raw), tid, ref.size, "f32", layout).cpu().numpy()
+    assert np.array_equal(out.view(np.uint32), ref.view(np.uint32))
+
+
+def test_dequant_reference_known_answers(eng, golden):
+    out = eng.dequant(eng.upload(golden["kat_q4k_uniform_raw"]), Q4_K, 256).cpu().numpy()
+    assert np.all(out[:128] == 28.0)
+    out = eng.dequant(eng.upload(golden["kat_q8_raw"]), Q8_0, 96).cpu().numpy().reshape(3, 32)
+    assert np.all(out[0] == 0) and np.all(out[1] == 5.0) and out[2, 0] == -1.0
+
+
+def test_dequant_subnormal_scale_follows_rust_conversion(eng, oracle):
+    blk = np.zeros(34, np.uint8)
+    blk[0:2] = np.array([0x0200], np.uint16).view(np.uint8)  # d = 2^-15 (subnormal fp16)
+    blk[2:] = np.arange(32, dtype=np.int8).view(np.uint8)
+    out = eng.dequant(eng.upload(blk), Q8_0, 32).cpu().numpy()
+    assert np.array_equal(out, oracle.dequant(blk, Q8_0, 0, fp16_mode=0))
+    assert out[1] == 2.0 ** -15
+
+
+def test_dequant_empty(eng):
+    w = eng.upload(np.zeros(144, np.uint8))
+    out = torch.empty(0, device=eng.device)
+    eng.dequant(w, Q4_K, 0, out=out)
+
+
+# ---------------------------------------------------------------- GEMV
+@pytest.mark.parametrize("tid,layout", ALL, ids=IDS)
+@pytest.mark.parametrize("m", [1, 2, 3, 4, 5, 8, 16])
+def test_gemv_parity(eng, oracle, tid, layout, m):
+    n, k = 300, 2048
+    w = Q.synthetic_weights(n, k, tid, seed=100 + tid, q6k_layout=layout)
+    x = Q.synthetic_activations(m, k, seed=200 + m)
+    ref = oracle.quant_matmul(w, tid, x, n, k, layout, threads=8)
+    y = eng.gemv(eng.upload(w), tid, torch.from_numpy(x).to(eng.device), n, k, layout).cpu().numpy()
+    assert rel_err(y, ref) <= GEMV_TOL
+
+
+@pytest.mark.parametrize("tid,layout", ALL, ids=IDS)
+@pytest.mark.parametrize("n,k", [(1, 256), (7, 512), (129, 768), (1000, 256), (64, 14336), (33, 28672)])
+def test_gemv_shapes(eng, oracle, tid, layout, n, k):
+    w = Q.synthetic_weights(n, k, tid, seed=7, q6k_layout=layout)
+    x = Q.synthetic_activations(1, k, seed=8)
+    ref = oracle.quant_matmul(w, tid, x, n, k, layout, threads=8)
+    y = eng.gemv(eng.upload(w), tid, torch.from_numpy(x).to(eng.device), n, k, layout).cpu().numpy()
+    assert rel_err(y, ref) <= GEMV_TOL
+
+
+def test_gemv_micro_config(eng, oracle):
+    """Micro-model Q8_0 matvec W[1536 x 512], x[1 x 512] (seeded N(0,0.02) / N(0,1))."""
+    n, k = 1536, 512
+    w = Q.synthetic_weights(n, k, Q8_0, seed=1000)
+    x = Q.synthetic_activations(1, k, seed=2000)
+    ref = oracle.quant_matmul(w, Q8_0, x, n, k)
+    y = eng.matmul_quant(torch.from_numpy(x).to(eng.device), eng.upload(w), Q8_0, 1, k, n).cpu().numpy()
+    assert rel_err(y, ref) <= GEMV_TOL
+
+
+def test_gemv_prepared_shares_activations(eng, oracle):
+    k = 1024
+    x = Q.synthetic_activations(2, k, seed=9)
+    xd = torch.from_numpy(x).to(eng.device)
+    ws = eng.prepare(xd, k)
+    for tid, n in [(Q4_K, 256), (Q6_K, 96), (Q8_0, 40)]:
+        w = Q.synthetic_weights(n, k, tid, seed=n)
+        y = eng.gemv_prepared(eng.upload(w), tid, ws, 2, n, k)
+        torch.cuda.synchronize()
+        assert rel_err(y.cpu().numpy(), oracle.quant_matmul(w, tid, x, n, k)) <= GEMV_TOL
+
+
+def test_gemv_zero_and_constant_activations(eng, oracle):
+    n, k = 64, 512
+    w = Q.synthetic_weights(n, k, Q4_K, seed=3)
+    wd = eng.upload(w)
+    y = eng.gemv(wd, Q4_K, torch.zeros(1, k, device=eng.device), n, k).cpu().numpy()
+    assert np.all(y == 0)
+    x = np.full((1, k), 0.5, np.float32)
+    y = eng.gemv(wd, Q4_K, torch.from_numpy(x).to(eng.device), n, k).cpu().numpy()
+    assert rel_err(y, oracle.quant_matmul(w, Q4_K, x, n, k)) <= GEMV_TOL
+
+
+def test_gemv_offset_weight_pointer(eng, oracle):
+    """A weight tensor at a 16-byte offset inside a larger buffer (GGUF data section)."""
+    n, k = 50, 512
+    w = Q.synthetic_weights(n, k, Q6_K, seed=4)
+    buf = eng.upload(np.concatenate([np.zeros(48, np.uint8), w, np.zeros(5, np.uint8)]))
+    x = Q.synthetic_activations(1, k, seed=5)
+    y = eng.gemv(buf[48:48 + w.size], Q6_K, torch.from_numpy(x).to(eng.device), n, k).cpu().numpy()
+    assert rel_err(y, oracle.quant_matmul(w, Q6_K, x, n, k)) <= GEMV_TOL
+
+
+def test_gemv_errors_on_gpu(eng):
+    w = eng.upload(np.zeros(144 * 4, np.uint8))
+    x = torch.zeros(1, 256, device=eng.device)
+    with pytest.raises(_lib.NsqError) as e:
+        eng.gemv(w[1:], Q4_K, x, 2, 256)
+    assert e.value.status == _lib.ERR_ALIGN
+    with pytest.raises(_lib.NsqError) as e:
+        eng.gemv(w, 3, x, 2, 256)
+    assert e.value.status == _lib.ERR_TYPE
+
+
+# ---------------------------------------------------------------- GEMM
+@pytest.mark.parametrize("tid,layout", ALL, ids=IDS)
+@pytest.mark.parametrize("m,n,k", [(128, 256, 512), (17, 200, 1024), (129, 130, 256), (300, 384, 2048)])
+def test_gemm_parity(eng, oracle, tid, layout, m, n, k):
+    w = Q.synthetic_weights(n, k, tid, seed=300 + n, q6k_layout=layout)
+    x = bf16_round(Q.synthetic_activations(m, k, seed=400 + m))
+    ref = oracle.quant_matmul(w, tid, x, n, k, layout, threads=8)
+    xd = torch.from_numpy(x).to(eng.device).to(torch.bfloat16)
+    y = eng.gemm_bf16(eng.upload(w), tid, xd, n, k, layout).float().cpu().numpy()
+    assert rel_err(y, ref) <= GEMM_TOL
+
+
+def test_gemm_matches_dequant_plus_torch(eng):
+    """bf16 GEMM equals (dequant -> bf16) @ x in fp32 closely (same bf16 operands)."""
+    n, k, m = 512, 4096, 256
+    w = Q.synthetic_weights(n, k, Q4_K, seed=21)
+    wd = eng.upload(w)
+    x = torch.randn(m, k, device=eng.device).to(torch.bfloat16)
+    wb = eng.dequant(wd, Q4_K, n * k, "bf16").reshape(n, k)
+    ref = (x.float() @ wb.float().T)
+    y = eng.gemm_bf16(wd, Q4_K, x, n, k).float()
+    assert rel_err(y.cpu().numpy(), ref.cpu().numpy()) <= 1e-2
+
+
+# ---------------------------------------------------------------- dense f32 matmul
+def test_matmul_f32(eng, oracle):
+    rng = np.random.default_rng(0)
+    m, k, n = 33, 70, 45
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b = rng.standard_normal((k, n)).astype(np.float32)
+    c = eng.matmul(torch.from_numpy(a).to(eng.device), torch.from_numpy(b).to(eng.device), m, k, n)
+    assert rel_err(c.cpu().numpy(), oracle.matmul_f32(a, b, m, k, n)) <= 1e-5
+    c = eng.matmul(torch.tensor([[1., 2.], [3., 4.]], device=eng.device),
+                   torch.tensor([[5., 6.], [7., 8.]], device=eng.device), 2, 2, 2)
+    assert c.cpu().tolist() == [[19.0, 22.0], [43.0, 50.0]]
