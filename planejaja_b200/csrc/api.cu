@@ -125,11 +125,11 @@ int nsq_dequant(const void* w, int ggml_type, int q6k_layout, int out_dtype, voi
   int rc = check_weights(w, ggml_type, q6k_layout, qk ? qk : 1);
   if (rc) return rc;
   if (n_elems < 0 || n_elems % qk) return NSQ_ERR_SHAPE;
+  if (n_elems == 0) return NSQ_OK;
   if (!out) return NSQ_ERR_NULL;
   if (reinterpret_cast<uintptr_t>(out) & (out_dtype == NSQ_OUT_F32 ? 3 : 1)) return NSQ_ERR_ALIGN;
   DevInfo di;
   if ((rc = check_device(di))) return rc;
-  if (n_elems == 0) return NSQ_OK;
   cudaError_t e = launch_dequant(static_cast<const uint8_t*>(w), ggml_type, q6k_layout, out_dtype, out, n_elems,
                                  static_cast<cudaStream_t>(stream), di.num_sms);
   return e == cudaSuccess ? NSQ_OK : NSQ_ERR_CUDA;
