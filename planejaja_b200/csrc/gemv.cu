@@ -21,6 +21,8 @@
 // against the reference's f32 composition (crates/nodestor-vulkan/src/
 // pipeline.rs:1256-1268 over the dequant of q4_k.rs / q8_0.rs / the
 // dequant_q4 / dequant_q6k shaders).
+#include <stdlib.h>
+
 #include "nsq_common.cuh"
 
 namespace nsq {
@@ -32,6 +34,10 @@ __global__ void __launch_bounds__(256) prepare_x_kernel(const float* __restrict_
   const int lane = threadIdx.x & 31;
   const int64_t warp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  // launched with programmatic stream serialization: x may come from the
+  // previous kernel and the workspace may still be read by it
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   for (int64_t gi = warp; gi < n_groups_total; gi += nwarps) {
     const int64_t m = gi / groups_per_row, g = gi % groups_per_row;
     const float v = x[(m * groups_per_row + g) * 32 + lane];
@@ -277,141 +283,157 @@ __device__ __forceinline__ void issue_stage(const GemvParams& p, uint8_t* slot, 
   if (bytes) bulk_g2s(slot, p.w + a16, bytes, bar);
 }
 
+constexpr int kConsumerWarps = 8;
+constexpr int kGemvThreads = 32 * (1 + kConsumerWarps);
+
 template <int TYPE, int LAYOUT, int M, bool XREG, int UMAX>
-__global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvParams p) {
   using UT = Unit<TYPE, LAYOUT>;
   constexpr int NG = UT::NG;
   constexpr int BB = Fmt<TYPE>::BB;
   extern __shared__ __align__(128) uint8_t smem[];
+  const int red_stride = (p.RT * M + 3) & ~3;
   uint8_t* stages = smem;
   float* red = reinterpret_cast<float*>(smem + (size_t)p.stage_bytes * p.nstages);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(red + ((p.RT * M + 1) & ~1));
-  __shared__ int64_t s_bad;
+  uint64_t* full = reinterpret_cast<uint64_t*>(red + (size_t)red_stride * p.nstages);
+  uint64_t* empty = full + p.nstages;
 
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t row_begin = p.N * blockIdx.x / gridDim.x;
   const int64_t row_end = p.N * (blockIdx.x + 1) / gridDim.x;
   const int nst = (int)((row_end - row_begin + p.RT - 1) / p.RT);
 
-  for (int i = tid; i < p.RT * M; i += blockDim.x) red[i] = 0.f;
+  for (int i = tid; i < red_stride * p.nstages; i += blockDim.x) red[i] = 0.f;
   if (tid == 0) {
-    s_bad = 0;
-    for (int s = 0; s < p.nstages; ++s) mbar_init(&bars[s], 1);
+    for (int s = 0; s < p.nstages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
     fence_mbar_init();
   }
   __syncthreads();
-  if (tid == 0) {
-    for (int t = 0; t < nst && t < p.nstages; ++t) {
-      const int64_t ra = row_begin + (int64_t)t * p.RT;
-      const int64_t rb = min(row_end, ra + p.RT);
-      issue_stage(p, stages + (size_t)t * p.stage_bytes, &bars[t], ra, rb);
-    }
-  }
 
-  // fixed unit ownership
-  const bool active = tid < p.P * p.G;
-  const int prow = tid / p.G;  // row offset inside a stage
-  const int gsub = tid % p.G;
-
-  XRegs xr[XREG ? UMAX * NG : 1];
-  if constexpr (XREG) {
-#pragma unroll
-    for (int i = 0; i < UMAX; ++i) {
-      const int64_t u = gsub + (int64_t)i * p.G;
-      if (active && i < p.UPT && u < p.U) {
-#pragma unroll
-        for (int gi = 0; gi < NG; ++gi) load_xgroup(p.xg + UT::group(u, gi), xr[i * NG + gi]);
+  if (warp == 0) {
+    // ---------------- producer: refills the ring and writes finished rows
+    int issued = 0;
+    if (lane == 0) {
+      for (; issued < nst && issued < p.nstages; ++issued) {
+        const int64_t ra = row_begin + (int64_t)issued * p.RT;
+        issue_stage(p, stages + (size_t)issued * p.stage_bytes, &full[issued], ra, min(row_end, ra + p.RT));
       }
     }
-  }
-  const bool warp_rows = (p.G % 32) == 0;
-
-  int issued = nst < p.nstages ? nst : p.nstages;
-  for (int t = 0; t < nst; ++t) {
-    const int slot = t % p.nstages;
-    const uint32_t parity = (uint32_t)((t / p.nstages) & 1);
-    const bool ok = mbar_wait_bounded(&bars[slot], parity);
-    if (__syncthreads_or(!ok)) {
-      if (tid == 0) s_bad = 1;
-      break;
+    issued = __shfl_sync(0xffffffffu, issued, 0);
+    bool ok = true;
+    for (int t = 0; t < nst; ++t) {
+      const int s = t % p.nstages;
+      if (!mbar_wait_bounded(&empty[s], (uint32_t)((t / p.nstages) & 1))) {
+        ok = false;
+        break;
+      }
+      const int64_t ra = row_begin + (int64_t)t * p.RT;
+      const int rows = (int)min((int64_t)p.RT, row_end - ra);
+      float* rs = red + (size_t)s * red_stride;
+      for (int i = lane; i < rows * M; i += 32) {
+        const int r = i / M, m = i - r * M;
+        p.y[(int64_t)m * p.N + ra + r] = rs[i];
+        rs[i] = 0.f;
+      }
+      __syncwarp();
+      if (lane == 0 && issued < nst) {
+        fence_proxy_async_smem();
+        const int64_t na = row_begin + (int64_t)issued * p.RT;
+        issue_stage(p, stages + (size_t)s * p.stage_bytes, &full[s], na, min(row_end, na + p.RT));
+      }
+      if (issued < nst) ++issued;
     }
-    const int64_t ra = row_begin + (int64_t)t * p.RT;
-    const int rows = (int)min((int64_t)p.RT, row_end - ra);
-    const uint8_t* sbase = stages + (size_t)slot * p.stage_bytes;
-    const int64_t a16 = (ra * p.RB) & ~int64_t(15);
+    if (!ok && lane == 0) {
+      // wind down: wait (bounded) for the copies still in flight
+      for (int t = issued - min(issued, p.nstages); t < issued; ++t)
+        (void)mbar_wait_bounded(&full[t % p.nstages], (uint32_t)((t / p.nstages) & 1));
+    }
+  } else {
+    // ---------------- consumers: fixed K units per thread
+    const int ct = tid - 32;
+    const bool active = ct < p.P * p.G;
+    const int prow = ct / p.G;
+    const int gsub = ct % p.G;
+    const bool warp_rows = (p.G % 32) == 0;
 
-    if (active) {
-      for (int r = prow; r < rows; r += p.P) {
-        const uint8_t* rowp = sbase + ((ra + r) * p.RB - a16);
-        float acc[M];
+    XRegs xr[XREG ? UMAX * NG : 1];
+    if constexpr (XREG) {
 #pragma unroll
-        for (int m = 0; m < M; ++m) acc[m] = 0.f;
+      for (int i = 0; i < UMAX; ++i) {
+        const int64_t u = gsub + (int64_t)i * p.G;
+        if (active && i < p.UPT && u < p.U) {
 #pragma unroll
-        for (int i = 0; i < UMAX; ++i) {
-          const int64_t u = gsub + (int64_t)i * p.G;
-          if (i < p.UPT && u < p.U) {
-            const int64_t b = u / UT::UPB;
-            const int ub = (int)(u - b * UT::UPB);
-            DGroup dg[NG];
-            UT::decode(rowp + b * BB, ub, dg);
-            if constexpr (XREG) {
+          for (int gi = 0; gi < NG; ++gi) load_xgroup(p.xg + UT::group(u, gi), xr[i * NG + gi]);
+        }
+      }
+    }
+    for (int t = 0; t < nst; ++t) {
+      const int s = t % p.nstages;
+      if (!mbar_wait_bounded(&full[s], (uint32_t)((t / p.nstages) & 1))) break;
+      const int64_t ra = row_begin + (int64_t)t * p.RT;
+      const int rows = (int)min((int64_t)p.RT, row_end - ra);
+      const uint8_t* sbase = stages + (size_t)s * p.stage_bytes;
+      const int64_t a16 = (ra * p.RB) & ~int64_t(15);
+      float* rs = red + (size_t)s * red_stride;
+      if (active) {
+        for (int r = prow; r < rows; r += p.P) {
+          const uint8_t* rowp = sbase + ((ra + r) * p.RB - a16);
+          float acc[M];
 #pragma unroll
-              for (int gi = 0; gi < NG; ++gi)
-                acc[0] += group_dot<UT::SIGNED, UT::OFF>(dg[gi], xr[i * NG + gi]);
-            } else {
+          for (int m = 0; m < M; ++m) acc[m] = 0.f;
 #pragma unroll
-              for (int gi = 0; gi < NG; ++gi) {
-                const int64_t gx = UT::group(u, gi);
+          for (int i = 0; i < UMAX; ++i) {
+            const int64_t u = gsub + (int64_t)i * p.G;
+            if (i < p.UPT && u < p.U) {
+              const int64_t b = u / UT::UPB;
+              const int ub = (int)(u - b * UT::UPB);
+              DGroup dg[NG];
+              UT::decode(rowp + b * BB, ub, dg);
+              if constexpr (XREG) {
 #pragma unroll
-                for (int m = 0; m < M; ++m) {
-                  XRegs x1;
-                  load_xgroup(p.xg + m * p.GX + gx, x1);
-                  acc[m] += group_dot<UT::SIGNED, UT::OFF>(dg[gi], x1);
+                for (int gi = 0; gi < NG; ++gi)
+                  acc[0] += group_dot<UT::SIGNED, UT::OFF>(dg[gi], xr[i * NG + gi]);
+              } else {
+#pragma unroll
+                for (int gi = 0; gi < NG; ++gi) {
+                  const int64_t gx = UT::group(u, gi);
+#pragma unroll
+                  for (int m = 0; m < M; ++m) {
+                    XRegs x1;
+                    load_xgroup(p.xg + m * p.GX + gx, x1);
+                    acc[m] += group_dot<UT::SIGNED, UT::OFF>(dg[gi], x1);
+                  }
                 }
               }
             }
           }
-        }
-        if (warp_rows) {
+          if (warp_rows) {
 #pragma unroll
-          for (int m = 0; m < M; ++m) {
-            float v = acc[m];
+            for (int m = 0; m < M; ++m) {
+              float v = acc[m];
 #pragma unroll
-            for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            acc[m] = v;
+              for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+              acc[m] = v;
+            }
+            if (lane == 0) {
+#pragma unroll
+              for (int m = 0; m < M; ++m) atomicAdd(&rs[r * M + m], acc[m]);
+            }
+          } else {
+#pragma unroll
+            for (int m = 0; m < M; ++m) atomicAdd(&rs[r * M + m], acc[m]);
           }
-          if ((tid & 31) == 0) {
-#pragma unroll
-            for (int m = 0; m < M; ++m) atomicAdd(&red[r * M + m], acc[m]);
-          }
-        } else {
-#pragma unroll
-          for (int m = 0; m < M; ++m) atomicAdd(&red[r * M + m], acc[m]);
         }
       }
-    }
-    __syncthreads();
-    if (tid == 0 && issued < nst) {
-      // slot `slot` is free: every thread passed the barrier above
-      fence_proxy_async_smem();
-      const int64_t na = row_begin + (int64_t)issued * p.RT;
-      const int64_t nb = min(row_end, na + p.RT);
-      issue_stage(p, stages + (size_t)slot * p.stage_bytes, &bars[slot], na, nb);
-      ++issued;
-    }
-    for (int i = tid; i < rows * M; i += blockDim.x) {
-      const int r = i / M, m = i - r * M;
-      p.y[(int64_t)m * p.N + ra + r] = red[i];
-      red[i] = 0.f;
+      __threadfence_block();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
     }
   }
-  // Abort path: drain the copies still in flight (bounded) before exiting.
   __syncthreads();
-  if (tid == 0 && s_bad == 1) {
-    for (int t = issued - min(issued, p.nstages); t < issued; ++t) {
-      (void)mbar_wait_bounded(&bars[t % p.nstages], (uint32_t)((t / p.nstages) & 1));
-    }
-  }
 }
 
 // ---------------------------------------------------------------------------
@@ -438,13 +460,17 @@ static cudaError_t launch_gemv_inst(const GemvParams& p, int blocks, size_t smem
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) configured[dev] = smem;
   }
-  kern<<<blocks, 256, smem, st>>>(p);
+  kern<<<blocks, kGemvThreads, smem, st>>>(p);
   return cudaGetLastError();
 }
 
 template <int TYPE, int LAYOUT, int M>
 static cudaError_t dispatch_x(const GemvParams& p, int blocks, size_t smem, cudaStream_t st) {
-  if (M == 1 && p.UPT <= 2) return launch_gemv_inst<TYPE, LAYOUT, M, true, 2>(p, blocks, smem, st);
+  // UMAX (units per thread) is a template constant so that only the
+  // activation registers a launch needs are allocated.
+  constexpr bool XR = (M == 1);
+  if (p.UPT == 1) return launch_gemv_inst<TYPE, LAYOUT, M, XR, 1>(p, blocks, smem, st);
+  if (p.UPT == 2) return launch_gemv_inst<TYPE, LAYOUT, M, XR, 2>(p, blocks, smem, st);
   return launch_gemv_inst<TYPE, LAYOUT, M, false, 4>(p, blocks, smem, st);
 }
 
@@ -462,7 +488,7 @@ static cudaError_t dispatch_m(const GemvParams& p, int M, int blocks, size_t sme
 // Host-side constants of the launch
 constexpr int kThreads = 256;
 constexpr int kStageTarget = 24 * 1024;
-constexpr int kSmemBudget = 100 * 1024;
+constexpr int kSmemBudget = 104 * 1024;
 
 template <int TYPE>
 static bool plan(int64_t N, int64_t K, int num_sms, GemvParams& p, int& blocks, size_t& smem, int M) {
@@ -481,7 +507,7 @@ static bool plan(int64_t N, int64_t K, int num_sms, GemvParams& p, int& blocks, 
   if (RT > P) RT -= RT % P;
   const int stage_bytes = (int)(((int64_t)RT * RB + 32 + 127) & ~int64_t(127));
   int nstages = kSmemBudget / stage_bytes;
-  if (nstages > 4) nstages = 4;
+  if (nstages > 6) nstages = 6;
   if (nstages < 2) nstages = 2;
   if ((size_t)stage_bytes * nstages > 200 * 1024) return false;
   int64_t nblk = (N + RT - 1) / RT;
@@ -491,7 +517,7 @@ static bool plan(int64_t N, int64_t K, int num_sms, GemvParams& p, int& blocks, 
   p.U = U; p.UPT = UPT; p.G = G; p.P = P; p.RT = RT;
   p.stage_bytes = stage_bytes; p.nstages = nstages; p.GX = K / 32;
   blocks = (int)nblk;
-  smem = (size_t)stage_bytes * nstages + (size_t)(((RT * M + 1) & ~1) * 4) + 8 * nstages + 16;
+  smem = (size_t)stage_bytes * nstages + (size_t)((RT * M + 3) & ~3) * 4 * nstages + 16 * nstages + 16;
   return true;
 }
 
@@ -514,8 +540,20 @@ static int run_gemv_t(const uint8_t* w, const XGroup* xg, float* y, int64_t M, i
   return NSQ_OK;
 }
 
+int run_gemv_rows(const uint8_t* w, int type, int layout, const XGroup* xg, float* y, int64_t M, int64_t N,
+                  int64_t K, cudaStream_t st, int num_sms);
+
 int run_gemv(const uint8_t* w, int type, int layout, const XGroup* xg, float* y, int64_t M, int64_t N, int64_t K,
              cudaStream_t st, int num_sms) {
+  // one lane per row (gemv_rows.cu) where the shape allows it, else the
+  // general kernel below
+  // NSQ_GEMV_GENERAL=1 forces the general kernel (used by the parity tests
+  // to cover both kernels on the same shapes)
+  const char* force = getenv("NSQ_GEMV_GENERAL");
+  if (!(force && force[0] == '1')) {
+    const int rc = run_gemv_rows(w, type, layout, xg, y, M, N, K, st, num_sms);
+    if (rc != -1) return rc;
+  }
   switch (type) {
     case NSQ_TYPE_Q4_0: return run_gemv_t<NSQ_TYPE_Q4_0, 0>(w, xg, y, M, N, K, st, num_sms);
     case NSQ_TYPE_Q8_0: return run_gemv_t<NSQ_TYPE_Q8_0, 0>(w, xg, y, M, N, K, st, num_sms);
@@ -534,8 +572,16 @@ cudaError_t launch_prepare_x(const float* x, XGroup* xg, int64_t M, int64_t K, c
   const int64_t cap = (int64_t)num_sms * 8;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
-  prepare_x_kernel<<<(unsigned)blocks, 256, 0, st>>>(x, xg, total, K / 32);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)blocks);
+  cfg.blockDim = dim3(256);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, prepare_x_kernel, x, xg, total, K / 32);
 }
 
 }  // namespace nsq

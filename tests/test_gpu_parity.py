@@ -84,9 +84,19 @@ def test_dequant_empty(eng):
 
 
 # ---------------------------------------------------------------- GEMV
+@pytest.fixture(params=["rows", "general"])
+def gemv_kernel(request, monkeypatch):
+    """Runs a test with the one-lane-per-row kernel and with the general kernel."""
+    if request.param == "general":
+        monkeypatch.setenv("NSQ_GEMV_GENERAL", "1")
+    else:
+        monkeypatch.delenv("NSQ_GEMV_GENERAL", raising=False)
+    return request.param
+
+
 @pytest.mark.parametrize("tid,layout", ALL, ids=IDS)
 @pytest.mark.parametrize("m", [1, 2, 3, 4, 5, 8, 16])
-def test_gemv_parity(eng, oracle, tid, layout, m):
+def test_gemv_parity(eng, oracle, gemv_kernel, tid, layout, m):
     n, k = 300, 2048
     w = Q.synthetic_weights(n, k, tid, seed=100 + tid, q6k_layout=layout)
     x = Q.synthetic_activations(m, k, seed=200 + m)
@@ -96,13 +106,24 @@ def test_gemv_parity(eng, oracle, tid, layout, m):
 
 
 @pytest.mark.parametrize("tid,layout", ALL, ids=IDS)
-@pytest.mark.parametrize("n,k", [(1, 256), (7, 512), (129, 768), (1000, 256), (64, 14336), (33, 28672)])
-def test_gemv_shapes(eng, oracle, tid, layout, n, k):
+@pytest.mark.parametrize("n,k", [(1, 256), (7, 512), (129, 768), (1000, 256), (64, 14336), (33, 28672),
+                                 (4096, 4096), (300, 2304)])
+def test_gemv_shapes(eng, oracle, gemv_kernel, tid, layout, n, k):
     w = Q.synthetic_weights(n, k, tid, seed=7, q6k_layout=layout)
     x = Q.synthetic_activations(1, k, seed=8)
     ref = oracle.quant_matmul(w, tid, x, n, k, layout, threads=8)
     y = eng.gemv(eng.upload(w), tid, torch.from_numpy(x).to(eng.device), n, k, layout).cpu().numpy()
     assert rel_err(y, ref) <= GEMV_TOL
+
+
+@pytest.mark.parametrize("tid", [Q4_0, Q8_0])
+@pytest.mark.parametrize("n,k", [(5, 32), (40, 96), (130, 1120)])
+def test_gemv_small_blocks(eng, oracle, tid, n, k):
+    """K not a multiple of 256: only the general kernel covers it."""
+    w = Q.synthetic_weights(n, k, tid, seed=17)
+    x = Q.synthetic_activations(2, k, seed=18)
+    y = eng.gemv(eng.upload(w), tid, torch.from_numpy(x).to(eng.device), n, k).cpu().numpy()
+    assert rel_err(y, oracle.quant_matmul(w, tid, x, n, k)) <= GEMV_TOL
 
 
 def test_gemv_micro_config(eng, oracle):
