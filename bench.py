@@ -9,9 +9,9 @@ Weights are N(0, 0.02) quantized on the host by planejaja_b200.quantize (seed
 The 32 layers are distinct device copies (4.44 GB), so every step streams far
 more than the 126 MB L2 and consecutive steps never hit in L2.
 
-Per layer: prepare activations (attention input) -> q, k, v GEMVs; prepare ->
-o; prepare (FFN input) -> gate, up; prepare -> down: 4 + 7 = 11 kernels.  A
-step is captured once as a CUDA graph and replayed.
+Per layer, one fused GEMV launch per shared activation: q|k|v (attention
+input), o, gate|up (FFN input), down -- 4 kernels, activations quantized on
+chip.  A step is captured once as a CUDA graph and replayed.
 
 With --gpus N > 1 (torchrun, one process per GPU, NCCL): every projection is
 row-sharded across the ranks (each rank holds N_out / N rows of each matrix)
@@ -23,9 +23,10 @@ metric  : decode GEMV HBM GB/s = (weight bytes + fp32 activations + fp32
 e2e     : the same step through the C-ABI engine calls with host buffers:
           pinned-host -> device copy of every activation vector, the GEMVs,
           device -> pinned-host copy of every output, stream sync per step.
-roofline: dominant kernel = the M = 1 Q4_K GEMV, timed alone with CUDA events
-          on the gate projection [14336 x 4096] (33.03 MB) rotating over the
-          32 layer copies; bound = HBM, peak = MEASURED_PEAKS.json hbm_gbs.
+roofline: dominant kernel = the fused M = 1 Q4_K gate|up launch (FFN input
+          projection, 2 x [14336 x 4096], 66.06 MB), timed alone with CUDA
+          events rotating over the 32 layer copies; bound = HBM, peak =
+          MEASURED_PEAKS.json hbm_gbs.
 prefill : the tcgen05 GEMM on Q4_K [14336 x 4096] at M = 512 tokens, TFLOP/s.
 cpu_baseline: the CPU oracle (C restatement of the reference's dequant +
           cpu_matmul_f32 composition) on one layer, all host threads.
@@ -37,6 +38,7 @@ workload, a bounded sample per step.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -147,9 +149,10 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------------- CPU (oracle) legs
-def cpu_leg(layer, acts, rows_frac: float = 1.0, reps: int = 1, threads: int = 0):
+def cpu_leg(layer, acts, rows_frac: float = 1.0, reps: int = 1, threads: int = 0, min_seconds: float = 0.0):
     """Time the oracle's dequant + cpu_matmul_f32 composition over (a row
-    sample of) one layer; returns (GB/s, bytes, seconds, threads)."""
+    sample of) one layer, `reps` times or until `min_seconds` have passed;
+    returns (GB/s, bytes, seconds, threads)."""
     from oracle import oracle as O
     from planejaja_b200.formats import fmt
     O.build()
@@ -162,11 +165,13 @@ def cpu_leg(layer, acts, rows_frac: float = 1.0, reps: int = 1, threads: int = 0
     nbytes = sum(j[0].nbytes + j[4] * 4 + j[3] * 4 for j in jobs)
     O.quant_matmul(jobs[0][0][: fmt(12).row_bytes(HIDDEN)], 12, acts[0], 1, HIDDEN, threads=th)  # warm
     t0 = time.perf_counter()
-    for _ in range(reps):
+    done = 0
+    while done < reps or time.perf_counter() - t0 < min_seconds:
         for w, t, x, nr, k in jobs:
             O.quant_matmul(w, t, x, nr, k, threads=th)
+        done += 1
     dt = time.perf_counter() - t0
-    return nbytes * reps / dt / 1e9, nbytes * reps, dt, th
+    return nbytes * done / dt / 1e9, nbytes * done, dt, th
 
 
 def run_reference(args, rank, world):
@@ -204,6 +209,7 @@ def run_gpu(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
 
+    from planejaja_b200 import _lib
     from planejaja_b200.engine import CudaEngine
     from planejaja_b200.formats import fmt
 
@@ -227,11 +233,23 @@ def run_gpu(args, rank, world, local_rank):
     for li in range(L):
         layers.append({name: (rows, buf if li == 0 else buf.clone()) for name, (rows, buf) in shards.items()})
     acts = [torch.from_numpy(a).to(dev) for a in acts_h]
-    ws = [torch.empty(lib.nsq_gemv_workspace_size(1, k), dtype=torch.uint8, device=dev) for k in ACT_K]
     outs_local = [{name: torch.empty(rows, dtype=torch.float32, device=dev) for name, (rows, _) in layers[0].items()}
                   for _ in range(L)]
     outs_full = [{name: torch.empty(n, dtype=torch.float32, device=dev) for name, n, k, t in LAYER_SPEC}
                  for _ in range(L)] if world > 1 else outs_local
+    # one fused launch per shared activation: q|k|v, o, gate|up, down
+    GROUPS = [(0, ["q", "k", "v"]), (1, ["o"]), (2, ["gate", "up"]), (3, ["down"])]
+    TYPE_OF = {name: t for name, n, k, t in LAYER_SPEC}
+    seg_arrays = []
+    for li in range(L):
+        per = []
+        for a, names in GROUPS:
+            arr = (_lib.Segment * len(names))()
+            for i, nm in enumerate(names):
+                rows, w = layers[li][nm]
+                arr[i] = _lib.Segment(w.data_ptr(), TYPE_OF[nm], 0, rows, outs_local[li][nm].data_ptr())
+            per.append((a, names, arr))
+        seg_arrays.append(per)
     n_launch = 0
 
     def step():
@@ -239,21 +257,14 @@ def run_gpu(args, rank, world, local_rank):
         n_launch = 0
         st = torch.cuda.current_stream(dev).cuda_stream
         for li in range(L):
-            prepared = set()
-            for name, n, k, t in LAYER_SPEC:
-                a = ACT_OF[name]
-                if a not in prepared:
-                    rc = lib.nsq_prepare_activations(acts[a].data_ptr(), 1, k, ws[a].data_ptr(), ws[a].numel(), st)
-                    assert rc == 0, rc
-                    prepared.add(a)
-                    n_launch += 1
-                rows, w = layers[li][name]
-                y = outs_local[li][name]
-                rc = lib.nsq_gemv_prepared(w.data_ptr(), t, 0, ws[a].data_ptr(), y.data_ptr(), 1, rows, k, st)
+            for a, names, arr in seg_arrays[li]:
+                rc = lib.nsq_gemv_multi(ctypes.cast(arr, ctypes.c_void_p), len(names), acts[a].data_ptr(), 1,
+                                        ACT_K[a], None, 0, st)
                 assert rc == 0, rc
                 n_launch += 1
                 if world > 1:
-                    dist.all_gather_into_tensor(outs_full[li][name], y)
+                    for nm in names:
+                        dist.all_gather_into_tensor(outs_full[li][nm], outs_local[li][nm])
 
     # warm + capture (single GPU: the whole step as one CUDA graph)
     step()
@@ -358,24 +369,21 @@ def run_gpu(args, rank, world, local_rank):
     }
     clocks = clk.summary()
 
-    # ---- dominant kernel alone: Q4_K gate GEMV over the layer copies
+    # ---- dominant kernel alone: the fused Q4_K gate|up launch (FFN input
+    # projection, 2 x [14336 x 4096]) over the layer copies
     if not args.skip_roofline:
-        gname = "gate"
-        rows, _ = layers[0][gname]
-        gbytes = fmt(12).tensor_bytes(rows, HIDDEN) + HIDDEN * 4 + rows * 4
+        rows, _ = layers[0]["gate"]
+        gbytes = 2 * fmt(12).tensor_bytes(rows, HIDDEN) + HIDDEN * 4 + 2 * rows * 4
         st = torch.cuda.current_stream(dev).cuda_stream
-        lib.nsq_prepare_activations(acts[2].data_ptr(), 1, HIDDEN, ws[2].data_ptr(), ws[2].numel(), st)
+        gu = [seg_arrays[li][2][2] for li in range(L)]
         reps = max(4, 256 // L) * L
         for i in range(L):
-            lib.nsq_gemv_prepared(layers[i][gname][1].data_ptr(), 12, 0, ws[2].data_ptr(),
-                                  outs_local[i][gname].data_ptr(), 1, rows, HIDDEN, st)
+            lib.nsq_gemv_multi(ctypes.cast(gu[i], ctypes.c_void_p), 2, acts[2].data_ptr(), 1, HIDDEN, None, 0, st)
         torch.cuda.synchronize()
         k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         k0.record()
         for i in range(reps):
-            li = i % L
-            lib.nsq_gemv_prepared(layers[li][gname][1].data_ptr(), 12, 0, ws[2].data_ptr(),
-                                  outs_local[li][gname].data_ptr(), 1, rows, HIDDEN, st)
+            lib.nsq_gemv_multi(ctypes.cast(gu[i % L], ctypes.c_void_p), 2, acts[2].data_ptr(), 1, HIDDEN, None, 0, st)
         k1.record()
         torch.cuda.synchronize()
         kms = k0.elapsed_time(k1) / reps
@@ -383,8 +391,9 @@ def run_gpu(args, rank, world, local_rank):
         traffic = None
         tp = os.path.join(ROOT, "profiles", "traffic.json")
         if os.path.exists(tp):
-            traffic = json.load(open(tp)).get("gemv_q4k_m1_gate")
-        result["roofline"] = {"bound": "hbm", "kernel": "gemv_kernel<Q4_K,M=1> gate [14336x4096]",
+            traffic = json.load(open(tp)).get("gemv_fused_q4k_m1_gate_up")
+        result["roofline"] = {"bound": "hbm",
+                              "kernel": "gemv_fused_kernel<M=1,Q4_K> gate|up 2 x [14336x4096] (FFN input projection)",
                               "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                               "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind,
                               "frac_of_nominal_8tbs": round(achieved / NOMINAL_HBM_GBS, 4),
@@ -419,11 +428,12 @@ def run_gpu(args, rank, world, local_rank):
 
     # ---- CPU baseline: oracle on one layer, all host threads (rank 0, N = 1)
     if rank == 0 and world == 1 and not args.skip_cpu:
-        v, nb, dt, th = cpu_leg(layer, acts_h, rows_frac=args.cpu_frac, reps=args.cpu_reps)
+        v, nb, dt, th = cpu_leg(layer, acts_h, rows_frac=args.cpu_frac, reps=args.cpu_reps,
+                                min_seconds=args.cpu_seconds)
         result["cpu_baseline"] = {"value": round(v, 3), "unit": UNIT, "cores": th, "kind": "port",
                                   "sample": f"oracle dequant + cpu_matmul_f32 over {args.cpu_frac:.3f} of the rows "
-                                            f"of one layer's 7 matrices x{args.cpu_reps} ({nb / 1e6:.1f} MB, "
-                                            f"{dt:.1f} s)"}
+                                            f"of one layer's 7 matrices, repeated for >= {args.cpu_seconds:.0f} s "
+                                            f"({nb / 1e6:.1f} MB in {dt:.1f} s)"}
     if rank == 0:
         print(json.dumps(result), flush=True)
     graph = None
@@ -441,7 +451,8 @@ def main():
     ap.add_argument("--skip-roofline", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--cpu-frac", type=float, default=1.0)
-    ap.add_argument("--cpu-reps", type=int, default=3)
+    ap.add_argument("--cpu-reps", type=int, default=1)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-frac", type=float, default=0.25)
     args = ap.parse_args()
     if args.warmup < 3:

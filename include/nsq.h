@@ -105,10 +105,11 @@ int nsq_dequant(const void *w, int ggml_type, int q6k_layout, int out_dtype, voi
  * (crates/nodestor-vulkan/src/lib.rs:117-122) on quantized weights and the
  * TensorOp::Matmul{quantized} dispatch (src/operator_registry.rs:246-259).
  *
- * Activations are first split into per-32 scaled int16 limbs in `workspace`
- * (nsq_gemv_workspace_size bytes, 16-byte aligned); the GEMV itself
- * accumulates exact integer dot products per 32 weights and combines them
- * in fp32.
+ * Activations are split into per-32 scaled int16 limbs (on chip when x is
+ * 16-byte aligned, M <= 4 and M * K / 32 * 80 <= 40 KB, else in `workspace`,
+ * nsq_gemv_workspace_size bytes, 16-byte aligned, which may be NULL when
+ * not needed); the GEMV accumulates exact integer dot products per 16 or 32
+ * weights and combines them in fp32.
  */
 size_t nsq_gemv_workspace_size(int64_t M, int64_t K);
 int nsq_gemv(const void *w, int ggml_type, int q6k_layout, const float *x, float *y, int64_t M,
@@ -120,6 +121,31 @@ int nsq_prepare_activations(const float *x, int64_t M, int64_t K, void *workspac
                             size_t workspace_bytes, void *stream);
 int nsq_gemv_prepared(const void *w, int ggml_type, int q6k_layout, const void *workspace,
                       float *y, int64_t M, int64_t N, int64_t K, void *stream);
+
+/*
+ * Fused decode GEMV over several weight matrices that share one activation
+ * (the q|k|v or gate|up projections of a transformer layer): for every
+ * segment s, segs[s].y[M x N_s] = x[M x K] . W_s^T.  One launch streams all
+ * segments; formats may differ between segments.  Same accuracy contract as
+ * nsq_gemv.  `workspace` (nsq_gemv_workspace_size(M, K) bytes) is used only
+ * when M * K is too large for the activations to be prepared on chip; it
+ * may be NULL otherwise (the call then returns NSQ_ERR_WORKSPACE if it is
+ * needed).  Replaces the per-projection engine.matmul calls of
+ * Transformer::forward (crates/nodestor-vulkan/src/transformer.rs:241-315),
+ * each of which is a separate submit + queue wait (src/pipeline.rs:486-487).
+ */
+typedef struct nsq_segment {
+  const void *w;   /* GGUF blocks, N rows of K weights, 16-byte aligned */
+  int ggml_type;
+  int q6k_layout;
+  int64_t N;
+  float *y;        /* [M x N] f32 */
+} nsq_segment;
+
+#define NSQ_MAX_SEGMENTS 4
+
+int nsq_gemv_multi(const nsq_segment *segs, int nseg, const float *x, int64_t M, int64_t K,
+                   void *workspace, size_t workspace_bytes, void *stream);
 
 /*
  * Prefill GEMM on tcgen05 tensor cores: y[M x N] bf16 = x[M x K] bf16 . W^T,

@@ -41,9 +41,19 @@ SIGNATURES = [
     ("nsq_gemv", _int, [_vp, _int, _int, _vp, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),
     ("nsq_prepare_activations", _int, [_vp, _i64, _i64, _vp, _sz, _vp]),
     ("nsq_gemv_prepared", _int, [_vp, _int, _int, _vp, _vp, _i64, _i64, _i64, _vp]),
+    ("nsq_gemv_multi", _int, [ctypes.c_void_p, _int, _vp, _i64, _i64, _vp, _sz, _vp]),
     ("nsq_gemm_bf16", _int, [_vp, _int, _int, _vp, _vp, _i64, _i64, _i64, _vp]),
     ("nsq_matmul_f32", _int, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
 ]
+
+
+class Segment(ctypes.Structure):
+    """struct nsq_segment (include/nsq.h)."""
+    _fields_ = [("w", ctypes.c_void_p), ("ggml_type", ctypes.c_int), ("q6k_layout", ctypes.c_int),
+                ("N", ctypes.c_int64), ("y", ctypes.c_void_p)]
+
+
+MAX_SEGMENTS = 4
 
 
 class NsqError(RuntimeError):

@@ -16,6 +16,11 @@ cudaError_t launch_dequant(const uint8_t* w, int type, int layout, int out_dtype
 cudaError_t launch_prepare_x(const float* x, XGroup* xg, int64_t M, int64_t K, cudaStream_t st, int num_sms);
 int run_gemv(const uint8_t* w, int type, int layout, const XGroup* xg, float* y, int64_t M, int64_t N, int64_t K,
              cudaStream_t st, int num_sms);
+int run_gemv_fused(const nsq_segment* segs, int nseg, const float* x, const XGroup* xg, int64_t M, int64_t K,
+                   cudaStream_t st, int num_sms);
+bool fused_covers(const nsq_segment* segs, int nseg, int64_t K);
+bool fused_self_prepare_fits(int64_t M, int64_t K);
+bool gemv_force_general();
 int run_gemm_bf16(const uint8_t* w, int type, int layout, const void* x, void* y, int64_t M, int64_t N, int64_t K,
                   cudaStream_t st, int num_sms);
 cudaError_t launch_matmul_f32(const float* a, const float* b, float* c, int64_t M, int64_t K, int64_t N,
@@ -171,12 +176,57 @@ int nsq_gemv_prepared(const void* w, int ggml_type, int q6k_layout, const void* 
 
 int nsq_gemv(const void* w, int ggml_type, int q6k_layout, const float* x, float* y, int64_t M, int64_t N,
              int64_t K, void* workspace, size_t workspace_bytes, void* stream) {
-  int rc = check_weights(w, ggml_type, q6k_layout, K);
-  if (rc) return rc;
-  if (M < 1 || M > NSQ_GEMV_MAX_M || N < 1) return NSQ_ERR_SHAPE;
-  if (!y) return NSQ_ERR_NULL;
-  if ((rc = nsq_prepare_activations(x, M, K, workspace, workspace_bytes, stream))) return rc;
-  return nsq_gemv_prepared(w, ggml_type, q6k_layout, workspace, y, M, N, K, stream);
+  nsq_segment sg{w, ggml_type, q6k_layout, N, y};
+  return nsq_gemv_multi(&sg, 1, x, M, K, workspace, workspace_bytes, stream);
+}
+
+int nsq_gemv_multi(const nsq_segment* segs, int nseg, const float* x, int64_t M, int64_t K, void* workspace,
+                   size_t workspace_bytes, void* stream) {
+  if (!segs) return NSQ_ERR_NULL;
+  if (nseg < 1 || nseg > NSQ_MAX_SEGMENTS) return NSQ_ERR_SHAPE;
+  int rc;
+  for (int i = 0; i < nseg; ++i) {
+    if ((rc = check_weights(segs[i].w, segs[i].ggml_type, segs[i].q6k_layout, K))) return rc;
+    if (segs[i].N < 1) return NSQ_ERR_SHAPE;
+    if (!segs[i].y) return NSQ_ERR_NULL;
+    if (reinterpret_cast<uintptr_t>(segs[i].y) & 3) return NSQ_ERR_ALIGN;
+  }
+  if (M < 1 || M > NSQ_GEMV_MAX_M || K % 32) return NSQ_ERR_SHAPE;
+  if (!x) return NSQ_ERR_NULL;
+  if (reinterpret_cast<uintptr_t>(x) & 15) {
+    // the on-chip path reads x with 16-byte loads; 4-byte aligned inputs go
+    // through the workspace
+    if (reinterpret_cast<uintptr_t>(x) & 3) return NSQ_ERR_ALIGN;
+  }
+  const bool fused = !gemv_force_general() && fused_covers(segs, nseg, K);
+  const bool self = fused && fused_self_prepare_fits(M, K) && !(reinterpret_cast<uintptr_t>(x) & 15);
+  if (!self) {
+    if (!workspace) return NSQ_ERR_WORKSPACE;
+    if (reinterpret_cast<uintptr_t>(workspace) & 15) return NSQ_ERR_ALIGN;
+    if (workspace_bytes < nsq_gemv_workspace_size(M, K)) return NSQ_ERR_WORKSPACE;
+  }
+  DevInfo di;
+  if ((rc = check_device(di))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (self) {
+    rc = run_gemv_fused(segs, nseg, x, nullptr, M, K, st, di.num_sms);
+    if (rc != -1) return rc;
+    // not covered on chip after all: go through the workspace
+    if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 15) ||
+        workspace_bytes < nsq_gemv_workspace_size(M, K))
+      return NSQ_ERR_WORKSPACE;
+  }
+  if (launch_prepare_x(x, static_cast<XGroup*>(workspace), M, K, st, di.num_sms) != cudaSuccess) return NSQ_ERR_CUDA;
+  if (fused) {
+    rc = run_gemv_fused(segs, nseg, nullptr, static_cast<const XGroup*>(workspace), M, K, st, di.num_sms);
+    if (rc != -1) return rc;
+  }
+  for (int i = 0; i < nseg; ++i) {
+    rc = run_gemv(static_cast<const uint8_t*>(segs[i].w), segs[i].ggml_type, segs[i].q6k_layout,
+                  static_cast<const XGroup*>(workspace), segs[i].y, M, segs[i].N, K, st, di.num_sms);
+    if (rc) return rc;
+  }
+  return NSQ_OK;
 }
 
 int nsq_gemm_bf16(const void* w, int ggml_type, int q6k_layout, const void* x_bf16, void* y_bf16, int64_t M,

@@ -540,18 +540,23 @@ static int run_gemv_t(const uint8_t* w, const XGroup* xg, float* y, int64_t M, i
   return NSQ_OK;
 }
 
-int run_gemv_rows(const uint8_t* w, int type, int layout, const XGroup* xg, float* y, int64_t M, int64_t N,
-                  int64_t K, cudaStream_t st, int num_sms);
+int run_gemv_fused(const nsq_segment* segs, int nseg, const float* x, const XGroup* xg, int64_t M, int64_t K,
+                   cudaStream_t st, int num_sms);
 
+bool gemv_force_general() {
+  // NSQ_GEMV_GENERAL=1 forces the general kernel below (the parity tests use
+  // it to cover both kernels on the same shapes)
+  const char* force = getenv("NSQ_GEMV_GENERAL");
+  return force && force[0] == '1';
+}
+
+// GEMV on prepared activations: the fused kernel (gemv_rows.cu) in
+// workspace mode where the shape allows it, else the general kernel.
 int run_gemv(const uint8_t* w, int type, int layout, const XGroup* xg, float* y, int64_t M, int64_t N, int64_t K,
              cudaStream_t st, int num_sms) {
-  // one lane per row (gemv_rows.cu) where the shape allows it, else the
-  // general kernel below
-  // NSQ_GEMV_GENERAL=1 forces the general kernel (used by the parity tests
-  // to cover both kernels on the same shapes)
-  const char* force = getenv("NSQ_GEMV_GENERAL");
-  if (!(force && force[0] == '1')) {
-    const int rc = run_gemv_rows(w, type, layout, xg, y, M, N, K, st, num_sms);
+  if (!gemv_force_general()) {
+    nsq_segment sg{w, type, layout, N, y};
+    const int rc = run_gemv_fused(&sg, 1, nullptr, xg, M, K, st, num_sms);
     if (rc != -1) return rc;
   }
   switch (type) {

@@ -31,18 +31,6 @@ namespace nsq {
 constexpr int kRowsConsumers = 4;
 constexpr int kRowsThreads = 32 * (1 + kRowsConsumers);
 
-struct RowsParams {
-  const uint8_t* w;
-  const XGroup* xg;
-  float* y;
-  int64_t N, K, RB;
-  int R, KS, PPS;             // rows per CTA, lane groups per warp, pieces per chunk
-  int piece_bytes, chunk_bytes, pitch;
-  int nchunks, npieces;       // chunks per row, pieces per row (K / 256)
-  int xstride;                // bytes of one token's activation records in a stage
-  int stage_bytes, nstages;
-  int64_t GX;                 // activation groups per token (K / 32)
-};
 
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
@@ -269,23 +257,130 @@ struct Piece<NSQ_TYPE_Q8_0, LAYOUT, M> {
 };
 
 // ---------------------------------------------------------------------------
-template <int TYPE, int LAYOUT, int M>
-__global__ void __launch_bounds__(kRowsThreads) gemv_rows_kernel(const RowsParams p) {
+// ---------------------------------------------------------------------------
+// Fused kernel: several segments (weight matrices sharing the activation),
+// rows concatenated, walked by persistent CTAs in row blocks x K chunks.
+enum : int { kQ4K = 0, kQ6KG = 1, kQ6KN = 2, kQ40 = 3, kQ80 = 4 };
+
+struct FSeg {
+  const uint8_t* w;
+  float* y;
+  int64_t N, RB, row0;  // rows, row bytes, first row in the concatenated row space
+  int code, piece_bytes, chunk_bytes, pitch;
+};
+
+struct FusedParams {
+  FSeg seg[NSQ_MAX_SEGMENTS];
+  int nseg;
+  int64_t T;            // total rows
+  const float* x;       // activations (self-prepared mode)
+  const XGroup* xg;     // prepared activations (workspace mode)
+  int64_t K, GX;        // GX = K / 32
+  int R, KS, PPS, npieces, nchunks;
+  int xstride;          // bytes per token of per-stage activation records (workspace mode)
+  int stage_bytes, nstages, max_pitch;
+};
+
+// CODE >= 0: every segment has that format (one decoder compiled in);
+// CODE == kMixed: dispatch on the segment's format.
+constexpr int kMixed = -1;
+template <int M, int CODE>
+__device__ __forceinline__ void run_piece(int code, const uint8_t* pc, const uint8_t* xp, int xstride, float (&acc)[M]) {
+  if constexpr (CODE == kQ4K) { Piece<NSQ_TYPE_Q4_K, 0, M>::run(pc, xp, xstride, acc); return; }
+  if constexpr (CODE == kQ6KG) { Piece<NSQ_TYPE_Q6_K, NSQ_Q6K_GGML, M>::run(pc, xp, xstride, acc); return; }
+  if constexpr (CODE == kQ6KN) { Piece<NSQ_TYPE_Q6_K, NSQ_Q6K_NODESTOR, M>::run(pc, xp, xstride, acc); return; }
+  if constexpr (CODE == kQ40) { Piece<NSQ_TYPE_Q4_0, 0, M>::run(pc, xp, xstride, acc); return; }
+  if constexpr (CODE == kQ80) { Piece<NSQ_TYPE_Q8_0, 0, M>::run(pc, xp, xstride, acc); return; }
+  switch (code) {
+    case kQ4K: Piece<NSQ_TYPE_Q4_K, 0, M>::run(pc, xp, xstride, acc); break;
+    case kQ6KG: Piece<NSQ_TYPE_Q6_K, NSQ_Q6K_GGML, M>::run(pc, xp, xstride, acc); break;
+    case kQ6KN: Piece<NSQ_TYPE_Q6_K, NSQ_Q6K_NODESTOR, M>::run(pc, xp, xstride, acc); break;
+    case kQ40: Piece<NSQ_TYPE_Q4_0, 0, M>::run(pc, xp, xstride, acc); break;
+    default: Piece<NSQ_TYPE_Q8_0, 0, M>::run(pc, xp, xstride, acc); break;
+  }
+}
+
+// Quantize one group of 32 activations into an 80-byte record (same math as
+// prepare_x_kernel in gemv.cu, one thread per group).
+__device__ __forceinline__ void prepare_group(const float* __restrict__ xs, uint8_t* rec) {
+  float v[32];
+  const float4* q = reinterpret_cast<const float4*>(xs);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 f = __ldg(q + i);
+    v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+  }
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  const float inv = amax > 0.f ? 32767.0f / amax : 0.f;
+  uint32_t hw[8], lw[8];
+  int s0 = 0, s1 = 0;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    uint32_t h = 0, l = 0;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      int X = __float2int_rn(v[4 * w + b] * inv);
+      X = max(-32767, min(32767, X));
+      if (w < 4) s0 += X; else s1 += X;
+      h |= ((uint32_t)(X >> 8) & 0xFF) << (8 * b);
+      l |= ((uint32_t)X & 0xFF) << (8 * b);
+    }
+    hw[w] = h;
+    lw[w] = l;
+  }
+  uint4* o = reinterpret_cast<uint4*>(rec);
+  o[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+  o[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+  o[2] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+  o[3] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+  o[4] = make_uint4(__float_as_uint(amax / 32767.0f), (uint32_t)s0, (uint32_t)s1, 0u);
+}
+
+// Walk of one CTA's work: items (segment, row block, chunk) in order.
+struct ItemCursor {
+  int seg;
+  int64_t row0, rows;  // segment-local first row and row count of the block
+  int c;               // chunk
+  __device__ void first(const FusedParams& p, int64_t r_begin, int64_t r_end) {
+    seg = 0;
+    while (seg < p.nseg - 1 && r_begin >= p.seg[seg].row0 + p.seg[seg].N) ++seg;
+    row0 = r_begin - p.seg[seg].row0;
+    const int64_t seg_end = min(r_end, p.seg[seg].row0 + p.seg[seg].N) - p.seg[seg].row0;
+    rows = min((int64_t)p.R, seg_end - row0);
+    c = 0;
+  }
+  // advance; returns false when the CTA's rows are done
+  __device__ bool next(const FusedParams& p, int64_t r_end) {
+    if (++c < p.nchunks) return true;
+    c = 0;
+    row0 += rows;
+    const int64_t seg_end_g = min(r_end, p.seg[seg].row0 + p.seg[seg].N);
+    if (p.seg[seg].row0 + row0 >= seg_end_g) {
+      if (seg_end_g >= r_end || seg + 1 >= p.nseg) return false;
+      ++seg;
+      row0 = 0;
+    }
+    const int64_t seg_end = min(r_end, p.seg[seg].row0 + p.seg[seg].N) - p.seg[seg].row0;
+    rows = min((int64_t)p.R, seg_end - row0);
+    return rows > 0;
+  }
+};
+
+template <int M, bool XSELF, int CODE>
+__global__ void __launch_bounds__(kRowsThreads) gemv_fused_kernel(const __grid_constant__ FusedParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* stages = smem;
-  float* red = reinterpret_cast<float*>(smem + (size_t)p.stage_bytes * p.nstages);  // [2][4][32][M]
+  uint8_t* xsm = smem + (size_t)p.stage_bytes * p.nstages;  // self-prepared activations [M][GX] records
+  const size_t xsm_bytes = XSELF ? (size_t)M * p.GX * 80 : 0;
+  float* red = reinterpret_cast<float*>(xsm + xsm_bytes);  // [2][4][32][M]
   uint64_t* full = reinterpret_cast<uint64_t*>(red + 2 * kRowsConsumers * 32 * M);
   uint64_t* empty = full + p.nstages;
   __shared__ int s_fail;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  // persistent CTA: a contiguous, balanced range of rows, walked in row
-  // blocks of R rows x chunks of K; items (row block, chunk) stream through
-  // the stage ring without a break at row-block boundaries
-  const int64_t r_begin = p.N * blockIdx.x / gridDim.x, r_end = p.N * (blockIdx.x + 1) / gridDim.x;
-  const int nrb = (int)((r_end - r_begin + p.R - 1) / p.R);
-  const int nitems = nrb * p.nchunks;
-  const int ppc_bytes = p.PPS * p.piece_bytes;
+  const int64_t r_begin = p.T * blockIdx.x / gridDim.x, r_end = p.T * (blockIdx.x + 1) / gridDim.x;
 
   if (tid == 0) {
     s_fail = 0;
@@ -298,92 +393,113 @@ __global__ void __launch_bounds__(kRowsThreads) gemv_rows_kernel(const RowsParam
   __syncthreads();
 
   if (warp == 0) {
-    if (lane == 0) {
-      auto issue_w = [&](int t, int s) {
-        const int rb = t / p.nchunks, c = t - rb * p.nchunks;
-        const int64_t row0 = r_begin + (int64_t)rb * p.R;
-        const int rows = (int)min((int64_t)p.R, r_end - row0);
-        const int64_t off = (int64_t)c * ppc_bytes;
-        const int rbytes = (int)min((int64_t)ppc_bytes, p.RB - off);
-        const int ng = (int)(min((int64_t)p.PPS, (int64_t)p.npieces - (int64_t)c * p.PPS)) * 8;
+    if (lane == 0 && r_begin < r_end) {
+      auto issue = [&](const ItemCursor& it, int s, bool with_w, bool with_x) {
+        const FSeg& sg = p.seg[it.seg];
+        const int64_t off = (int64_t)it.c * sg.chunk_bytes;
+        const int rbytes = (int)min((int64_t)sg.chunk_bytes, sg.RB - off);
+        const int ng = (int)(min((int64_t)p.PPS, (int64_t)p.npieces - (int64_t)it.c * p.PPS)) * 8;
         uint8_t* slot = stages + (size_t)s * p.stage_bytes;
-        mbar_arrive_expect_tx(&full[s], (uint32_t)(rows * rbytes + M * ng * 80));
-        for (int r = 0; r < rows; ++r) bulk_g2s(slot + r * p.pitch, p.w + (row0 + r) * p.RB + off, rbytes, &full[s]);
-      };
-      auto issue_x = [&](int t, int s) {
-        const int rb = t / p.nchunks, c = t - rb * p.nchunks;
-        const int ng = (int)(min((int64_t)p.PPS, (int64_t)p.npieces - (int64_t)c * p.PPS)) * 8;
-        uint8_t* xs = stages + (size_t)s * p.stage_bytes + p.R * p.pitch;
-        for (int m = 0; m < M; ++m)
-          bulk_g2s(xs + m * p.xstride, p.xg + m * p.GX + (int64_t)c * p.PPS * 8, ng * 80, &full[s]);
+        if (with_w) {
+          mbar_arrive_expect_tx(&full[s], (uint32_t)(it.rows * rbytes + (XSELF ? 0 : M * ng * 80)));
+          for (int r = 0; r < (int)it.rows; ++r)
+            bulk_g2s(slot + r * sg.pitch, sg.w + (it.row0 + r) * sg.RB + off, rbytes, &full[s]);
+        }
+        if (!XSELF && with_x) {
+          uint8_t* xs = slot + p.R * p.max_pitch;
+          for (int m = 0; m < M; ++m)
+            bulk_g2s(xs + m * p.xstride, p.xg + m * p.GX + (int64_t)it.c * p.PPS * 8, ng * 80, &full[s]);
+        }
       };
       // weights of the first stages do not depend on the previous kernel
-      const int pre = min(nitems, p.nstages);
-      for (int t = 0; t < pre; ++t) issue_w(t, t);
+      ItemCursor it;
+      it.first(p, r_begin, r_end);
+      ItemCursor pre[8];
+      int npre = 0;
+      bool more = true;
+      while (more && npre < p.nstages) {
+        pre[npre] = it;
+        issue(it, npre, true, false);
+        ++npre;
+        more = it.next(p, r_end);
+      }
       grid_dep_wait();
       grid_dep_launch();
-      for (int t = 0; t < pre; ++t) issue_x(t, t);
-      for (int t = pre; t < nitems; ++t) {
+      for (int t = 0; t < npre; ++t) issue(pre[t], t, false, true);
+      for (int t = npre; more; ++t) {
         const int s = t % p.nstages;
         if (!mbar_wait_bounded(&empty[s], (uint32_t)(((t / p.nstages) - 1) & 1))) {
           s_fail = 1;
           break;
         }
         fence_proxy_async_smem();
-        issue_w(t, s);
-        issue_x(t, s);
+        issue(it, s, true, true);
+        more = it.next(p, r_end);
       }
+    } else if (lane == 0) {
+      grid_dep_wait();
+      grid_dep_launch();
     }
   } else {
-    const int cw = warp - 1;
+    const int cw = warp - 1, ct = tid - 32;
+    grid_dep_wait();
+    grid_dep_launch();
+    if constexpr (XSELF) {
+      for (int64_t gi = ct; gi < (int64_t)M * p.GX; gi += kRowsConsumers * 32) {
+        const int64_t m = gi / p.GX, g = gi - m * p.GX;
+        prepare_group(p.x + m * p.K + 32 * g, xsm + (m * p.GX + g) * 80);
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(kRowsConsumers * 32) : "memory");
+    }
     const int r = lane % p.R, ks = lane / p.R;
     const int lanes_per_piece = kRowsConsumers * p.KS;
+    const int xstride = XSELF ? (int)(p.GX * 80) : p.xstride;
     float acc[M];
 #pragma unroll
     for (int m = 0; m < M; ++m) acc[m] = 0.f;
     bool ok = true;
     int par = 0;
-    for (int t = 0; t < nitems; ++t) {
-      const int rb = t / p.nchunks, c = t - rb * p.nchunks;
-      const int64_t row0 = r_begin + (int64_t)rb * p.R;
-      const int rows = (int)min((int64_t)p.R, r_end - row0);
-      const int s = t % p.nstages;
-      // after a failed wait, skip the remaining waits but keep every barrier
-      if (ok) ok = mbar_wait_bounded(&full[s], (uint32_t)((t / p.nstages) & 1));
-      if (ok) {
-        const int np = (int)min((int64_t)p.PPS, (int64_t)p.npieces - (int64_t)c * p.PPS);
-        const uint8_t* slot = stages + (size_t)s * p.stage_bytes;
-        if (r < rows) {
-          for (int j = cw * p.KS + ks; j < np; j += lanes_per_piece) {
-            Piece<TYPE, LAYOUT, M>::run(slot + r * p.pitch + j * p.piece_bytes, slot + p.R * p.pitch + j * 8 * 80,
-                                        p.xstride, acc);
+    if (r_begin < r_end) {
+      ItemCursor it;
+      it.first(p, r_begin, r_end);
+      bool more = true;
+      for (int t = 0; more; ++t) {
+        const int s = t % p.nstages;
+        const FSeg& sg = p.seg[it.seg];
+        if (ok) ok = mbar_wait_bounded(&full[s], (uint32_t)((t / p.nstages) & 1));
+        if (ok) {
+          const int np = (int)min((int64_t)p.PPS, (int64_t)p.npieces - (int64_t)it.c * p.PPS);
+          const uint8_t* slot = stages + (size_t)s * p.stage_bytes;
+          const uint8_t* xbase = XSELF ? xsm + (int64_t)it.c * p.PPS * 8 * 80 : slot + p.R * p.max_pitch;
+          if (r < it.rows) {
+            for (int j = cw * p.KS + ks; j < np; j += lanes_per_piece)
+              run_piece<M, CODE>(sg.code, slot + r * sg.pitch + j * sg.piece_bytes, xbase + j * 8 * 80, xstride, acc);
           }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[s]);
+        } else {
+          s_fail = 1;
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-      } else {
-        s_fail = 1;
-      }
-      if (c == p.nchunks - 1) {
-        // row block done: reduce lane groups (shuffles) and warps (shared)
-        float* rd = red + (size_t)par * kRowsConsumers * 32 * M;
+        if (it.c == p.nchunks - 1) {
+          float* rd = red + (size_t)par * kRowsConsumers * 32 * M;
 #pragma unroll
-        for (int m = 0; m < M; ++m) {
-          float v = acc[m];
-          for (int o = p.R; o < 32; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-          rd[(cw * 32 + lane) * M + m] = v;
-          acc[m] = 0.f;
-        }
-        asm volatile("bar.sync 1, %0;" ::"r"(kRowsConsumers * 32) : "memory");
-        const int ct = tid - 32;
-        if (ct < rows * M && s_fail == 0) {
-          const int rr = ct / M, m = ct - rr * M;
-          float v = 0.f;
+          for (int m = 0; m < M; ++m) {
+            float v = acc[m];
+            for (int o = p.R; o < 32; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            rd[(cw * 32 + lane) * M + m] = v;
+            acc[m] = 0.f;
+          }
+          asm volatile("bar.sync 1, %0;" ::"r"(kRowsConsumers * 32) : "memory");
+          if (ct < it.rows * M && s_fail == 0) {
+            const int rr = ct / M, m = ct - rr * M;
+            float v = 0.f;
 #pragma unroll
-          for (int w = 0; w < kRowsConsumers; ++w) v += rd[(w * 32 + rr) * M + m];
-          p.y[(int64_t)m * p.N + row0 + rr] = v;
+            for (int w = 0; w < kRowsConsumers; ++w) v += rd[(w * 32 + rr) * M + m];
+            sg.y[(int64_t)m * sg.N + it.row0 + rr] = v;
+          }
+          par ^= 1;
         }
-        par ^= 1;
+        more = it.next(p, r_end);
       }
     }
   }
@@ -392,73 +508,113 @@ __global__ void __launch_bounds__(kRowsThreads) gemv_rows_kernel(const RowsParam
 
 // ---------------------------------------------------------------------------
 // Host side
-template <int TYPE>
-struct PieceGeom;
-template <> struct PieceGeom<NSQ_TYPE_Q4_K> { static constexpr int bytes = 144, align_pieces = 1; };
-template <> struct PieceGeom<NSQ_TYPE_Q6_K> { static constexpr int bytes = 210, align_pieces = 8; };
-template <> struct PieceGeom<NSQ_TYPE_Q4_0> { static constexpr int bytes = 144, align_pieces = 1; };
-template <> struct PieceGeom<NSQ_TYPE_Q8_0> { static constexpr int bytes = 272, align_pieces = 1; };
-
-constexpr int kRowsSmemBudget = 64 * 1024;
+constexpr int kXSelfMaxBytes = 40 * 1024;
 
 static int env_int(const char* name, int dflt) {
   const char* v = getenv(name);
   return (v && v[0]) ? atoi(v) : dflt;
 }
 
-// Plans a launch; false if the shape is not covered by this kernel (the
-// general kernel in gemv.cu then runs it).
-template <int TYPE>
-static bool plan_rows(int64_t N, int64_t K, int M, int num_sms, RowsParams& p, int& blocks, size_t& smem) {
-  using G = PieceGeom<TYPE>;
-  if (K % 256) return false;
+static int seg_code(int type, int layout) {
+  switch (type) {
+    case NSQ_TYPE_Q4_K: return kQ4K;
+    case NSQ_TYPE_Q6_K: return layout == NSQ_Q6K_NODESTOR ? kQ6KN : kQ6KG;
+    case NSQ_TYPE_Q4_0: return kQ40;
+    case NSQ_TYPE_Q8_0: return kQ80;
+    default: return -1;
+  }
+}
+static int piece_bytes_of(int type) {
+  switch (type) {
+    case NSQ_TYPE_Q4_K: return 144;
+    case NSQ_TYPE_Q6_K: return 210;
+    case NSQ_TYPE_Q4_0: return 144;
+    case NSQ_TYPE_Q8_0: return 272;
+    default: return 0;
+  }
+}
+
+// Plans a fused launch; false if a segment's shape is not covered (K % 256,
+// Q6_K needs K % 2048, 16-byte row alignment).
+static bool plan_fused(const nsq_segment* segs, int nseg, int64_t K, int M, bool xself, int num_sms, FusedParams& p,
+                       int& blocks, size_t& smem) {
+  if (nseg < 1 || nseg > NSQ_MAX_SEGMENTS || K % 256) return false;
   const int64_t npieces = K / 256;
-  if (npieces % G::align_pieces) return false;
-  const int64_t RB = npieces * G::bytes;
-  if (RB % 16) return false;
-  // rows per block: 8 (four lane groups per warp split each piece range);
-  // small matrices use fewer rows so that every SM gets work.  The
-  // NSQ_ROWS_* environment variables override the plan (tuning sweeps).
+  bool any_q6k = false;
+  int64_t T = 0;
+  for (int i = 0; i < nseg; ++i) {
+    const int t = segs[i].ggml_type;
+    if (seg_code(t, segs[i].q6k_layout) < 0) return false;
+    if (t == NSQ_TYPE_Q6_K) {
+      any_q6k = true;
+      if (npieces % 8) return false;
+    }
+    if ((npieces * piece_bytes_of(t)) % 16) return false;
+    T += segs[i].N;
+  }
   int R = env_int("NSQ_ROWS_R", 8);
   if (R != 4 && R != 8 && R != 16 && R != 32) R = 8;
-  while (R > 4 && (N + R - 1) / R < (int64_t)num_sms) R >>= 1;
+  while (R > 4 && (T + R - 1) / R < (int64_t)num_sms) R >>= 1;
   const int KS = 32 / R;
   int PPS = env_int("NSQ_ROWS_PPSM", 1) * kRowsConsumers * KS;
   if (PPS < 1) PPS = kRowsConsumers * KS;
-  if (PPS % G::align_pieces) PPS = ((PPS + G::align_pieces - 1) / G::align_pieces) * G::align_pieces;
+  if (any_q6k && PPS % 8) PPS = (PPS + 7) / 8 * 8;
   if (PPS > npieces) PPS = (int)npieces;
-  const int chunk_bytes = PPS * G::bytes;
-  const int pitch = ((chunk_bytes + 15) & ~15) + 16;
-  const int xstride = PPS * 8 * 80;
-  const int stage_bytes = (R * pitch + M * xstride + 127) & ~127;
   int nstages = env_int("NSQ_ROWS_STAGES", 2);
   if (nstages < 2 || nstages > 8) nstages = 2;
-  if ((size_t)stage_bytes * nstages > (size_t)kRowsSmemBudget && nstages > 2) nstages = 2;
-  smem = (size_t)stage_bytes * nstages + (size_t)2 * kRowsConsumers * 32 * M * 4 + 16 * nstages + 16;
-  if (smem > 200 * 1024) return false;
-  const int nchunks = (int)((npieces + PPS - 1) / PPS);
-  p.N = N; p.K = K; p.RB = RB;
-  p.R = R; p.KS = KS; p.PPS = PPS;
-  p.piece_bytes = G::bytes; p.chunk_bytes = chunk_bytes; p.pitch = pitch;
-  p.nchunks = nchunks; p.npieces = (int)npieces; p.xstride = xstride;
-  p.stage_bytes = stage_bytes; p.nstages = nstages; p.GX = K / 32;
-  // persistent grid: as many CTAs as fit on the GPU at once, but no more
-  // than there are row blocks
+  const size_t xsm = xself ? (size_t)M * (K / 32) * 80 : 0;
+  const int min_pps = any_q6k ? 8 : 1;
+  int max_pitch = 0, xstride = 0, stage_bytes = 0;
+  for (;;) {
+    // shrink the chunk until the stages fit in shared memory
+    max_pitch = 0;
+    for (int i = 0; i < nseg; ++i) {
+      const int cb = PPS * piece_bytes_of(segs[i].ggml_type);
+      const int pitch = ((cb + 15) & ~15) + 16;
+      if (pitch > max_pitch) max_pitch = pitch;
+    }
+    xstride = PPS * 8 * 80;
+    stage_bytes = (R * max_pitch + (xself ? 0 : M * xstride) + 127) & ~127;
+    smem = (size_t)stage_bytes * nstages + xsm + (size_t)2 * kRowsConsumers * 32 * M * 4 + 16 * nstages + 16;
+    if (smem <= 200 * 1024) break;
+    if (PPS / 2 < min_pps || (PPS / 2) % min_pps) return false;
+    PPS /= 2;
+  }
+  for (int i = 0; i < nseg; ++i) {
+    FSeg& f = p.seg[i];
+    const int pb = piece_bytes_of(segs[i].ggml_type);
+    f.w = static_cast<const uint8_t*>(segs[i].w);
+    f.y = segs[i].y;
+    f.N = segs[i].N;
+    f.RB = npieces * pb;
+    f.code = seg_code(segs[i].ggml_type, segs[i].q6k_layout);
+    f.piece_bytes = pb;
+    f.chunk_bytes = PPS * pb;
+    f.pitch = ((f.chunk_bytes + 15) & ~15) + 16;
+  }
+  int64_t acc_rows = 0;
+  for (int i = 0; i < nseg; ++i) {
+    p.seg[i].row0 = acc_rows;
+    acc_rows += p.seg[i].N;
+  }
+  p.nseg = nseg; p.T = T; p.K = K; p.GX = K / 32;
+  p.R = R; p.KS = KS; p.PPS = PPS; p.npieces = (int)npieces; p.nchunks = (int)((npieces + PPS - 1) / PPS);
+  p.xstride = xstride; p.stage_bytes = stage_bytes; p.nstages = nstages; p.max_pitch = max_pitch;
   int per_sm = (int)((220 * 1024) / (smem + 1024));
   if (per_sm > 4) per_sm = 4;
   if (per_sm < 1) per_sm = 1;
   const int cps = env_int("NSQ_ROWS_CPS", 0);
   if (cps >= 1 && cps <= per_sm) per_sm = cps;
   int64_t g = (int64_t)num_sms * per_sm;
-  const int64_t nrb = (N + R - 1) / R;
+  const int64_t nrb = (T + R - 1) / R;
   if (g > nrb) g = nrb;
   blocks = (int)g;
   return true;
 }
 
-template <int TYPE, int LAYOUT, int M>
-static cudaError_t launch_rows(const RowsParams& p, int blocks, size_t smem, cudaStream_t st) {
-  auto kern = gemv_rows_kernel<TYPE, LAYOUT, M>;
+template <int M, bool XSELF, int CODE>
+static cudaError_t launch_fused(const FusedParams& p, int blocks, size_t smem, cudaStream_t st) {
+  auto kern = gemv_fused_kernel<M, XSELF, CODE>;
   static size_t configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -480,54 +636,70 @@ static cudaError_t launch_rows(const RowsParams& p, int blocks, size_t smem, cud
   return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
-template <int TYPE, int LAYOUT>
-static int run_rows_t(const uint8_t* w, const XGroup* xg, float* y, int64_t M, int64_t N, int64_t K, cudaStream_t st,
-                      int num_sms) {
+template <bool XSELF, int CODE>
+static cudaError_t launch_fused_mc(int M, const FusedParams& p, int blocks, size_t smem, cudaStream_t st) {
+  switch (M) {
+    case 1: return launch_fused<1, XSELF, CODE>(p, blocks, smem, st);
+    case 2: return launch_fused<2, XSELF, CODE>(p, blocks, smem, st);
+    case 3: return launch_fused<3, XSELF, CODE>(p, blocks, smem, st);
+    default: return launch_fused<4, XSELF, CODE>(p, blocks, smem, st);
+  }
+}
+
+template <bool XSELF>
+static cudaError_t launch_fused_m(int M, const FusedParams& p, int blocks, size_t smem, cudaStream_t st) {
+  int code = p.seg[0].code;
+  for (int i = 1; i < p.nseg; ++i)
+    if (p.seg[i].code != code) code = kMixed;
+  switch (code) {
+    case kQ4K: return launch_fused_mc<XSELF, kQ4K>(M, p, blocks, smem, st);
+    case kQ6KG: return launch_fused_mc<XSELF, kQ6KG>(M, p, blocks, smem, st);
+    case kQ6KN: return launch_fused_mc<XSELF, kQ6KN>(M, p, blocks, smem, st);
+    case kQ40: return launch_fused_mc<XSELF, kQ40>(M, p, blocks, smem, st);
+    case kQ80: return launch_fused_mc<XSELF, kQ80>(M, p, blocks, smem, st);
+    default: return launch_fused_mc<XSELF, kMixed>(M, p, blocks, smem, st);
+  }
+}
+
+// True if the fused kernel can prepare the activations of M tokens on chip.
+bool fused_self_prepare_fits(int64_t M, int64_t K) { return M <= 4 && M * (K / 32) * 80 <= kXSelfMaxBytes; }
+
+// Fused decode GEMV.  xg == nullptr: activations are prepared on chip from x
+// (requires fused_self_prepare_fits); otherwise xg holds prepared records.
+// Returns NSQ_OK / an error, or -1 if a shape is not covered.
+int run_gemv_fused(const nsq_segment* segs, int nseg, const float* x, const XGroup* xg, int64_t M, int64_t K,
+                   cudaStream_t st, int num_sms) {
+  const bool xself = (xg == nullptr);
   for (int64_t m0 = 0; m0 < M; m0 += 4) {
     const int mm = (int)((M - m0) < 4 ? (M - m0) : 4);
-    RowsParams p{};
+    nsq_segment sl[NSQ_MAX_SEGMENTS];
+    for (int i = 0; i < nseg && i < NSQ_MAX_SEGMENTS; ++i) {
+      sl[i] = segs[i];
+      sl[i].y = segs[i].y + m0 * segs[i].N;
+    }
+    FusedParams p{};
     int blocks;
     size_t smem;
-    if (!plan_rows<TYPE>(N, K, mm, num_sms, p, blocks, smem)) return -1;
-    p.w = w;
-    p.xg = xg + m0 * (K / 32);
-    p.y = y + m0 * N;
-    cudaError_t e;
-    switch (mm) {
-      case 1: e = launch_rows<TYPE, LAYOUT, 1>(p, blocks, smem, st); break;
-      case 2: e = launch_rows<TYPE, LAYOUT, 2>(p, blocks, smem, st); break;
-      case 3: e = launch_rows<TYPE, LAYOUT, 3>(p, blocks, smem, st); break;
-      default: e = launch_rows<TYPE, LAYOUT, 4>(p, blocks, smem, st); break;
-    }
+    if (!plan_fused(sl, nseg, K, mm, xself, num_sms, p, blocks, smem)) return -1;
+    p.x = x ? x + m0 * K : nullptr;
+    p.xg = xg ? xg + m0 * (K / 32) : nullptr;
+    cudaError_t e = xself ? launch_fused_m<true>(mm, p, blocks, smem, st) : launch_fused_m<false>(mm, p, blocks, smem, st);
     if (e != cudaSuccess) return NSQ_ERR_CUDA;
   }
   return NSQ_OK;
 }
 
-// Returns NSQ_OK / an error, or -1 if the shape is not covered (caller falls
-// back to the general kernel).
-int run_gemv_rows(const uint8_t* w, int type, int layout, const XGroup* xg, float* y, int64_t M, int64_t N,
-                  int64_t K, cudaStream_t st, int num_sms) {
-  RowsParams probe{};
-  int b;
-  size_t sm;
-  const int mm = (int)(M < 4 ? M : 4);
-  switch (type) {
-    case NSQ_TYPE_Q4_K:
-      if (!plan_rows<NSQ_TYPE_Q4_K>(N, K, mm, num_sms, probe, b, sm)) return -1;
-      return run_rows_t<NSQ_TYPE_Q4_K, 0>(w, xg, y, M, N, K, st, num_sms);
-    case NSQ_TYPE_Q6_K:
-      if (!plan_rows<NSQ_TYPE_Q6_K>(N, K, mm, num_sms, probe, b, sm)) return -1;
-      if (layout == NSQ_Q6K_NODESTOR) return run_rows_t<NSQ_TYPE_Q6_K, NSQ_Q6K_NODESTOR>(w, xg, y, M, N, K, st, num_sms);
-      return run_rows_t<NSQ_TYPE_Q6_K, NSQ_Q6K_GGML>(w, xg, y, M, N, K, st, num_sms);
-    case NSQ_TYPE_Q4_0:
-      if (!plan_rows<NSQ_TYPE_Q4_0>(N, K, mm, num_sms, probe, b, sm)) return -1;
-      return run_rows_t<NSQ_TYPE_Q4_0, 0>(w, xg, y, M, N, K, st, num_sms);
-    case NSQ_TYPE_Q8_0:
-      if (!plan_rows<NSQ_TYPE_Q8_0>(N, K, mm, num_sms, probe, b, sm)) return -1;
-      return run_rows_t<NSQ_TYPE_Q8_0, 0>(w, xg, y, M, N, K, st, num_sms);
-    default: return -1;
+// Probe: would run_gemv_fused accept these segments?
+bool fused_covers(const nsq_segment* segs, int nseg, int64_t K) {
+  if (nseg < 1 || nseg > NSQ_MAX_SEGMENTS || K % 256) return false;
+  const int64_t npieces = K / 256;
+  for (int i = 0; i < nseg; ++i) {
+    const int t = segs[i].ggml_type;
+    if (seg_code(t, segs[i].q6k_layout) < 0) return false;
+    if (t == NSQ_TYPE_Q6_K && npieces % 8) return false;
+    if ((npieces * piece_bytes_of(t)) % 16) return false;
   }
+  return true;
 }
 
 }  // namespace nsq

@@ -26,6 +26,7 @@ environment variable NSQ_MATMUL_PATH=gemv|gemm forces one of them.
 """
 from __future__ import annotations
 
+import ctypes
 import os
 from typing import Optional
 
@@ -104,6 +105,27 @@ class CudaEngine:
                                 self._stream()), "nsq_gemv")
         self._sync(sync)
         return y
+
+    def gemv_multi(self, segments, x: torch.Tensor, k: int, sync: bool = True):
+        """Fused GEMV over matrices sharing `x` (q|k|v, gate|up).
+
+        segments: list of (w, ggml_type, n) or (w, ggml_type, n, q6k_layout);
+        returns the list of outputs [m, n_s] (f32)."""
+        m = x.numel() // k
+        segs = (_lib.Segment * len(segments))()
+        outs = []
+        for i, sg in enumerate(segments):
+            w, t, n = sg[0], sg[1], sg[2]
+            layout = sg[3] if len(sg) > 3 else Q6K_GGML
+            y = torch.empty((m, n), dtype=torch.float32, device=self.device)
+            outs.append(y)
+            segs[i] = _lib.Segment(_ptr(w), t, layout, n, _ptr(y))
+        wsb = self.lib.nsq_gemv_workspace_size(m, k)
+        ws = self.workspace(wsb)
+        check(self.lib.nsq_gemv_multi(ctypes.cast(segs, ctypes.c_void_p), len(segments), _ptr(x), m, k, _ptr(ws),
+                                      ws.numel(), self._stream()), "nsq_gemv_multi")
+        self._sync(sync)
+        return outs
 
     def prepare(self, x: torch.Tensor, k: int, ws: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Prepare activations once for several GEMVs (q|k|v, gate|up)."""

@@ -69,11 +69,17 @@ def test_host_side_argument_errors(lib):
     assert lib.nsq_gemv(al, 12, 0, al, al, 1, 16, 300, al, 1 << 20, None) == _lib.ERR_SHAPE
     assert lib.nsq_gemv(al, 12, 0, al, al, 17, 16, 256, al, 1 << 20, None) == _lib.ERR_SHAPE
     assert lib.nsq_gemv(al, 12, 0, al, al, 0, 16, 256, al, 1 << 20, None) == _lib.ERR_SHAPE
-    assert lib.nsq_gemv(al, 12, 0, al, al, 1, 16, 256, al, 10, None) == _lib.ERR_WORKSPACE
-    assert lib.nsq_gemv(al, 12, 0, al, al, 1, 16, 256, None, 1 << 20, None) == _lib.ERR_WORKSPACE
+    x4 = ctypes.c_void_p(0x10004)  # only 4-byte aligned: needs the workspace path
+    assert lib.nsq_gemv(al, 12, 0, x4, al, 1, 16, 256, al, 10, None) == _lib.ERR_WORKSPACE
+    assert lib.nsq_gemv(al, 12, 0, x4, al, 1, 16, 256, None, 1 << 20, None) == _lib.ERR_WORKSPACE
+    assert lib.nsq_gemv(al, 12, 0, ctypes.c_void_p(0x10002), al, 1, 16, 256, al, 1 << 20, None) == _lib.ERR_ALIGN
     assert lib.nsq_gemv(al, 12, 0, None, al, 1, 16, 256, al, 1 << 20, None) == _lib.ERR_NULL
     assert lib.nsq_gemm_bf16(al, 8, 0, al, al, 128, 128, 96, None) == _lib.ERR_SHAPE
     assert lib.nsq_gemm_bf16(al, 12, 0, ctypes.c_void_p(0x10004), al, 128, 128, 256, None) == _lib.ERR_ALIGN
+    segs = (_lib.Segment * 2)(_lib.Segment(0x10000, 12, 0, 16, 0x10000), _lib.Segment(0x10000, 3, 0, 16, 0x10000))
+    assert lib.nsq_gemv_multi(ctypes.cast(segs, ctypes.c_void_p), 2, al, 1, 256, None, 0, None) == _lib.ERR_TYPE
+    assert lib.nsq_gemv_multi(ctypes.cast(segs, ctypes.c_void_p), 5, al, 1, 256, None, 0, None) == _lib.ERR_SHAPE
+    assert lib.nsq_gemv_multi(None, 1, al, 1, 256, None, 0, None) == _lib.ERR_NULL
     assert lib.nsq_matmul_f32(None, al, al, 2, 2, 2, None) == _lib.ERR_NULL
     assert lib.nsq_matmul_f32(al, al, al, 0, 2, 2, None) == _lib.ERR_SHAPE
 

@@ -136,6 +136,42 @@ def test_gemv_micro_config(eng, oracle):
     assert rel_err(y, ref) <= GEMV_TOL
 
 
+@pytest.mark.parametrize("m", [1, 2, 4, 5])
+def test_gemv_multi_mixed_segments(eng, oracle, m):
+    """Fused q|k|v-style launch: two Q4_K segments and a Q6_K one sharing x."""
+    k = 2048
+    specs = [(Q4_K, 0, 200), (Q4_K, 0, 64), (Q6_K, Q6K_GGML, 72)]
+    ws = [Q.synthetic_weights(n, k, t, seed=50 + i, q6k_layout=l) for i, (t, l, n) in enumerate(specs)]
+    x = Q.synthetic_activations(m, k, seed=51)
+    outs = eng.gemv_multi([(eng.upload(w), t, n, l) for w, (t, l, n) in zip(ws, specs)],
+                          torch.from_numpy(x).to(eng.device), k)
+    for w, (t, l, n), y in zip(ws, specs, outs):
+        assert rel_err(y.cpu().numpy(), oracle.quant_matmul(w, t, x, n, k, l)) <= GEMV_TOL
+
+
+def test_gemv_multi_workspace_mode(eng, oracle):
+    """M * K too large for on-chip preparation: activations go through the workspace."""
+    m, k = 4, 14336
+    specs = [(Q4_K, 0, 40), (Q6_K, Q6K_NODESTOR, 24)]
+    ws = [Q.synthetic_weights(n, k, t, seed=60 + i, q6k_layout=l) for i, (t, l, n) in enumerate(specs)]
+    x = Q.synthetic_activations(m, k, seed=61)
+    outs = eng.gemv_multi([(eng.upload(w), t, n, l) for w, (t, l, n) in zip(ws, specs)],
+                          torch.from_numpy(x).to(eng.device), k)
+    for w, (t, l, n), y in zip(ws, specs, outs):
+        assert rel_err(y.cpu().numpy(), oracle.quant_matmul(w, t, x, n, k, l, threads=8)) <= GEMV_TOL
+
+
+def test_gemv_unaligned_activations(eng, oracle):
+    """x only 4-byte aligned: taken through the workspace path."""
+    n, k = 96, 1024
+    w = Q.synthetic_weights(n, k, Q4_K, seed=70)
+    x = Q.synthetic_activations(1, k, seed=71)
+    buf = torch.empty(k + 1, device=eng.device)
+    buf[1:] = torch.from_numpy(x[0]).to(eng.device)
+    y = eng.gemv(eng.upload(w), Q4_K, buf[1:], n, k).cpu().numpy()
+    assert rel_err(y, oracle.quant_matmul(w, Q4_K, x, n, k)) <= GEMV_TOL
+
+
 def test_gemv_prepared_shares_activations(eng, oracle):
     k = 1024
     x = Q.synthetic_activations(2, k, seed=9)
