@@ -123,6 +123,26 @@ int nsq_gemv_prepared(const void *w, int ggml_type, int q6k_layout, const void *
                       float *y, int64_t M, int64_t N, int64_t K, void *stream);
 
 /*
+ * nsq_gemv for callers that cannot allocate device memory.  This entry point
+ * has no counterpart in the reference.  It computes what nsq_gemv computes
+ * (same kernels, same accuracy) but keeps the prepared activations in a
+ * fixed scratch array inside the library (NSQ_NOALLOC_MAX_ELEMS / 32 records
+ * of 80 bytes, 640 KiB, held by every GPU that loads the library until the
+ * process exits), so the call allocates nothing and takes no workspace.
+ * For engines whose memory is entirely owned by another allocator, or code
+ * that may not call cudaMalloc (it can synchronise the device).
+ *   - M * K must not exceed NSQ_NOALLOC_MAX_ELEMS; larger calls return
+ *     NSQ_ERR_WORKSPACE.
+ *   - All calls share the array: calls that overlap on the GPU (unordered
+ *     streams or threads) race and give wrong results.
+ *   - The first call on a device looks up the array's device address; make
+ *     it before capturing a stream into a CUDA graph.
+ */
+#define NSQ_NOALLOC_MAX_ELEMS 262144 /* M * K */
+int nsq_gemv_noalloc(const void *w, int ggml_type, int q6k_layout, const float *x, float *y,
+                     int64_t M, int64_t N, int64_t K, void *stream);
+
+/*
  * Fused decode GEMV over several weight matrices that share one activation
  * (the q|k|v or gate|up projections of a transformer layer): for every
  * segment s, segs[s].y[M x N_s] = x[M x K] . W_s^T.  One launch streams all

@@ -42,6 +42,7 @@ SIGNATURES = [
     ("nsq_prepare_activations", _int, [_vp, _i64, _i64, _vp, _sz, _vp]),
     ("nsq_gemv_prepared", _int, [_vp, _int, _int, _vp, _vp, _i64, _i64, _i64, _vp]),
     ("nsq_gemv_multi", _int, [ctypes.c_void_p, _int, _vp, _i64, _i64, _vp, _sz, _vp]),
+    ("nsq_gemv_noalloc", _int, [_vp, _int, _int, _vp, _vp, _i64, _i64, _i64, _vp]),
     ("nsq_gemm_bf16", _int, [_vp, _int, _int, _vp, _vp, _i64, _i64, _i64, _vp]),
     ("nsq_matmul_f32", _int, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
 ]
@@ -54,6 +55,7 @@ class Segment(ctypes.Structure):
 
 
 MAX_SEGMENTS = 4
+NOALLOC_MAX_ELEMS = 262144  # NSQ_NOALLOC_MAX_ELEMS: largest M * K of nsq_gemv_noalloc
 
 
 class NsqError(RuntimeError):
