@@ -233,7 +233,7 @@ int nsq_gemm_bf16(const void* w, int ggml_type, int q6k_layout, const void* x_bf
                   int64_t N, int64_t K, void* stream) {
   int rc = check_weights(w, ggml_type, q6k_layout, K);
   if (rc) return rc;
-  if (M < 1 || N < 1 || K % 64) return NSQ_ERR_SHAPE;
+  if (M < 1 || N < 1 || K % 256) return NSQ_ERR_SHAPE;
   if (M > (int64_t)1 << 24 || N > (int64_t)1 << 24) return NSQ_ERR_SHAPE;
   if (!x_bf16 || !y_bf16) return NSQ_ERR_NULL;
   if ((reinterpret_cast<uintptr_t>(x_bf16) & 15) || (reinterpret_cast<uintptr_t>(y_bf16) & 15)) return NSQ_ERR_ALIGN;

@@ -39,10 +39,20 @@ namespace nsq {
 
 constexpr int GEMM_BM = 128;   // W rows per CTA (UMMA M)
 constexpr int GEMM_BK = 64;    // K per stage (bf16: 128 bytes per row)
-constexpr int GEMM_STAGES = 4;
+constexpr int GEMM_STAGES = 3;     // bf16 W / x stages (64-wide K blocks)
+constexpr int GEMM_RAW_STAGES = 2; // raw GGUF byte stages (256-wide K columns)
 constexpr int GEMM_THREADS = 384;
 constexpr int GEMM_DQ_WARP0 = 4;  // first dequant / epilogue warp
 constexpr int GEMM_DQ_THREADS = 256;
+
+// Raw bytes of one row for one 256-weight column of K: a K-quant
+// super-block, or 8 Q4_0 / Q8_0 blocks.  Q6_K columns (210 B) start at any
+// even offset, so their copies carry up to 15 bytes of slack on each side.
+template <int TYPE> struct RawCol;
+template <> struct RawCol<NSQ_TYPE_Q4_K> { static constexpr int bytes = 144, pitch = 144; };
+template <> struct RawCol<NSQ_TYPE_Q4_0> { static constexpr int bytes = 144, pitch = 144; };
+template <> struct RawCol<NSQ_TYPE_Q8_0> { static constexpr int bytes = 272, pitch = 272; };
+template <> struct RawCol<NSQ_TYPE_Q6_K> { static constexpr int bytes = 210, pitch = 240; };
 
 // ---------------------------------------------------------------------------
 // tcgen05 / TMA PTX wrappers
@@ -87,6 +97,9 @@ __device__ __forceinline__ void tc_ld_32x32b_x32(uint32_t taddr, uint32_t (&v)[3
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
@@ -120,37 +133,35 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
 }
-__device__ __forceinline__ uint32_t ldg_u16(const uint8_t* p) {
-  return __ldg(reinterpret_cast<const unsigned short*>(p));
-}
 
+// Dequant of 32 weights of one row for one 64-wide K block q (0..3) of a
+// 256-weight column whose raw bytes `raw` sit in shared memory; h picks
+// which 32 of the 64.  Same formulas and roundings as dequant.cu.
 template <int TYPE, int LAYOUT>
-__device__ __forceinline__ void dequant_row_kblock(const uint8_t* __restrict__ row, int kb, int h, uint32_t (&out)[16],
+__device__ __forceinline__ void dequant_col_kblock(const uint8_t* raw, int q, int h, uint32_t (&out)[16],
                                                    int (&chunk)[4]) {
   float v[32];
   if constexpr (TYPE == NSQ_TYPE_Q4_K) {
-    const int b = kb >> 2, p = kb & 3;
-    const uint8_t* blk = row + (int64_t)b * 144;
-    const uint4 hdr = __ldg(reinterpret_cast<const uint4*>(blk));
-    const uint4 q = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 32 * p + 16 * h));
+    const uint4 hdr = *reinterpret_cast<const uint4*>(raw);
+    const uint4 qv = *reinterpret_cast<const uint4*>(raw + 16 + 32 * q + 16 * h);
     const float d = h2f((uint16_t)(hdr.x & 0xFFFF)), dmin = h2f((uint16_t)(hdr.x >> 16));
     uint32_t sc[2], mn[2];
 #pragma unroll
-    for (int s = 0; s < 2; ++s) {
-      const int j = 2 * p + s;
+    for (int s2 = 0; s2 < 2; ++s2) {
+      const int j = 2 * q + s2;
       if (j < 4) {
-        sc[s] = (hdr.y >> (8 * j)) & 63;
-        mn[s] = (hdr.z >> (8 * j)) & 63;
+        sc[s2] = (hdr.y >> (8 * j)) & 63;
+        mn[s2] = (hdr.z >> (8 * j)) & 63;
       } else {
         const int sh = 8 * (j - 4);
         const uint32_t b2 = (hdr.w >> sh) & 0xFF, b0 = (hdr.y >> sh) & 0xFF, b1 = (hdr.z >> sh) & 0xFF;
-        sc[s] = (b2 & 0xF) | ((b0 >> 6) << 4);
-        mn[s] = (b2 >> 4) | ((b1 >> 6) << 4);
+        sc[s2] = (b2 & 0xF) | ((b0 >> 6) << 4);
+        mn[s2] = (b2 >> 4) | ((b1 >> 6) << 4);
       }
     }
     const float d1 = __fmul_rn(d, (float)sc[0]), m1 = __fmul_rn(dmin, (float)mn[0]);
     const float d2 = __fmul_rn(d, (float)sc[1]), m2 = __fmul_rn(dmin, (float)mn[1]);
-    const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+    const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       const uint32_t byte = (qw[i >> 2] >> (8 * (i & 3))) & 0xFF;
@@ -159,73 +170,63 @@ __device__ __forceinline__ void dequant_row_kblock(const uint8_t* __restrict__ r
     }
     chunk[0] = 2 * h; chunk[1] = 2 * h + 1; chunk[2] = 4 + 2 * h; chunk[3] = 5 + 2 * h;
   } else if constexpr (TYPE == NSQ_TYPE_Q6_K) {
-    const int b = kb >> 2, q = kb & 3;
-    const uint8_t* blk = row + (int64_t)b * 210;
-    const float d = h2f((uint16_t)ldg_u16(blk + 208));
+    const float d = h2f((uint16_t)ld_u16(raw + 208));
     if constexpr (LAYOUT == NSQ_Q6K_NODESTOR) {
       // elements e = 64q + 32h + l: ql[e>>1], qh[e>>2], scale byte [e>>4]
-      const uint8_t* ql = blk + 32 * q + 16 * h;
-      const uint8_t* qh = blk + 128 + 16 * q + 8 * h;
-      const uint32_t s01 = ldg_u16(blk + 192 + 4 * q + 2 * h);
+      uint32_t ql[4], qh[2];
+      ld_words_unaligned<4>(raw + 32 * q + 16 * h, ql);
+      ld_words_unaligned<2>(raw + 128 + 16 * q + 8 * h, qh);
+      const uint32_t s01 = ld_u16(raw + 192 + 4 * q + 2 * h);
       const float sa = __fmul_rn(d, (float)((int)(s01 & 0xFF) - 128) / 64.0f);
       const float sb = __fmul_rn(d, (float)((int)(s01 >> 8) - 128) / 64.0f);
 #pragma unroll
       for (int t = 0; t < 8; ++t) {
-        const uint32_t l2 = ldg_u16(ql + 2 * t);  // elements 4t .. 4t+3
-        const uint32_t hb = (t & 1) ? (ldg_u16(qh + (t & ~1)) >> 8) : (ldg_u16(qh + t) & 0xFF);
+        const uint32_t l2 = (ql[t >> 1] >> (16 * (t & 1))) & 0xFFFF;  // elements 4t .. 4t+3
+        const uint32_t hb = (qh[t >> 2] >> (8 * (t & 3))) & 0xFF;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const uint32_t lo = (l2 >> (4 * e)) & 0xF;  // byte e>>1, nibble e&1
+          const uint32_t lo = (l2 >> (4 * e)) & 0xF;
           const uint32_t hi = (hb >> (2 * e)) & 3;
-          const int qq = (int)(lo | (hi << 4)) - 32;
-          v[4 * t + e] = __fmul_rn(t < 4 ? sa : sb, (float)qq);
+          v[4 * t + e] = __fmul_rn(t < 4 ? sa : sb, (float)((int)(lo | (hi << 4)) - 32));
         }
       }
     } else {
       // ggml: n = q>>1, group j = 2(q&1) + h; ql[64n + 32h + l] nibble (q&1),
-      // qh[32n + l] bits 2j, scale int8 sc[8n + l/16 + 2j]
+      // qh[32n + l] bits 2j, int8 scale sc[8n + l/16 + 2j]
       const int n = q >> 1, j = 2 * (q & 1) + h, nib = q & 1;
-      const uint8_t* ql = blk + 64 * n + 32 * h;
-      const uint8_t* qh = blk + 128 + 32 * n;
-      const uint32_t s01 = ldg_u16(blk + 192 + 8 * n + 2 * j);
+      uint32_t ql[8], qh[8];
+      ld_words_unaligned<8>(raw + 64 * n + 32 * h, ql);
+      ld_words_unaligned<8>(raw + 128 + 32 * n, qh);
+      const uint32_t s01 = ld_u16(raw + 192 + 8 * n + 2 * j);
       const float sa = __fmul_rn(d, (float)(int8_t)(s01 & 0xFF));
       const float sb = __fmul_rn(d, (float)(int8_t)(s01 >> 8));
 #pragma unroll
-      for (int t = 0; t < 16; ++t) {
-        const uint32_t l2 = ldg_u16(ql + 2 * t), h2 = ldg_u16(qh + 2 * t);
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const uint32_t lo = ((l2 >> (8 * e)) >> (4 * nib)) & 0xF;
-          const uint32_t hi = ((h2 >> (8 * e)) >> (2 * j)) & 3;
-          const int qq = (int)(lo | (hi << 4)) - 32;
-          v[2 * t + e] = __fmul_rn(t < 8 ? sa : sb, (float)qq);
-        }
+      for (int l = 0; l < 32; ++l) {
+        const uint32_t lo = (ql[l >> 2] >> (8 * (l & 3) + 4 * nib)) & 0xF;
+        const uint32_t hi = (qh[l >> 2] >> (8 * (l & 3) + 2 * j)) & 3;
+        v[l] = __fmul_rn(l < 16 ? sa : sb, (float)((int)(lo | (hi << 4)) - 32));
       }
     }
     chunk[0] = 4 * h; chunk[1] = 4 * h + 1; chunk[2] = 4 * h + 2; chunk[3] = 4 * h + 3;
   } else if constexpr (TYPE == NSQ_TYPE_Q4_0) {
-    const uint8_t* blk = row + (int64_t)(2 * kb + h) * 18;
-    const float d = h2f((uint16_t)ldg_u16(blk));
+    const uint8_t* blk = raw + (2 * q + h) * 18;
+    const float d = h2f((uint16_t)ld_u16(blk));
+    uint32_t qs[4];
+    ld_words_unaligned<4>(blk + 2, qs);
 #pragma unroll
-    for (int t = 0; t < 8; ++t) {
-      const uint32_t b2 = ldg_u16(blk + 2 + 2 * t);
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const uint32_t byte = (b2 >> (8 * e)) & 0xFF;
-        v[2 * t + e] = __fmul_rn((float)((int)(byte & 0xF) - 8), d);
-        v[16 + 2 * t + e] = __fmul_rn((float)((int)(byte >> 4) - 8), d);
-      }
+    for (int i = 0; i < 16; ++i) {
+      const uint32_t byte = (qs[i >> 2] >> (8 * (i & 3))) & 0xFF;
+      v[i] = __fmul_rn((float)((int)(byte & 0xF) - 8), d);
+      v[16 + i] = __fmul_rn((float)((int)(byte >> 4) - 8), d);
     }
     chunk[0] = 4 * h; chunk[1] = 4 * h + 1; chunk[2] = 4 * h + 2; chunk[3] = 4 * h + 3;
   } else {  // Q8_0
-    const uint8_t* blk = row + (int64_t)(2 * kb + h) * 34;
-    const float d = h2f((uint16_t)ldg_u16(blk));
+    const uint8_t* blk = raw + (2 * q + h) * 34;
+    const float d = h2f((uint16_t)ld_u16(blk));
+    uint32_t qs[8];
+    ld_words_unaligned<8>(blk + 2, qs);
 #pragma unroll
-    for (int t = 0; t < 16; ++t) {
-      const uint32_t b2 = ldg_u16(blk + 2 + 2 * t);
-      v[2 * t] = __fmul_rn(d, (float)(int8_t)(b2 & 0xFF));
-      v[2 * t + 1] = __fmul_rn(d, (float)(int8_t)(b2 >> 8));
-    }
+    for (int i = 0; i < 32; ++i) v[i] = __fmul_rn(d, (float)(int8_t)((qs[i >> 2] >> (8 * (i & 3))) & 0xFF));
     chunk[0] = 4 * h; chunk[1] = 4 * h + 1; chunk[2] = 4 * h + 2; chunk[3] = 4 * h + 3;
   }
 #pragma unroll
@@ -237,34 +238,45 @@ struct GemmParams {
   const uint8_t* w;
   __nv_bfloat16* y;
   int64_t M, N, K, RB;
+  int wmap_ok;  // 1: raw weight columns come by one 2-D TMA box per column
 };
 
 template <int TYPE, int LAYOUT, int TOK>
 __global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap xmap,
+                                                                   const __grid_constant__ CUtensorMap wmap,
                                                                    const GemmParams p) {
   constexpr uint32_t W_STAGE = GEMM_BM * 128;  // bytes
   constexpr uint32_t X_STAGE = TOK * 128;
+  constexpr uint32_t RAW_STAGE = GEMM_BM * RawCol<TYPE>::pitch;
+  constexpr int CB = RawCol<TYPE>::bytes;
   constexpr uint32_t IDESC = umma_idesc_bf16(GEMM_BM, TOK);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* w_sm = smem;
   uint8_t* x_sm = smem + GEMM_STAGES * W_STAGE;
-  uint64_t* full = reinterpret_cast<uint64_t*>(x_sm + GEMM_STAGES * X_STAGE);
+  uint8_t* raw_sm = x_sm + GEMM_STAGES * X_STAGE;
+  uint64_t* full = reinterpret_cast<uint64_t*>(raw_sm + GEMM_RAW_STAGES * RAW_STAGE);
   uint64_t* empty = full + GEMM_STAGES;
-  uint64_t* accum = empty + GEMM_STAGES;
+  uint64_t* raw_full = empty + GEMM_STAGES;
+  uint64_t* raw_empty = raw_full + GEMM_RAW_STAGES;
+  uint64_t* accum = raw_empty + GEMM_RAW_STAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
-  __shared__ int s_abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t n0 = (int64_t)blockIdx.x * GEMM_BM;
   const int m0 = (int)blockIdx.y * TOK;
   const int KB = (int)(p.K / GEMM_BK);
+  const int NCOL = KB / 4;  // 256-wide K columns
+  const int rows_valid = (int)min((int64_t)GEMM_BM, p.N - n0);
 
   if (threadIdx.x == 0) {
-    s_abort = 0;
     for (int s = 0; s < GEMM_STAGES; ++s) {
       mbar_init(&full[s], 1 + GEMM_DQ_THREADS / 32);
       mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < GEMM_RAW_STAGES; ++s) {
+      mbar_init(&raw_full[s], 1);
+      mbar_init(&raw_empty[s], GEMM_DQ_THREADS / 32);
     }
     mbar_init(accum, 1);
     fence_mbar_init();
@@ -280,19 +292,18 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_tc_kernel(const __grid_c
   const uint32_t tmem_d = *tmem_slot;
 
   if (warp == 0) {
+    // ---- x tiles: TMA 2-D, 128B swizzle
     if (lane == 0) {
       for (int kb = 0; kb < KB; ++kb) {
         const int s = kb % GEMM_STAGES;
         const uint32_t par = (uint32_t)((kb / GEMM_STAGES) & 1);
-        if (!mbar_wait_bounded(&empty[s], par ^ 1)) {
-          s_abort = 1;
-          break;
-        }
+        if (!mbar_wait_bounded(&empty[s], par ^ 1)) break;
         mbar_arrive_expect_tx(&full[s], X_STAGE);
         tma_load_2d(x_sm + s * X_STAGE, &xmap, kb * GEMM_BK, m0, &full[s]);
       }
     }
   } else if (warp == 1) {
+    // ---- MMA issue (one thread)
     if (lane == 0) {
       const uint32_t w_base = smem_u32(w_sm), x_base = smem_u32(x_sm);
       bool ok = true;
@@ -300,7 +311,6 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_tc_kernel(const __grid_c
         const int s = kb % GEMM_STAGES;
         const uint32_t par = (uint32_t)((kb / GEMM_STAGES) & 1);
         if (!mbar_wait_bounded(&full[s], par)) {
-          s_abort = 1;
           ok = false;
           break;
         }
@@ -315,49 +325,108 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_tc_kernel(const __grid_c
       }
       if (ok) tc_commit(accum);
     }
+  } else if (warp == 2) {
+    // ---- raw GGUF bytes of the CTA's 128 rows, one 256-wide column at a time
+    const int64_t total = p.N * p.RB;
+    const int64_t cap = total & ~int64_t(15);
+    for (int c = 0; c < NCOL; ++c) {
+      const int rs = c % GEMM_RAW_STAGES;
+      if (!mbar_wait_bounded(&raw_empty[rs], (uint32_t)(((c / GEMM_RAW_STAGES) & 1) ^ 1))) break;
+      fence_proxy_async_smem();
+      uint8_t* dst = raw_sm + rs * RAW_STAGE;
+      if (p.wmap_ok) {
+        // rows are 16-byte aligned: one 2-D box [128 rows x pitch bytes]
+        // (16-bit elements) starting at the column's 16-byte aligned offset
+        if (lane == 0) {
+          const int x0 = (int)(((int64_t)c * CB) & ~int64_t(15)) / 2;
+          mbar_arrive_expect_tx(&raw_full[rs], RAW_STAGE);
+          tma_load_2d(dst, &wmap, x0, (int)n0, &raw_full[rs]);
+        }
+      } else {
+        // one 1-D bulk copy per row (16-byte aligned span of the column)
+        uint32_t bytes = 0;
+        for (int r = lane; r < rows_valid; r += 32) {
+          const int64_t off = (n0 + r) * p.RB + (int64_t)c * CB;
+          const int64_t a16 = off & ~int64_t(15);
+          int64_t e16 = (off + CB + 15) & ~int64_t(15);
+          if (e16 > cap) e16 = cap > a16 ? cap : a16;
+          bytes += (uint32_t)(e16 - a16);
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) bytes += __shfl_xor_sync(0xffffffffu, bytes, o);
+        if (lane == 0) mbar_expect_tx(&raw_full[rs], bytes);
+        __syncwarp();
+        for (int r = lane; r < rows_valid; r += 32) {
+          const int64_t off = (n0 + r) * p.RB + (int64_t)c * CB;
+          const int64_t a16 = off & ~int64_t(15);
+          int64_t e16 = (off + CB + 15) & ~int64_t(15);
+          if (e16 > cap) {
+            // the tensor ends inside this span: copy the tail bytes by hand
+            for (int64_t i = cap > a16 ? cap : a16; i < off + CB; ++i)
+              dst[r * RawCol<TYPE>::pitch + (i - a16)] = p.w[i];
+            e16 = cap > a16 ? cap : a16;
+          }
+          if (e16 > a16) bulk_g2s(dst + r * RawCol<TYPE>::pitch, p.w + a16, (uint32_t)(e16 - a16), &raw_full[rs]);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&raw_full[rs]);
+      }
+    }
   } else if (warp >= GEMM_DQ_WARP0) {
+    // ---- dequant: each quarter-warp covers 8 distinct rows of one half,
+    // so its 16-byte swizzled stores hit 8 distinct bank groups
     const int t = threadIdx.x - GEMM_DQ_WARP0 * 32;  // 0..255
-    const int r = t >> 1, h = t & 1;
-    const int64_t grow = n0 + r;
-    const uint8_t* rowp = p.w + (grow < p.N ? grow : 0) * p.RB;
+    const int h = (t >> 3) & 1;
+    const int r = (t & 7) | ((t >> 4) << 3);
+    const bool row_ok = r < rows_valid;
     bool ok = true;
     for (int kb = 0; kb < KB; ++kb) {
+      const int c = kb >> 2, q = kb & 3, rs = c % GEMM_RAW_STAGES;
       const int s = kb % GEMM_STAGES;
-      const uint32_t par = (uint32_t)((kb / GEMM_STAGES) & 1);
+      if (q == 0 && !mbar_wait_bounded(&raw_full[rs], (uint32_t)((c / GEMM_RAW_STAGES) & 1))) {
+        ok = false;
+        break;
+      }
       uint32_t pk[16];
       int chunk[4];
-      if (grow < p.N) {
-        dequant_row_kblock<TYPE, LAYOUT>(rowp, kb, h, pk, chunk);
+      if (row_ok) {
+        const int64_t off = (n0 + r) * p.RB + (int64_t)c * CB;
+        const uint8_t* raw = raw_sm + rs * RAW_STAGE + r * RawCol<TYPE>::pitch + (int)(off & 15);
+        dequant_col_kblock<TYPE, LAYOUT>(raw, q, h, pk, chunk);
       } else {
 #pragma unroll
         for (int i = 0; i < 16; ++i) pk[i] = 0u;
         chunk[0] = 4 * h; chunk[1] = 4 * h + 1; chunk[2] = 4 * h + 2; chunk[3] = 4 * h + 3;
       }
-      if (!mbar_wait_bounded(&empty[s], par ^ 1)) {
-        s_abort = 1;
+      if (q == 3) {
+        // this column's raw bytes are no longer read by this warp
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&raw_empty[rs]);
+      }
+      if (!mbar_wait_bounded(&empty[s], (uint32_t)(((kb / GEMM_STAGES) & 1) ^ 1))) {
         ok = false;
         break;
       }
       uint8_t* dst = w_sm + s * W_STAGE + r * 128;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const int c = chunk[i] ^ (r & 7);
-        *reinterpret_cast<uint4*>(dst + c * 16) = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+        const int cc = chunk[i] ^ (r & 7);
+        *reinterpret_cast<uint4*>(dst + cc * 16) = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
       }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&full[s]);
     }
-    // epilogue
+    // ---- epilogue
     if (ok && mbar_wait_bounded(accum, 0)) {
       tc_fence_after();
-      const int q = warp & 3;
+      const int qd = warp & 3;
       const int half = (warp - GEMM_DQ_WARP0) >> 2;
-      const int64_t n = n0 + 32 * q + lane;
+      const int64_t n = n0 + 32 * qd + lane;
 #pragma unroll 1
       for (int c0 = half * (TOK / 2); c0 < (half + 1) * (TOK / 2); c0 += 32) {
         uint32_t v[32];
-        tc_ld_32x32b_x32(tmem_d + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
+        tc_ld_32x32b_x32(tmem_d + ((uint32_t)(32 * qd) << 16) + (uint32_t)c0, v);
         if (n < p.N) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
@@ -366,8 +435,6 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_tc_kernel(const __grid_c
           }
         }
       }
-    } else {
-      s_abort = 1;
     }
   }
   tc_fence_before();
@@ -393,15 +460,17 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return fn;
 }
 
-template <int TOK>
+template <int TYPE, int TOK>
 static size_t gemm_smem_bytes() {
-  return 1024 + (size_t)GEMM_STAGES * (GEMM_BM * 128 + TOK * 128) + (2 * GEMM_STAGES + 1) * 8 + 16;
+  return 1024 + (size_t)GEMM_STAGES * (GEMM_BM * 128 + TOK * 128) +
+         (size_t)GEMM_RAW_STAGES * GEMM_BM * RawCol<TYPE>::pitch + (2 * GEMM_STAGES + 2 * GEMM_RAW_STAGES + 1) * 8 +
+         16;
 }
 
 template <int TYPE, int LAYOUT, int TOK>
-static int launch_gemm_t(const CUtensorMap& map, const GemmParams& p, cudaStream_t st) {
+static int launch_gemm_t(const CUtensorMap& map, const CUtensorMap& wmap, const GemmParams& p, cudaStream_t st) {
   auto kern = gemm_tc_kernel<TYPE, LAYOUT, TOK>;
-  const size_t smem = gemm_smem_bytes<TOK>();
+  const size_t smem = gemm_smem_bytes<TYPE, TOK>();
   static bool configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -412,14 +481,31 @@ static int launch_gemm_t(const CUtensorMap& map, const GemmParams& p, cudaStream
   }
   dim3 grid((unsigned)((p.N + GEMM_BM - 1) / GEMM_BM), (unsigned)((p.M + TOK - 1) / TOK));
   if (grid.y > 65535) return NSQ_ERR_SHAPE;
-  kern<<<grid, GEMM_THREADS, smem, st>>>(map, p);
+  kern<<<grid, GEMM_THREADS, smem, st>>>(map, wmap, p);
   return cudaGetLastError() == cudaSuccess ? NSQ_OK : NSQ_ERR_CUDA;
 }
 
 template <int TYPE, int LAYOUT>
-static int run_gemm_t(const CUtensorMap& map128, const CUtensorMap& map256, const GemmParams& p, cudaStream_t st) {
-  if (p.M <= 128) return launch_gemm_t<TYPE, LAYOUT, 128>(map128, p, st);
-  return launch_gemm_t<TYPE, LAYOUT, 256>(map256, p, st);
+static int run_gemm_t(const CUtensorMap& xmap, const GemmParams& p0, cudaStream_t st) {
+  GemmParams p = p0;
+  alignas(64) CUtensorMap wmap{};
+  p.wmap_ok = 0;
+  if (p.RB % 16 == 0 && p.N <= 0x7FFFFFFF) {
+    // W viewed as [N rows x RB bytes] of 16-bit elements; box = one column
+    auto enc = get_encode_fn();
+    if (enc) {
+      cuuint64_t dims[2] = {(cuuint64_t)(p.RB / 2), (cuuint64_t)p.N};
+      cuuint64_t strides[1] = {(cuuint64_t)p.RB};
+      cuuint32_t box[2] = {(cuuint32_t)(RawCol<TYPE>::pitch / 2), (cuuint32_t)GEMM_BM};
+      cuuint32_t estr[2] = {1, 1};
+      if (enc(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint8_t*>(p.w), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
+        p.wmap_ok = 1;
+    }
+  }
+  if (p.M <= 128) return launch_gemm_t<TYPE, LAYOUT, 128>(xmap, wmap, p, st);
+  return launch_gemm_t<TYPE, LAYOUT, 256>(xmap, wmap, p, st);
 }
 
 static int encode_xmap(CUtensorMap* map, const void* x, int64_t M, int64_t K, int box_rows) {
@@ -437,7 +523,7 @@ static int encode_xmap(CUtensorMap* map, const void* x, int64_t M, int64_t K, in
 
 int run_gemm_bf16(const uint8_t* w, int type, int layout, const void* x, void* y, int64_t M, int64_t N, int64_t K,
                   cudaStream_t st, int /*num_sms*/) {
-  if (K % GEMM_BK) return NSQ_ERR_SHAPE;
+  if (K % 256) return NSQ_ERR_SHAPE;  // whole 256-weight columns
   GemmParams p{};
   p.w = w;
   p.y = static_cast<__nv_bfloat16*>(y);
@@ -450,12 +536,12 @@ int run_gemm_bf16(const uint8_t* w, int type, int layout, const void* x, void* y
   int rc = encode_xmap(&map, x, M, K, tok);
   if (rc) return rc;
   switch (type) {
-    case NSQ_TYPE_Q4_0: return run_gemm_t<NSQ_TYPE_Q4_0, 0>(map, map, p, st);
-    case NSQ_TYPE_Q8_0: return run_gemm_t<NSQ_TYPE_Q8_0, 0>(map, map, p, st);
-    case NSQ_TYPE_Q4_K: return run_gemm_t<NSQ_TYPE_Q4_K, 0>(map, map, p, st);
+    case NSQ_TYPE_Q4_0: return run_gemm_t<NSQ_TYPE_Q4_0, 0>(map, p, st);
+    case NSQ_TYPE_Q8_0: return run_gemm_t<NSQ_TYPE_Q8_0, 0>(map, p, st);
+    case NSQ_TYPE_Q4_K: return run_gemm_t<NSQ_TYPE_Q4_K, 0>(map, p, st);
     case NSQ_TYPE_Q6_K:
-      if (layout == NSQ_Q6K_NODESTOR) return run_gemm_t<NSQ_TYPE_Q6_K, NSQ_Q6K_NODESTOR>(map, map, p, st);
-      return run_gemm_t<NSQ_TYPE_Q6_K, NSQ_Q6K_GGML>(map, map, p, st);
+      if (layout == NSQ_Q6K_NODESTOR) return run_gemm_t<NSQ_TYPE_Q6_K, NSQ_Q6K_NODESTOR>(map, p, st);
+      return run_gemm_t<NSQ_TYPE_Q6_K, NSQ_Q6K_GGML>(map, p, st);
     default: return NSQ_ERR_TYPE;
   }
 }

@@ -369,7 +369,7 @@ struct ItemCursor {
 };
 
 template <int M, bool XSELF, int CODE>
-__global__ void __launch_bounds__(kRowsThreads) gemv_fused_kernel(const __grid_constant__ FusedParams p) {
+__global__ void __launch_bounds__(kRowsThreads, 4) gemv_fused_kernel(const __grid_constant__ FusedParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* stages = smem;
   uint8_t* xsm = smem + (size_t)p.stage_bytes * p.nstages;  // self-prepared activations [M][GX] records
@@ -393,7 +393,9 @@ __global__ void __launch_bounds__(kRowsThreads) gemv_fused_kernel(const __grid_c
   __syncthreads();
 
   if (warp == 0) {
-    if (lane == 0 && r_begin < r_end) {
+    // producer warp: lane r issues row r's bulk copy, lane 0 the barrier
+    // bookkeeping and the activation copies
+    if (r_begin < r_end) {
       auto issue = [&](const ItemCursor& it, int s, bool with_w, bool with_x) {
         const FSeg& sg = p.seg[it.seg];
         const int64_t off = (int64_t)it.c * sg.chunk_bytes;
@@ -401,11 +403,13 @@ __global__ void __launch_bounds__(kRowsThreads) gemv_fused_kernel(const __grid_c
         const int ng = (int)(min((int64_t)p.PPS, (int64_t)p.npieces - (int64_t)it.c * p.PPS)) * 8;
         uint8_t* slot = stages + (size_t)s * p.stage_bytes;
         if (with_w) {
-          mbar_arrive_expect_tx(&full[s], (uint32_t)(it.rows * rbytes + (XSELF ? 0 : M * ng * 80)));
-          for (int r = 0; r < (int)it.rows; ++r)
+          if (lane == 0)
+            mbar_arrive_expect_tx(&full[s], (uint32_t)(it.rows * rbytes + (XSELF ? 0 : M * ng * 80)));
+          __syncwarp();
+          for (int r = lane; r < (int)it.rows; r += 32)
             bulk_g2s(slot + r * sg.pitch, sg.w + (it.row0 + r) * sg.RB + off, rbytes, &full[s]);
         }
-        if (!XSELF && with_x) {
+        if (!XSELF && with_x && lane == 0) {
           uint8_t* xs = slot + p.R * p.max_pitch;
           for (int m = 0; m < M; ++m)
             bulk_g2s(xs + m * p.xstride, p.xg + m * p.GX + (int64_t)it.c * p.PPS * 8, ng * 80, &full[s]);
@@ -436,7 +440,7 @@ __global__ void __launch_bounds__(kRowsThreads) gemv_fused_kernel(const __grid_c
         issue(it, s, true, true);
         more = it.next(p, r_end);
       }
-    } else if (lane == 0) {
+    } else {
       grid_dep_wait();
       grid_dep_launch();
     }
