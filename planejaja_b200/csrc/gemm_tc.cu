@@ -31,6 +31,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <stdlib.h>
+
 #include <mutex>
 
 #include "nsq_common.cuh"
@@ -39,11 +41,11 @@ namespace nsq {
 
 constexpr int GEMM_BM = 128;   // W rows per CTA (UMMA M)
 constexpr int GEMM_BK = 64;    // K per stage (bf16: 128 bytes per row)
-constexpr int GEMM_STAGES = 3;     // bf16 W / x stages (64-wide K blocks)
 constexpr int GEMM_RAW_STAGES = 2; // raw GGUF byte stages (256-wide K columns)
-constexpr int GEMM_THREADS = 384;
+constexpr int GEMM_SMEM_LIMIT = 232448;  // opt-in shared memory per CTA on sm_100
+constexpr int GEMM_THREADS = 640;
 constexpr int GEMM_DQ_WARP0 = 4;  // first dequant / epilogue warp
-constexpr int GEMM_DQ_THREADS = 256;
+constexpr int GEMM_DQ_THREADS = 512;
 
 // Raw bytes of one row for one 256-weight column of K: a K-quant
 // super-block, or 8 Q4_0 / Q8_0 blocks.  Q6_K columns (210 B) start at any
@@ -53,6 +55,15 @@ template <> struct RawCol<NSQ_TYPE_Q4_K> { static constexpr int bytes = 144, pit
 template <> struct RawCol<NSQ_TYPE_Q4_0> { static constexpr int bytes = 144, pitch = 144; };
 template <> struct RawCol<NSQ_TYPE_Q8_0> { static constexpr int bytes = 272, pitch = 272; };
 template <> struct RawCol<NSQ_TYPE_Q6_K> { static constexpr int bytes = 210, pitch = 240; };
+
+// bf16 W / x stages (64-wide K blocks): as many as fit beside the raw ring
+template <int TYPE, int TOK>
+__host__ __device__ constexpr int gemm_stages() {
+  constexpr int fixed = 1024 + GEMM_RAW_STAGES * 128 * RawCol<TYPE>::pitch + 256;
+  constexpr int per = 128 * 128 + TOK * 128;
+  constexpr int n = (GEMM_SMEM_LIMIT - fixed) / per;
+  return n > 6 ? 6 : n;
+}
 
 // ---------------------------------------------------------------------------
 // tcgen05 / TMA PTX wrappers
@@ -134,16 +145,19 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Dequant of 32 weights of one row for one 64-wide K block q (0..3) of a
-// 256-weight column whose raw bytes `raw` sit in shared memory; h picks
-// which 32 of the 64.  Same formulas and roundings as dequant.cu.
+// Dequant of 16 weights of one row for one 64-wide K block q (0..3) of a
+// 256-weight column whose raw bytes `raw` sit in shared memory; qq (0..3)
+// picks which 16 of the 64 (two 16-byte chunks of the bf16 row segment,
+// chunk[0] and chunk[1]).  Same formulas and roundings as dequant.cu.
 template <int TYPE, int LAYOUT>
-__device__ __forceinline__ void dequant_col_kblock(const uint8_t* raw, int q, int h, uint32_t (&out)[16],
-                                                   int (&chunk)[4]) {
-  float v[32];
+__device__ __forceinline__ void dequant_col_kblock(const uint8_t* raw, int q, int qq, uint32_t (&out)[8],
+                                                   int (&chunk)[2]) {
+  float v[16];
   if constexpr (TYPE == NSQ_TYPE_Q4_K) {
+    // qs[32q + 8qq .. +8): low nibbles -> K 8qq.. (sub-block 2q),
+    // high nibbles -> K 32 + 8qq.. (sub-block 2q+1)
     const uint4 hdr = *reinterpret_cast<const uint4*>(raw);
-    const uint4 qv = *reinterpret_cast<const uint4*>(raw + 16 + 32 * q + 16 * h);
+    const uint2 qv = *reinterpret_cast<const uint2*>(raw + 16 + 32 * q + 8 * qq);
     const float d = h2f((uint16_t)(hdr.x & 0xFFFF)), dmin = h2f((uint16_t)(hdr.x >> 16));
     uint32_t sc[2], mn[2];
 #pragma unroll
@@ -161,76 +175,84 @@ __device__ __forceinline__ void dequant_col_kblock(const uint8_t* raw, int q, in
     }
     const float d1 = __fmul_rn(d, (float)sc[0]), m1 = __fmul_rn(dmin, (float)mn[0]);
     const float d2 = __fmul_rn(d, (float)sc[1]), m2 = __fmul_rn(dmin, (float)mn[1]);
-    const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
+    // d1*q is exact (<= 21 significant bits), so fma(d1, q, -m1) rounds
+    // once, exactly like the reference's d1*q - m1
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const uint32_t byte = (qw[i >> 2] >> (8 * (i & 3))) & 0xFF;
-      v[i] = __fsub_rn(__fmul_rn(d1, (float)(byte & 0xF)), m1);
-      v[16 + i] = __fsub_rn(__fmul_rn(d2, (float)(byte >> 4)), m2);
+    for (int w2 = 0; w2 < 2; ++w2) {
+      const uint32_t wv = w2 ? qv.y : qv.x;
+      const uint32_t lo = wv & 0x0F0F0F0Fu, hi = (wv >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        v[4 * w2 + b] = __fmaf_rn(d1, (float)((lo >> (8 * b)) & 0xFF), -m1);
+        v[8 + 4 * w2 + b] = __fmaf_rn(d2, (float)((hi >> (8 * b)) & 0xFF), -m2);
+      }
     }
-    chunk[0] = 2 * h; chunk[1] = 2 * h + 1; chunk[2] = 4 + 2 * h; chunk[3] = 5 + 2 * h;
+    chunk[0] = qq;
+    chunk[1] = 4 + qq;
   } else if constexpr (TYPE == NSQ_TYPE_Q6_K) {
     const float d = h2f((uint16_t)ld_u16(raw + 208));
     if constexpr (LAYOUT == NSQ_Q6K_NODESTOR) {
-      // elements e = 64q + 32h + l: ql[e>>1], qh[e>>2], scale byte [e>>4]
-      uint32_t ql[4], qh[2];
-      ld_words_unaligned<4>(raw + 32 * q + 16 * h, ql);
-      ld_words_unaligned<2>(raw + 128 + 16 * q + 8 * h, qh);
-      const uint32_t s01 = ld_u16(raw + 192 + 4 * q + 2 * h);
-      const float sa = __fmul_rn(d, (float)((int)(s01 & 0xFF) - 128) / 64.0f);
-      const float sb = __fmul_rn(d, (float)((int)(s01 >> 8) - 128) / 64.0f);
+      // elements e = 64q + 16qq + l: ql[e>>1], qh[e>>2], scale byte [e>>4]
+      uint32_t ql[2], qh[1];
+      ld_words_unaligned<2>(raw + 32 * q + 8 * qq, ql);
+      ld_words_unaligned<1>(raw + 128 + 16 * q + 4 * qq, qh);
+      const float sa = __fmul_rn(d, (float)((int)raw[192 + 4 * q + qq] - 128) / 64.0f);
 #pragma unroll
-      for (int t = 0; t < 8; ++t) {
+      for (int t = 0; t < 4; ++t) {
         const uint32_t l2 = (ql[t >> 1] >> (16 * (t & 1))) & 0xFFFF;  // elements 4t .. 4t+3
-        const uint32_t hb = (qh[t >> 2] >> (8 * (t & 3))) & 0xFF;
+        const uint32_t hb = (qh[0] >> (8 * t)) & 0xFF;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const uint32_t lo = (l2 >> (4 * e)) & 0xF;
           const uint32_t hi = (hb >> (2 * e)) & 3;
-          v[4 * t + e] = __fmul_rn(t < 4 ? sa : sb, (float)((int)(lo | (hi << 4)) - 32));
+          v[4 * t + e] = __fmul_rn(sa, (float)((int)(lo | (hi << 4)) - 32));
         }
       }
     } else {
-      // ggml: n = q>>1, group j = 2(q&1) + h; ql[64n + 32h + l] nibble (q&1),
-      // qh[32n + l] bits 2j, int8 scale sc[8n + l/16 + 2j]
-      const int n = q >> 1, j = 2 * (q & 1) + h, nib = q & 1;
-      uint32_t ql[8], qh[8];
-      ld_words_unaligned<8>(raw + 64 * n + 32 * h, ql);
-      ld_words_unaligned<8>(raw + 128 + 32 * n, qh);
-      const uint32_t s01 = ld_u16(raw + 192 + 8 * n + 2 * j);
-      const float sa = __fmul_rn(d, (float)(int8_t)(s01 & 0xFF));
-      const float sb = __fmul_rn(d, (float)(int8_t)(s01 >> 8));
+      // ggml: n = q>>1, group j = 2(q&1) + (qq>>1), l = 16(qq&1) + i;
+      // ql[64n + 32(j&1) + l] nibble (q&1), qh[32n + l] bits 2j, int8 scale
+      // sc[8n + (qq&1) + 2j]
+      const int n = q >> 1, j = 2 * (q & 1) + (qq >> 1), nib = q & 1, l0 = 16 * (qq & 1);
+      uint32_t ql[4], qh[4];
+      ld_words_unaligned<4>(raw + 64 * n + 32 * (j & 1) + l0, ql);
+      ld_words_unaligned<4>(raw + 128 + 32 * n + l0, qh);
+      const float sa = __fmul_rn(d, (float)(int8_t)raw[192 + 8 * n + (qq & 1) + 2 * j]);
 #pragma unroll
-      for (int l = 0; l < 32; ++l) {
-        const uint32_t lo = (ql[l >> 2] >> (8 * (l & 3) + 4 * nib)) & 0xF;
-        const uint32_t hi = (qh[l >> 2] >> (8 * (l & 3) + 2 * j)) & 3;
-        v[l] = __fmul_rn(l < 16 ? sa : sb, (float)((int)(lo | (hi << 4)) - 32));
+      for (int i = 0; i < 16; ++i) {
+        const uint32_t lo = (ql[i >> 2] >> (8 * (i & 3) + 4 * nib)) & 0xF;
+        const uint32_t hi = (qh[i >> 2] >> (8 * (i & 3) + 2 * j)) & 3;
+        v[i] = __fmul_rn(sa, (float)((int)(lo | (hi << 4)) - 32));
       }
     }
-    chunk[0] = 4 * h; chunk[1] = 4 * h + 1; chunk[2] = 4 * h + 2; chunk[3] = 4 * h + 3;
+    chunk[0] = 2 * qq;
+    chunk[1] = 2 * qq + 1;
   } else if constexpr (TYPE == NSQ_TYPE_Q4_0) {
-    const uint8_t* blk = raw + (2 * q + h) * 18;
+    // block 2q + (qq>>1); qq&1 picks the low (weights 0..15) or high
+    // (16..31) nibbles of its 16 bytes
+    const uint8_t* blk = raw + (2 * q + (qq >> 1)) * 18;
     const float d = h2f((uint16_t)ld_u16(blk));
     uint32_t qs[4];
     ld_words_unaligned<4>(blk + 2, qs);
+    const int sh = 4 * (qq & 1);
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-      const uint32_t byte = (qs[i >> 2] >> (8 * (i & 3))) & 0xFF;
-      v[i] = __fmul_rn((float)((int)(byte & 0xF) - 8), d);
-      v[16 + i] = __fmul_rn((float)((int)(byte >> 4) - 8), d);
+      const uint32_t nibv = (qs[i >> 2] >> (8 * (i & 3) + sh)) & 0xF;
+      v[i] = __fmul_rn((float)((int)nibv - 8), d);
     }
-    chunk[0] = 4 * h; chunk[1] = 4 * h + 1; chunk[2] = 4 * h + 2; chunk[3] = 4 * h + 3;
-  } else {  // Q8_0
-    const uint8_t* blk = raw + (2 * q + h) * 34;
+    chunk[0] = 2 * qq;
+    chunk[1] = 2 * qq + 1;
+  } else {  // Q8_0: block 2q + (qq>>1), bytes 16(qq&1) .. +16
+    const uint8_t* blk = raw + (2 * q + (qq >> 1)) * 34;
     const float d = h2f((uint16_t)ld_u16(blk));
-    uint32_t qs[8];
-    ld_words_unaligned<8>(blk + 2, qs);
+    uint32_t qs[4];
+    ld_words_unaligned<4>(blk + 2 + 16 * (qq & 1), qs);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __fmul_rn(d, (float)(int8_t)((qs[i >> 2] >> (8 * (i & 3))) & 0xFF));
-    chunk[0] = 4 * h; chunk[1] = 4 * h + 1; chunk[2] = 4 * h + 2; chunk[3] = 4 * h + 3;
+    for (int i = 0; i < 16; ++i) v[i] = __fmul_rn(d, (float)(int8_t)((qs[i >> 2] >> (8 * (i & 3))) & 0xFF));
+    chunk[0] = 2 * qq;
+    chunk[1] = 2 * qq + 1;
   }
 #pragma unroll
-  for (int i = 0; i < 16; ++i) out[i] = pack_bf16(v[2 * i], v[2 * i + 1]);
+  for (int i = 0; i < 8; ++i) out[i] = pack_bf16(v[2 * i], v[2 * i + 1]);
 }
 
 // ---------------------------------------------------------------------------
@@ -250,6 +272,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_tc_kernel(const __grid_c
   constexpr uint32_t RAW_STAGE = GEMM_BM * RawCol<TYPE>::pitch;
   constexpr int CB = RawCol<TYPE>::bytes;
   constexpr uint32_t IDESC = umma_idesc_bf16(GEMM_BM, TOK);
+  constexpr int GEMM_STAGES = gemm_stages<TYPE, TOK>();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* w_sm = smem;
@@ -373,11 +396,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_tc_kernel(const __grid_c
       }
     }
   } else if (warp >= GEMM_DQ_WARP0) {
-    // ---- dequant: each quarter-warp covers 8 distinct rows of one half,
-    // so its 16-byte swizzled stores hit 8 distinct bank groups
-    const int t = threadIdx.x - GEMM_DQ_WARP0 * 32;  // 0..255
-    const int h = (t >> 3) & 1;
-    const int r = (t & 7) | ((t >> 4) << 3);
+    // ---- dequant: each quarter-warp covers 8 distinct rows of one K
+    // quarter, so its 16-byte swizzled stores hit 8 distinct bank groups
+    const int t = threadIdx.x - GEMM_DQ_WARP0 * 32;  // 0..511
+    const int qq = (t >> 3) & 3;
+    const int r = (t & 7) | ((t >> 5) << 3);
     const bool row_ok = r < rows_valid;
     bool ok = true;
     for (int kb = 0; kb < KB; ++kb) {
@@ -387,16 +410,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_tc_kernel(const __grid_c
         ok = false;
         break;
       }
-      uint32_t pk[16];
-      int chunk[4];
+      uint32_t pk[8];
+      int chunk[2];
       if (row_ok) {
         const int64_t off = (n0 + r) * p.RB + (int64_t)c * CB;
         const uint8_t* raw = raw_sm + rs * RAW_STAGE + r * RawCol<TYPE>::pitch + (int)(off & 15);
-        dequant_col_kblock<TYPE, LAYOUT>(raw, q, h, pk, chunk);
+        dequant_col_kblock<TYPE, LAYOUT>(raw, q, qq, pk, chunk);
       } else {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) pk[i] = 0u;
-        chunk[0] = 4 * h; chunk[1] = 4 * h + 1; chunk[2] = 4 * h + 2; chunk[3] = 4 * h + 3;
+        for (int i = 0; i < 8; ++i) pk[i] = 0u;
+        chunk[0] = 2 * qq;
+        chunk[1] = 2 * qq + 1;
       }
       if (q == 3) {
         // this column's raw bytes are no longer read by this warp
@@ -409,7 +433,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_tc_kernel(const __grid_c
       }
       uint8_t* dst = w_sm + s * W_STAGE + r * 128;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < 2; ++i) {
         const int cc = chunk[i] ^ (r & 7);
         *reinterpret_cast<uint4*>(dst + cc * 16) = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
       }
@@ -417,14 +441,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_tc_kernel(const __grid_c
       __syncwarp();
       if (lane == 0) mbar_arrive(&full[s]);
     }
-    // ---- epilogue
+    // ---- epilogue: warp w reads TMEM lanes 32*(w%4).. (its W rows) for a
+    // quarter of the TOK accumulator columns
     if (ok && mbar_wait_bounded(accum, 0)) {
       tc_fence_after();
       const int qd = warp & 3;
-      const int half = (warp - GEMM_DQ_WARP0) >> 2;
+      const int part = (warp - GEMM_DQ_WARP0) >> 2;  // 0..3
       const int64_t n = n0 + 32 * qd + lane;
 #pragma unroll 1
-      for (int c0 = half * (TOK / 2); c0 < (half + 1) * (TOK / 2); c0 += 32) {
+      for (int c0 = part * (TOK / 4); c0 < (part + 1) * (TOK / 4); c0 += 32) {
         uint32_t v[32];
         tc_ld_32x32b_x32(tmem_d + ((uint32_t)(32 * qd) << 16) + (uint32_t)c0, v);
         if (n < p.N) {
@@ -462,9 +487,9 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 
 template <int TYPE, int TOK>
 static size_t gemm_smem_bytes() {
-  return 1024 + (size_t)GEMM_STAGES * (GEMM_BM * 128 + TOK * 128) +
-         (size_t)GEMM_RAW_STAGES * GEMM_BM * RawCol<TYPE>::pitch + (2 * GEMM_STAGES + 2 * GEMM_RAW_STAGES + 1) * 8 +
-         16;
+  constexpr int S = gemm_stages<TYPE, TOK>();
+  return 1024 + (size_t)S * (GEMM_BM * 128 + TOK * 128) + (size_t)GEMM_RAW_STAGES * GEMM_BM * RawCol<TYPE>::pitch +
+         (2 * S + 2 * GEMM_RAW_STAGES + 1) * 8 + 16;
 }
 
 template <int TYPE, int LAYOUT, int TOK>
@@ -486,7 +511,7 @@ static int launch_gemm_t(const CUtensorMap& map, const CUtensorMap& wmap, const 
 }
 
 template <int TYPE, int LAYOUT>
-static int run_gemm_t(const CUtensorMap& xmap, const GemmParams& p0, cudaStream_t st) {
+static int run_gemm_t(const CUtensorMap& xmap, const GemmParams& p0, int tok, cudaStream_t st) {
   GemmParams p = p0;
   alignas(64) CUtensorMap wmap{};
   p.wmap_ok = 0;
@@ -504,7 +529,7 @@ static int run_gemm_t(const CUtensorMap& xmap, const GemmParams& p0, cudaStream_
         p.wmap_ok = 1;
     }
   }
-  if (p.M <= 128) return launch_gemm_t<TYPE, LAYOUT, 128>(xmap, wmap, p, st);
+  if (p.M <= 128 || tok == 128) return launch_gemm_t<TYPE, LAYOUT, 128>(xmap, wmap, p, st);
   return launch_gemm_t<TYPE, LAYOUT, 256>(xmap, wmap, p, st);
 }
 
@@ -532,16 +557,19 @@ int run_gemm_bf16(const uint8_t* w, int type, int layout, const void* x, void* y
   p.K = K;
   p.RB = (K / nsq_block_weights(type)) * nsq_block_bytes(type);
   alignas(64) CUtensorMap map{};
-  const int tok = M <= 128 ? 128 : 256;
+  // tokens per CTA: 128 for short prompts, else 256 (NSQ_GEMM_TOK overrides)
+  const char* te = getenv("NSQ_GEMM_TOK");
+  int tok = M <= 128 ? 128 : 256;
+  if (te && atoi(te) == 128) tok = 128;
   int rc = encode_xmap(&map, x, M, K, tok);
   if (rc) return rc;
   switch (type) {
-    case NSQ_TYPE_Q4_0: return run_gemm_t<NSQ_TYPE_Q4_0, 0>(map, p, st);
-    case NSQ_TYPE_Q8_0: return run_gemm_t<NSQ_TYPE_Q8_0, 0>(map, p, st);
-    case NSQ_TYPE_Q4_K: return run_gemm_t<NSQ_TYPE_Q4_K, 0>(map, p, st);
+    case NSQ_TYPE_Q4_0: return run_gemm_t<NSQ_TYPE_Q4_0, 0>(map, p, tok, st);
+    case NSQ_TYPE_Q8_0: return run_gemm_t<NSQ_TYPE_Q8_0, 0>(map, p, tok, st);
+    case NSQ_TYPE_Q4_K: return run_gemm_t<NSQ_TYPE_Q4_K, 0>(map, p, tok, st);
     case NSQ_TYPE_Q6_K:
-      if (layout == NSQ_Q6K_NODESTOR) return run_gemm_t<NSQ_TYPE_Q6_K, NSQ_Q6K_NODESTOR>(map, p, st);
-      return run_gemm_t<NSQ_TYPE_Q6_K, NSQ_Q6K_GGML>(map, p, st);
+      if (layout == NSQ_Q6K_NODESTOR) return run_gemm_t<NSQ_TYPE_Q6_K, NSQ_Q6K_NODESTOR>(map, p, tok, st);
+      return run_gemm_t<NSQ_TYPE_Q6_K, NSQ_Q6K_GGML>(map, p, tok, st);
     default: return NSQ_ERR_TYPE;
   }
 }

@@ -217,9 +217,19 @@ def test_gemv_errors_on_gpu(eng):
 
 
 # ---------------------------------------------------------------- GEMM
+@pytest.fixture(params=["tok_auto", "tok128"])
+def gemm_tok(request, monkeypatch):
+    """Runs a GEMM test with the default token tile and with 128-token tiles."""
+    if request.param == "tok128":
+        monkeypatch.setenv("NSQ_GEMM_TOK", "128")
+    else:
+        monkeypatch.delenv("NSQ_GEMM_TOK", raising=False)
+    return request.param
+
+
 @pytest.mark.parametrize("tid,layout", ALL, ids=IDS)
 @pytest.mark.parametrize("m,n,k", [(128, 256, 512), (17, 200, 1024), (129, 130, 256), (300, 384, 2048)])
-def test_gemm_parity(eng, oracle, tid, layout, m, n, k):
+def test_gemm_parity(eng, oracle, gemm_tok, tid, layout, m, n, k):
     w = Q.synthetic_weights(n, k, tid, seed=300 + n, q6k_layout=layout)
     x = bf16_round(Q.synthetic_activations(m, k, seed=400 + m))
     ref = oracle.quant_matmul(w, tid, x, n, k, layout, threads=8)
