@@ -270,7 +270,8 @@ def run_gpu(args, rank, world, local_rank):
     step()
     torch.cuda.synchronize()
     graph = None
-    if world == 1 and not args.no_graph:
+    if not args.no_graph:
+        # the whole step, NCCL all-gathers included for N > 1, as one graph
         s = torch.cuda.Stream(dev)
         s.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(s):
