@@ -22,6 +22,12 @@
 // Programmatic dependent launch: the weight copies of the first stages are
 // issued before griddepcontrol.wait, so they overlap the tail of the kernel
 // that produces the activation records.
+//
+// Self-prepared activations: every CTA needs all K/32 activation records.
+// With thread-block clusters of C CTAs, each CTA quantises 1/C of the groups
+// and stores the records into the shared memory of every CTA of its cluster
+// (distributed shared memory), so the L2 serves each activation line to 1/C
+// as many CTAs; one cluster barrier publishes the records.
 #include <stdlib.h>
 
 #include "nsq_common.cuh"
@@ -279,6 +285,8 @@ struct FusedParams {
   int R, KS, PPS, npieces, nchunks;
   int xstride;          // bytes per token of per-stage activation records (workspace mode)
   int stage_bytes, nstages, max_pitch;
+  int C;                // self-prepared mode: CTAs per cluster sharing the activation quantisation
+  int64_t nrb;          // row blocks of R rows in the concatenated row space
 };
 
 // CODE >= 0: every segment has that format (one decoder compiled in);
@@ -301,8 +309,9 @@ __device__ __forceinline__ void run_piece(int code, const uint8_t* pc, const uin
 }
 
 // Quantize one group of 32 activations into an 80-byte record (same math as
-// prepare_x_kernel in gemv.cu, one thread per group).
-__device__ __forceinline__ void prepare_group(const float* __restrict__ xs, uint8_t* rec) {
+// prepare_x_kernel in gemv.cu, one thread per group), returned as 5 words of
+// 16 bytes.
+__device__ __forceinline__ void quantize_group(const float* __restrict__ xs, uint4 (&o)[5]) {
   float v[32];
   const float4* q = reinterpret_cast<const float4*>(xs);
 #pragma unroll
@@ -330,12 +339,30 @@ __device__ __forceinline__ void prepare_group(const float* __restrict__ xs, uint
     hw[w] = h;
     lw[w] = l;
   }
-  uint4* o = reinterpret_cast<uint4*>(rec);
   o[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
   o[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
   o[2] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
   o[3] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
   o[4] = make_uint4(__float_as_uint(amax / 32767.0f), (uint32_t)s0, (uint32_t)s1, 0u);
+}
+
+// Thread-block cluster helpers (distributed shared memory).
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_arrive_release() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait_acquire() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+__device__ __forceinline__ uint32_t cluster_map(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, const uint4& v) {
+  asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
 }
 
 // Walk of one CTA's work: items (segment, row block, chunk) in order.
@@ -380,7 +407,12 @@ __global__ void __launch_bounds__(kRowsThreads, 4) gemv_fused_kernel(const __gri
   __shared__ int s_fail;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int64_t r_begin = p.T * blockIdx.x / gridDim.x, r_end = p.T * (blockIdx.x + 1) / gridDim.x;
+  // rows per CTA: whole row blocks (nrb > 0; the counts differ by at most
+  // one) or an even split of the rows
+  const int64_t r_begin = p.nrb > 0 ? min(p.T, p.R * (p.nrb * blockIdx.x / gridDim.x)) : p.T * blockIdx.x / gridDim.x;
+  const int64_t r_end = p.nrb > 0 ? min(p.T, p.R * (p.nrb * (blockIdx.x + 1) / gridDim.x))
+                                  : p.T * (blockIdx.x + 1) / gridDim.x;
+  const bool clustered = XSELF && p.C > 1;
 
   if (tid == 0) {
     s_fail = 0;
@@ -391,6 +423,9 @@ __global__ void __launch_bounds__(kRowsThreads, 4) gemv_fused_kernel(const __gri
     fence_mbar_init();
   }
   __syncthreads();
+  // cluster phase 1: every CTA of the cluster has started before any writes
+  // into its shared memory
+  if (clustered) cluster_arrive_relaxed();
 
   if (warp == 0) {
     // producer warp: lane r issues row r's bulk copy, lane 0 the barrier
@@ -427,8 +462,14 @@ __global__ void __launch_bounds__(kRowsThreads, 4) gemv_fused_kernel(const __gri
         ++npre;
         more = it.next(p, r_end);
       }
+      __syncwarp();
       grid_dep_wait();
       grid_dep_launch();
+      if (clustered) {
+        cluster_wait_acquire();
+        cluster_arrive_relaxed();
+        cluster_wait_acquire();
+      }
       for (int t = 0; t < npre; ++t) issue(pre[t], t, false, true);
       for (int t = npre; more; ++t) {
         const int s = t % p.nstages;
@@ -443,17 +484,47 @@ __global__ void __launch_bounds__(kRowsThreads, 4) gemv_fused_kernel(const __gri
     } else {
       grid_dep_wait();
       grid_dep_launch();
+      if (clustered) {
+        cluster_wait_acquire();
+        cluster_arrive_relaxed();
+        cluster_wait_acquire();
+      }
     }
   } else {
     const int cw = warp - 1, ct = tid - 32;
     grid_dep_wait();
     grid_dep_launch();
     if constexpr (XSELF) {
-      for (int64_t gi = ct; gi < (int64_t)M * p.GX; gi += kRowsConsumers * 32) {
+      // the cluster's CTAs quantise disjoint ranges of the groups and write
+      // every record into each CTA of the cluster (the L2 serves each
+      // activation line to 1/C as many CTAs)
+      const int64_t ng = (int64_t)M * p.GX;
+      const int q = clustered ? (int)cluster_rank() : 0, C = clustered ? p.C : 1;
+      if (clustered) cluster_wait_acquire();
+      for (int64_t gi = ng * q / C + ct; gi < ng * (q + 1) / C; gi += kRowsConsumers * 32) {
         const int64_t m = gi / p.GX, g = gi - m * p.GX;
-        prepare_group(p.x + m * p.K + 32 * g, xsm + (m * p.GX + g) * 80);
+        uint4 o[5];
+        quantize_group(p.x + m * p.K + 32 * g, o);
+        uint8_t* rec = xsm + (m * p.GX + g) * 80;
+        if (clustered) {
+          for (int qq = 0; qq < C; ++qq) {
+            const uint32_t ra = cluster_map(rec, (uint32_t)qq);
+#pragma unroll
+            for (int i = 0; i < 5; ++i) st_cluster_v4(ra + 16 * i, o[i]);
+          }
+        } else {
+          uint4* d = reinterpret_cast<uint4*>(rec);
+#pragma unroll
+          for (int i = 0; i < 5; ++i) d[i] = o[i];
+        }
       }
-      asm volatile("bar.sync 1, %0;" ::"r"(kRowsConsumers * 32) : "memory");
+      if (clustered) {
+        // cluster phase 2: all records of the cluster have landed
+        cluster_arrive_release();
+        cluster_wait_acquire();
+      } else {
+        asm volatile("bar.sync 1, %0;" ::"r"(kRowsConsumers * 32) : "memory");
+      }
     }
     const int r = lane % p.R, ks = lane / p.R;
     const int lanes_per_piece = kRowsConsumers * p.KS;
@@ -540,8 +611,8 @@ static int piece_bytes_of(int type) {
 
 // Plans a fused launch; false if a segment's shape is not covered (K % 256,
 // Q6_K needs K % 2048, 16-byte row alignment).
-static bool plan_fused(const nsq_segment* segs, int nseg, int64_t K, int M, bool xself, int num_sms, FusedParams& p,
-                       int& blocks, size_t& smem) {
+static bool plan_fused(const nsq_segment* segs, int nseg, int64_t K, int M, bool xself, int num_sms,
+                       int max_clusters, FusedParams& p, int& blocks, size_t& smem) {
   if (nseg < 1 || nseg > NSQ_MAX_SEGMENTS || K % 256) return false;
   const int64_t npieces = K / 256;
   bool any_q6k = false;
@@ -556,11 +627,17 @@ static bool plan_fused(const nsq_segment* segs, int nseg, int64_t K, int M, bool
     if ((npieces * piece_bytes_of(t)) % 16) return false;
     T += segs[i].N;
   }
-  int R = env_int("NSQ_ROWS_R", 8);
+  // Defaults from measurement on B200 (M = 1): many rows per SM (an FFN
+  // input projection) stream best in 16-row blocks of whole 4096-wide rows;
+  // long rows (K >= 8192) gain from sharing the activation quantisation in
+  // CTA pairs and from whole row blocks per CTA.
+  const bool many_rows = T >= (int64_t)128 * num_sms;
+  const bool long_k = K >= 8192;
+  int R = env_int("NSQ_ROWS_R", many_rows ? 16 : 8);
   if (R != 4 && R != 8 && R != 16 && R != 32) R = 8;
   while (R > 4 && (T + R - 1) / R < (int64_t)num_sms) R >>= 1;
   const int KS = 32 / R;
-  int PPS = env_int("NSQ_ROWS_PPSM", 1) * kRowsConsumers * KS;
+  int PPS = env_int("NSQ_ROWS_PPSM", many_rows ? 2 : 1) * kRowsConsumers * KS;
   if (PPS < 1) PPS = kRowsConsumers * KS;
   if (any_q6k && PPS % 8) PPS = (PPS + 7) / 8 * 8;
   if (PPS > npieces) PPS = (int)npieces;
@@ -609,15 +686,33 @@ static bool plan_fused(const nsq_segment* segs, int nseg, int64_t K, int M, bool
   if (per_sm < 1) per_sm = 1;
   const int cps = env_int("NSQ_ROWS_CPS", 0);
   if (cps >= 1 && cps <= per_sm) per_sm = cps;
-  int64_t g = (int64_t)num_sms * per_sm;
+  // clusters share the activation quantisation (self-prepared mode only)
+  int C = xself ? env_int("NSQ_ROWS_C", long_k ? 2 : 1) : 1;
+  if (C != 2 && C != 4 && C != 8) C = 1;
+  // grid: as many CTAs as fit at once, then the fewest that give every CTA
+  // the same number of whole row blocks (give or take one)
   const int64_t nrb = (T + R - 1) / R;
-  if (g > nrb) g = nrb;
+  int64_t gmax = (int64_t)num_sms * per_sm;
+  if (C > 1 && max_clusters > 0 && gmax > (int64_t)max_clusters * C) gmax = (int64_t)max_clusters * C;
+  gmax = gmax / C * C;
+  if (gmax < C) return false;
+  const bool whole_blocks = env_int("NSQ_ROWS_BAL", long_k ? 1 : 0) != 0;
+  int64_t g = gmax < nrb ? gmax : nrb;
+  if (whole_blocks) {
+    const int64_t per_cta = (nrb + gmax - 1) / gmax;
+    g = (nrb + per_cta - 1) / per_cta;
+  }
+  g = (g + C - 1) / C * C;
   blocks = (int)g;
+  p.C = C;
+  p.nrb = whole_blocks ? nrb : 0;
   return true;
 }
 
+static constexpr int kNoRoom = -2;  // launch_fused: the clusters do not all fit at once
+
 template <int M, bool XSELF, int CODE>
-static cudaError_t launch_fused(const FusedParams& p, int blocks, size_t smem, cudaStream_t st) {
+static cudaError_t launch_fused(const FusedParams& p, int blocks, size_t smem, cudaStream_t st, int* max_clusters) {
   auto kern = gemv_fused_kernel<M, XSELF, CODE>;
   static size_t configured[64] = {};
   int dev = 0;
@@ -632,36 +727,66 @@ static cudaError_t launch_fused(const FusedParams& p, int blocks, size_t smem, c
   cfg.blockDim = dim3(kRowsThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = (unsigned)(XSELF ? p.C : 1);
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  const int C = XSELF ? p.C : 1;
+  cfg.numAttrs = C > 1 ? 2 : 1;
+  if (C > 1) {
+    // all clusters must be resident at once: a second wave would double the
+    // time.  The answer is cached per device, cluster size and smem size.
+    struct Fit { int dev, S; size_t smem; int n; };
+    static Fit cache[32];
+    static int ncache = 0;
+    int n = -1;
+    for (int i = 0; i < ncache; ++i)
+      if (cache[i].dev == dev && cache[i].S == C && cache[i].smem == smem) n = cache[i].n;
+    if (n < 0) {
+      cudaLaunchConfig_t q = cfg;
+      q.numAttrs = 1;
+      q.attrs = attr + 1;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &q) != cudaSuccess || n < 1) {
+        cudaGetLastError();
+        n = 0;
+      }
+      if (ncache < 32) cache[ncache++] = Fit{dev, C, smem, n};
+    }
+    if (n < 1) return cudaErrorInvalidConfiguration;
+    if (blocks > n * C) {
+      *max_clusters = n;
+      return static_cast<cudaError_t>(kNoRoom);
+    }
+  }
   return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
 template <bool XSELF, int CODE>
-static cudaError_t launch_fused_mc(int M, const FusedParams& p, int blocks, size_t smem, cudaStream_t st) {
+static cudaError_t launch_fused_mc(int M, const FusedParams& p, int blocks, size_t smem, cudaStream_t st, int* mc) {
   switch (M) {
-    case 1: return launch_fused<1, XSELF, CODE>(p, blocks, smem, st);
-    case 2: return launch_fused<2, XSELF, CODE>(p, blocks, smem, st);
-    case 3: return launch_fused<3, XSELF, CODE>(p, blocks, smem, st);
-    default: return launch_fused<4, XSELF, CODE>(p, blocks, smem, st);
+    case 1: return launch_fused<1, XSELF, CODE>(p, blocks, smem, st, mc);
+    case 2: return launch_fused<2, XSELF, CODE>(p, blocks, smem, st, mc);
+    case 3: return launch_fused<3, XSELF, CODE>(p, blocks, smem, st, mc);
+    default: return launch_fused<4, XSELF, CODE>(p, blocks, smem, st, mc);
   }
 }
 
 template <bool XSELF>
-static cudaError_t launch_fused_m(int M, const FusedParams& p, int blocks, size_t smem, cudaStream_t st) {
+static cudaError_t launch_fused_m(int M, const FusedParams& p, int blocks, size_t smem, cudaStream_t st, int* mc) {
   int code = p.seg[0].code;
   for (int i = 1; i < p.nseg; ++i)
     if (p.seg[i].code != code) code = kMixed;
   switch (code) {
-    case kQ4K: return launch_fused_mc<XSELF, kQ4K>(M, p, blocks, smem, st);
-    case kQ6KG: return launch_fused_mc<XSELF, kQ6KG>(M, p, blocks, smem, st);
-    case kQ6KN: return launch_fused_mc<XSELF, kQ6KN>(M, p, blocks, smem, st);
-    case kQ40: return launch_fused_mc<XSELF, kQ40>(M, p, blocks, smem, st);
-    case kQ80: return launch_fused_mc<XSELF, kQ80>(M, p, blocks, smem, st);
-    default: return launch_fused_mc<XSELF, kMixed>(M, p, blocks, smem, st);
+    case kQ4K: return launch_fused_mc<XSELF, kQ4K>(M, p, blocks, smem, st, mc);
+    case kQ6KG: return launch_fused_mc<XSELF, kQ6KG>(M, p, blocks, smem, st, mc);
+    case kQ6KN: return launch_fused_mc<XSELF, kQ6KN>(M, p, blocks, smem, st, mc);
+    case kQ40: return launch_fused_mc<XSELF, kQ40>(M, p, blocks, smem, st, mc);
+    case kQ80: return launch_fused_mc<XSELF, kQ80>(M, p, blocks, smem, st, mc);
+    default: return launch_fused_mc<XSELF, kMixed>(M, p, blocks, smem, st, mc);
   }
 }
 
@@ -681,13 +806,19 @@ int run_gemv_fused(const nsq_segment* segs, int nseg, const float* x, const XGro
       sl[i] = segs[i];
       sl[i].y = segs[i].y + m0 * segs[i].N;
     }
-    FusedParams p{};
-    int blocks;
-    size_t smem;
-    if (!plan_fused(sl, nseg, K, mm, xself, num_sms, p, blocks, smem)) return -1;
-    p.x = x ? x + m0 * K : nullptr;
-    p.xg = xg ? xg + m0 * (K / 32) : nullptr;
-    cudaError_t e = xself ? launch_fused_m<true>(mm, p, blocks, smem, st) : launch_fused_m<false>(mm, p, blocks, smem, st);
+    int max_clusters = 0;
+    cudaError_t e = cudaSuccess;
+    for (int attempt = 0; attempt < 2; ++attempt) {
+      FusedParams p{};
+      int blocks;
+      size_t smem;
+      if (!plan_fused(sl, nseg, K, mm, xself, num_sms, max_clusters, p, blocks, smem)) return -1;
+      p.x = x ? x + m0 * K : nullptr;
+      p.xg = xg ? xg + m0 * (K / 32) : nullptr;
+      e = xself ? launch_fused_m<true>(mm, p, blocks, smem, st, &max_clusters)
+                : launch_fused_m<false>(mm, p, blocks, smem, st, &max_clusters);
+      if (e != static_cast<cudaError_t>(kNoRoom)) break;  // else re-plan with fewer clusters
+    }
     if (e != cudaSuccess) return NSQ_ERR_CUDA;
   }
   return NSQ_OK;
