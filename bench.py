@@ -235,27 +235,60 @@ def run_gpu(args, rank, world, local_rank):
     acts = [torch.from_numpy(a).to(dev) for a in acts_h]
     outs_local = [{name: torch.empty(rows, dtype=torch.float32, device=dev) for name, (rows, _) in layers[0].items()}
                   for _ in range(L)]
-    outs_full = [{name: torch.empty(n, dtype=torch.float32, device=dev) for name, n, k, t in LAYER_SPEC}
-                 for _ in range(L)] if world > 1 else outs_local
+    p2p = world > 1 and args.exchange == "p2p"
+    exchange = None
+    if p2p:
+        # full outputs of every projection live in the exchange buffer; each
+        # GEMV stores its rows into every rank's buffer (all-gather fused)
+        from planejaja_b200.sharded import Exchange, OutputLayout, xsegments
+        layout = OutputLayout()
+        for li in range(L):
+            for name, n, k, t in LAYER_SPEC:
+                layout.add((li, name), 1, n)
+        exchange = Exchange(layout.nbytes)
+        outs_full = [{name: exchange.view(layout.offsets[(li, name)][0], (n,)) for name, n, k, t in LAYER_SPEC}
+                     for li in range(L)]
+    elif world > 1:
+        outs_full = [{name: torch.empty(n, dtype=torch.float32, device=dev) for name, n, k, t in LAYER_SPEC}
+                     for _ in range(L)]
+    else:
+        outs_full = outs_local
     # one fused launch per shared activation: q|k|v, o, gate|up, down
     GROUPS = [(0, ["q", "k", "v"]), (1, ["o"]), (2, ["gate", "up"]), (3, ["down"])]
     TYPE_OF = {name: t for name, n, k, t in LAYER_SPEC}
+    N_OF = {name: n for name, n, k, t in LAYER_SPEC}
     seg_arrays = []
+    xseg_arrays = []
     for li in range(L):
-        per = []
+        per, xper = [], []
         for a, names in GROUPS:
             arr = (_lib.Segment * len(names))()
             for i, nm in enumerate(names):
                 rows, w = layers[li][nm]
                 arr[i] = _lib.Segment(w.data_ptr(), TYPE_OF[nm], 0, rows, outs_local[li][nm].data_ptr())
             per.append((a, names, arr))
+            if p2p:
+                xper.append((a, names, xsegments([(layers[li][nm][1].data_ptr(), TYPE_OF[nm], 0, layers[li][nm][0],
+                                                   rank * layers[li][nm][0], N_OF[nm],
+                                                   layout.offsets[(li, nm)][0]) for nm in names])))
         seg_arrays.append(per)
+        xseg_arrays.append(xper)
     n_launch = 0
 
     def step():
         nonlocal n_launch
         n_launch = 0
         st = torch.cuda.current_stream(dev).cuda_stream
+        if p2p:
+            for li in range(L):
+                for a, names, arr in xseg_arrays[li]:
+                    rc = lib.nsq_gemv_multi_xchg(ctypes.cast(arr, ctypes.c_void_p), len(names), acts[a].data_ptr(),
+                                                 1, ACT_K[a], exchange.comm, None, 0, st)
+                    assert rc == 0, rc
+                    n_launch += 1
+            exchange.wait(st)  # the step ends when every rank's rows have landed here
+            n_launch += 1
+            return
         for li in range(L):
             for a, names, arr in seg_arrays[li]:
                 rc = lib.nsq_gemv_multi(ctypes.cast(arr, ctypes.c_void_p), len(names), acts[a].data_ptr(), 1,
@@ -360,7 +393,8 @@ def run_gpu(args, rank, world, local_rank):
         "data": "synthetic (N(0,0.02) weights quantized on host; N(0,1) activations)",
         "config": {"workload": f"llama3-8b Q4_K_M decode, M=1, {L} layers x 7 projections per step",
                    "layers": L, "batch": 1, "weight_bytes_per_step": wb * L,
-                   "parallelism": f"tp{world} row-sharded + NCCL all-gather" if world > 1 else "single GPU",
+                   "parallelism": (f"tp{world} row-sharded, all-gather fused into the GEMV (NVLink peer stores)"
+                                   if p2p else f"tp{world} row-sharded + NCCL all-gather") if world > 1 else "single GPU",
                    "l2": f"inputs larger than L2: {L} distinct layer copies, {wb * L / 1e9:.2f} GB per step",
                    "cuda_graph": graph is not None},
         "frac_of_nominal_8tbs": round(value / NOMINAL_HBM_GBS, 4),
@@ -438,6 +472,11 @@ def run_gpu(args, rank, world, local_rank):
     if rank == 0:
         print(json.dumps(result), flush=True)
     graph = None
+    if exchange is not None:
+        # no rank may unmap its buffer while a peer can still store into it
+        torch.cuda.synchronize()
+        barrier()
+        exchange.close()
 
 
 def main():
@@ -455,6 +494,8 @@ def main():
     ap.add_argument("--cpu-reps", type=int, default=1)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-frac", type=float, default=0.25)
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
+                    help="N > 1: all-gather fused into the GEMV (p2p) or NCCL all_gather per projection")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -171,8 +171,7 @@ int nsq_gemv_multi(const nsq_segment *segs, int nseg, const float *x, int64_t M,
  * Prefill GEMM on tcgen05 tensor cores: y[M x N] bf16 = x[M x K] bf16 . W^T,
  * weights dequantized to bf16 in shared memory, fp32 accumulation in TMEM.
  * Within 2e-2 relative error of the reference composition on the same
- * (bf16-valued) inputs.  x must be 16-byte aligned with K % 64 == 0; y must
- * be 16-byte aligned.  Same reference operator as nsq_gemv, for M > 16.
+ * (bf16-valued) inputs.  K % 256 == 0; x and y must be 16-byte aligned.  Same reference operator as nsq_gemv, for M > 16.
  */
 int nsq_gemm_bf16(const void *w, int ggml_type, int q6k_layout, const void *x_bf16, void *y_bf16,
                   int64_t M, int64_t N, int64_t K, void *stream);
@@ -186,6 +185,64 @@ int nsq_gemm_bf16(const void *w, int ggml_type, int q6k_layout, const void *x_bf
  */
 int nsq_matmul_f32(const float *a, const float *b, float *c, int64_t M, int64_t K, int64_t N,
                    void *stream);
+
+
+/*
+ * Row-sharded decode GEMV with the all-gather fused into the kernel
+ * (tensor parallelism over the GPUs of one node, one process per GPU).
+ *
+ * Each of `world` ranks holds a contiguous row slice of every weight matrix
+ * (a row slice of a GGUF tensor is a contiguous byte range).  The GEMV
+ * epilogue stores every output row straight into the exchange buffer of
+ * every rank over NVLink (peer stores through CUDA IPC mappings); the last
+ * CTA of the grid then publishes a sequence number to each rank's flag
+ * word.  The next exchange call (or nsq_comm_wait) waits, with a bounded
+ * spin, until every rank's previous exchange has landed before it reads
+ * its activations, so the full y is in place on every rank without a
+ * separate collective launch.  A wait that gives up after 2 s records
+ * NSQ_ERR_TIMEOUT in nsq_device_status and lets the kernel finish.
+ *
+ * The reference has no collectives (its "fabric" crate simulates RDMA
+ * in-process, crates/nodestor-fabric/src/rdma_sim.rs:6-17); this is the
+ * build's multi-GPU form of Transformer::forward's matmul calls
+ * (crates/nodestor-vulkan/src/transformer.rs:241-315).
+ *
+ * Setup, on every rank with its device current:
+ *   nsq_comm_create(world, rank, bytes, &comm, handle)   -> this rank's handle
+ *   (the host exchanges the world handles, e.g. an all-gather over sockets)
+ *   nsq_comm_connect(comm, handles)                      -> maps the peers
+ * Every rank must issue the same sequence of exchange calls.
+ */
+#define NSQ_MAX_RANKS 8
+
+typedef struct nsq_comm nsq_comm;
+
+size_t nsq_comm_handle_bytes(void);
+/* Allocates this rank's exchange buffer (`bytes` of outputs, zeroed) and
+ * writes its IPC handle (nsq_comm_handle_bytes() bytes) to handle_out. */
+int nsq_comm_create(int world, int rank, size_t bytes, nsq_comm **comm, void *handle_out);
+/* handles: world * nsq_comm_handle_bytes() bytes, rank order. */
+int nsq_comm_connect(nsq_comm *comm, const void *handles);
+/* Device pointer of this rank's outputs (exchange buffer offset 0). */
+void *nsq_comm_buffer(nsq_comm *comm);
+/* Enqueues a wait until every rank's latest exchange has landed here. */
+int nsq_comm_wait(nsq_comm *comm, void *stream);
+int nsq_comm_destroy(nsq_comm *comm);
+
+typedef struct nsq_xsegment {
+  const void *w;   /* this rank's rows of the GGUF tensor, 16-byte aligned */
+  int ggml_type;
+  int q6k_layout;
+  int64_t N;       /* rows held by this rank */
+  int64_t row0;    /* first row of this rank's slice in the full output */
+  int64_t n_full;  /* rows of the full output */
+  int64_t y_off;   /* byte offset of y [M x n_full] f32 in every exchange buffer */
+} nsq_xsegment;
+
+/* y[m, row0 + r] of every rank's buffer = x[m] . W_rank[r].  Same accuracy
+ * contract and workspace rule as nsq_gemv_multi; needs K % 256 == 0. */
+int nsq_gemv_multi_xchg(const nsq_xsegment *segs, int nseg, const float *x, int64_t M, int64_t K,
+                        nsq_comm *comm, void *workspace, size_t workspace_bytes, void *stream);
 
 #ifdef __cplusplus
 }

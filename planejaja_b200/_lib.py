@@ -45,6 +45,13 @@ SIGNATURES = [
     ("nsq_gemv_noalloc", _int, [_vp, _int, _int, _vp, _vp, _i64, _i64, _i64, _vp]),
     ("nsq_gemm_bf16", _int, [_vp, _int, _int, _vp, _vp, _i64, _i64, _i64, _vp]),
     ("nsq_matmul_f32", _int, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    ("nsq_comm_handle_bytes", _sz, []),
+    ("nsq_comm_create", _int, [_int, _int, _sz, ctypes.POINTER(ctypes.c_void_p), _vp]),
+    ("nsq_comm_connect", _int, [_vp, _vp]),
+    ("nsq_comm_buffer", _vp, [_vp]),
+    ("nsq_comm_wait", _int, [_vp, _vp]),
+    ("nsq_comm_destroy", _int, [_vp]),
+    ("nsq_gemv_multi_xchg", _int, [ctypes.c_void_p, _int, _vp, _i64, _i64, _vp, _vp, _sz, _vp]),
 ]
 
 
@@ -54,7 +61,15 @@ class Segment(ctypes.Structure):
                 ("N", ctypes.c_int64), ("y", ctypes.c_void_p)]
 
 
+class XSegment(ctypes.Structure):
+    """struct nsq_xsegment (include/nsq.h): one rank's rows of a row-sharded matrix."""
+    _fields_ = [("w", ctypes.c_void_p), ("ggml_type", ctypes.c_int), ("q6k_layout", ctypes.c_int),
+                ("N", ctypes.c_int64), ("row0", ctypes.c_int64), ("n_full", ctypes.c_int64),
+                ("y_off", ctypes.c_int64)]
+
+
 MAX_SEGMENTS = 4
+MAX_RANKS = 8
 NOALLOC_MAX_ELEMS = 262144  # NSQ_NOALLOC_MAX_ELEMS: largest M * K of nsq_gemv_noalloc
 
 

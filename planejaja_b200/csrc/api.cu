@@ -17,7 +17,7 @@ cudaError_t launch_prepare_x(const float* x, XGroup* xg, int64_t M, int64_t K, c
 int run_gemv(const uint8_t* w, int type, int layout, const XGroup* xg, float* y, int64_t M, int64_t N, int64_t K,
              cudaStream_t st, int num_sms);
 int run_gemv_fused(const nsq_segment* segs, int nseg, const float* x, const XGroup* xg, int64_t M, int64_t K,
-                   cudaStream_t st, int num_sms);
+                   cudaStream_t st, int num_sms, const XchgDesc* xd = nullptr);
 bool fused_covers(const nsq_segment* segs, int nseg, int64_t K);
 bool fused_self_prepare_fits(int64_t M, int64_t K);
 bool gemv_force_general();
@@ -25,6 +25,9 @@ int run_gemm_bf16(const uint8_t* w, int type, int layout, const void* x, void* y
                   cudaStream_t st, int num_sms);
 cudaError_t launch_matmul_f32(const float* a, const float* b, float* c, int64_t M, int64_t K, int64_t N,
                               cudaStream_t st);
+bool comm_desc(const nsq_comm* c, XchgDesc& d);
+size_t comm_bytes(const nsq_comm* c);
+cudaError_t comm_launch_wait(const nsq_comm* c, cudaStream_t st);
 
 struct DevInfo {
   int num_sms = 0;
@@ -227,6 +230,52 @@ int nsq_gemv_multi(const nsq_segment* segs, int nseg, const float* x, int64_t M,
     if (rc) return rc;
   }
   return NSQ_OK;
+}
+
+int nsq_gemv_multi_xchg(const nsq_xsegment* segs, int nseg, const float* x, int64_t M, int64_t K, nsq_comm* comm,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  if (!segs || !comm) return NSQ_ERR_NULL;
+  if (nseg < 1 || nseg > NSQ_MAX_SEGMENTS) return NSQ_ERR_SHAPE;
+  if (M < 1 || M > NSQ_GEMV_MAX_M || K % 256) return NSQ_ERR_SHAPE;
+  nsq::XchgDesc xd;
+  if (!nsq::comm_desc(comm, xd)) return NSQ_ERR_SHAPE;
+  const int64_t cap = (int64_t)nsq::comm_bytes(comm);
+  nsq_segment sl[NSQ_MAX_SEGMENTS];
+  int rc;
+  for (int i = 0; i < nseg; ++i) {
+    const nsq_xsegment& g = segs[i];
+    if ((rc = check_weights(g.w, g.ggml_type, g.q6k_layout, K))) return rc;
+    if (g.N < 1 || g.row0 < 0 || g.n_full < g.row0 + g.N) return NSQ_ERR_SHAPE;
+    if (g.y_off < 0 || (g.y_off & 3)) return NSQ_ERR_ALIGN;
+    if (g.y_off + M * g.n_full * 4 > cap) return NSQ_ERR_SHAPE;
+    sl[i] = nsq_segment{g.w, g.ggml_type, g.q6k_layout, g.N, nullptr};
+    xd.row0[i] = g.row0;
+    xd.nfull[i] = g.n_full;
+    xd.off[i] = g.y_off;
+  }
+  if (!x) return NSQ_ERR_NULL;
+  if (reinterpret_cast<uintptr_t>(x) & 3) return NSQ_ERR_ALIGN;
+  if (!fused_covers(sl, nseg, K)) return NSQ_ERR_SHAPE;
+  const bool self = fused_self_prepare_fits(M, K) && !(reinterpret_cast<uintptr_t>(x) & 15);
+  if (!self) {
+    if (!workspace) return NSQ_ERR_WORKSPACE;
+    if (reinterpret_cast<uintptr_t>(workspace) & 15) return NSQ_ERR_ALIGN;
+    if (workspace_bytes < nsq_gemv_workspace_size(M, K)) return NSQ_ERR_WORKSPACE;
+  }
+  DevInfo di;
+  if ((rc = check_device(di))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // every rank's previous exchange lands here before x is read: inside the
+  // GEMV's prologue, or before the kernel that quantises x into the workspace
+  if (!self) {
+    xd.wait = false;
+    if (comm_launch_wait(comm, st) != cudaSuccess ||
+        launch_prepare_x(x, static_cast<XGroup*>(workspace), M, K, st, di.num_sms) != cudaSuccess)
+      return NSQ_ERR_CUDA;
+  }
+  rc = run_gemv_fused(sl, nseg, self ? x : nullptr, self ? nullptr : static_cast<const XGroup*>(workspace), M, K, st,
+                      di.num_sms, &xd);
+  return rc == -1 ? NSQ_ERR_SHAPE : rc;
 }
 
 int nsq_gemm_bf16(const void* w, int ggml_type, int q6k_layout, const void* x_bf16, void* y_bf16, int64_t M,

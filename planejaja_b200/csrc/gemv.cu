@@ -541,7 +541,7 @@ static int run_gemv_t(const uint8_t* w, const XGroup* xg, float* y, int64_t M, i
 }
 
 int run_gemv_fused(const nsq_segment* segs, int nseg, const float* x, const XGroup* xg, int64_t M, int64_t K,
-                   cudaStream_t st, int num_sms);
+                   cudaStream_t st, int num_sms, const XchgDesc* xd = nullptr);
 
 bool gemv_force_general() {
   // NSQ_GEMV_GENERAL=1 forces the general kernel below (the parity tests use

@@ -287,6 +287,14 @@ struct FusedParams {
   int stage_bytes, nstages, max_pitch;
   int C;                // self-prepared mode: CTAs per cluster sharing the activation quantisation
   int64_t nrb;          // row blocks of R rows in the concatenated row space
+  // Row-sharded exchange (P > 1): every output row is stored into the
+  // exchange buffer of each of the P ranks.  Segment s writes y[M x xnfull]
+  // f32 at byte offset kXchgCtlBytes + xoff[s] of every buffer, this rank's
+  // rows starting at xrow0[s].  xwait: first wait until every rank's
+  // previous exchange has landed here.
+  int P, rank, xwait;
+  uint8_t* xbuf[NSQ_MAX_RANKS];
+  int64_t xrow0[NSQ_MAX_SEGMENTS], xnfull[NSQ_MAX_SEGMENTS], xoff[NSQ_MAX_SEGMENTS];
 };
 
 // CODE >= 0: every segment has that format (one decoder compiled in);
@@ -494,6 +502,20 @@ __global__ void __launch_bounds__(kRowsThreads, 4) gemv_fused_kernel(const __gri
     const int cw = warp - 1, ct = tid - 32;
     grid_dep_wait();
     grid_dep_launch();
+    if (p.P > 1 && p.xwait) {
+      // every rank's previous exchange has landed here before the
+      // activations (in a transformer, that exchange's output) are read
+      if (ct == 0) {
+        const uint32_t* ctl = reinterpret_cast<const uint32_t*>(p.xbuf[p.rank]);
+        const uint32_t want = ld_acquire_sys(ctl + kXchgSeq);
+        for (int r = 0; r < p.P; ++r)
+          if (r != p.rank && !wait_geq_bounded(ctl + r, want)) {
+            s_fail = 1;
+            break;
+          }
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(kRowsConsumers * 32) : "memory");
+    }
     if constexpr (XSELF) {
       // the cluster's CTAs quantise disjoint ranges of the groups and write
       // every record into each CTA of the cluster (the L2 serves each
@@ -570,7 +592,13 @@ __global__ void __launch_bounds__(kRowsThreads, 4) gemv_fused_kernel(const __gri
             float v = 0.f;
 #pragma unroll
             for (int w = 0; w < kRowsConsumers; ++w) v += rd[(w * 32 + rr) * M + m];
-            sg.y[(int64_t)m * sg.N + it.row0 + rr] = v;
+            if (p.P > 1) {
+              const int64_t idx = (int64_t)m * p.xnfull[it.seg] + p.xrow0[it.seg] + it.row0 + rr;
+              for (int pr = 0; pr < p.P; ++pr)
+                reinterpret_cast<float*>(p.xbuf[pr] + kXchgCtlBytes + p.xoff[it.seg])[idx] = v;
+            } else {
+              sg.y[(int64_t)m * sg.N + it.row0 + rr] = v;
+            }
           }
           par ^= 1;
         }
@@ -579,6 +607,20 @@ __global__ void __launch_bounds__(kRowsThreads, 4) gemv_fused_kernel(const __gri
     }
   }
   __syncthreads();
+  if (p.P > 1 && tid == 0) {
+    // Publish: the fence orders this CTA's peer stores before its count;
+    // the grid's last CTA advances the exchange count and writes it to this
+    // rank's flag word in every buffer with release stores at system scope.
+    fence_acq_rel_gpu();
+    uint32_t* ctl = reinterpret_cast<uint32_t*>(p.xbuf[p.rank]);
+    if (atomicAdd(ctl + kXchgDone, 1u) == gridDim.x - 1) {
+      fence_acq_rel_gpu();  // acquire side: every CTA's stores precede the flags
+      ctl[kXchgDone] = 0;
+      const uint32_t seq = ctl[kXchgSeq] + 1;
+      ctl[kXchgSeq] = seq;
+      for (int pr = 0; pr < p.P; ++pr) st_release_sys(reinterpret_cast<uint32_t*>(p.xbuf[pr]) + p.rank, seq);
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -797,7 +839,7 @@ bool fused_self_prepare_fits(int64_t M, int64_t K) { return M <= 4 && M * (K / 3
 // (requires fused_self_prepare_fits); otherwise xg holds prepared records.
 // Returns NSQ_OK / an error, or -1 if a shape is not covered.
 int run_gemv_fused(const nsq_segment* segs, int nseg, const float* x, const XGroup* xg, int64_t M, int64_t K,
-                   cudaStream_t st, int num_sms) {
+                   cudaStream_t st, int num_sms, const XchgDesc* xd) {
   const bool xself = (xg == nullptr);
   for (int64_t m0 = 0; m0 < M; m0 += 4) {
     const int mm = (int)((M - m0) < 4 ? (M - m0) : 4);
@@ -815,6 +857,18 @@ int run_gemv_fused(const nsq_segment* segs, int nseg, const float* x, const XGro
       if (!plan_fused(sl, nseg, K, mm, xself, num_sms, max_clusters, p, blocks, smem)) return -1;
       p.x = x ? x + m0 * K : nullptr;
       p.xg = xg ? xg + m0 * (K / 32) : nullptr;
+      p.P = 1;
+      if (xd && xd->P > 1) {
+        p.P = xd->P;
+        p.rank = xd->rank;
+        p.xwait = xd->wait && m0 == 0;
+        for (int r = 0; r < xd->P; ++r) p.xbuf[r] = xd->buf[r];
+        for (int i = 0; i < nseg; ++i) {
+          p.xrow0[i] = xd->row0[i];
+          p.xnfull[i] = xd->nfull[i];
+          p.xoff[i] = xd->off[i] + m0 * xd->nfull[i] * 4;
+        }
+      }
       e = xself ? launch_fused_m<true>(mm, p, blocks, smem, st, &max_clusters)
                 : launch_fused_m<false>(mm, p, blocks, smem, st, &max_clusters);
       if (e != static_cast<cudaError_t>(kNoRoom)) break;  // else re-plan with fewer clusters

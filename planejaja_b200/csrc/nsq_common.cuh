@@ -179,4 +179,50 @@ struct __align__(16) XGroup {
 };
 static_assert(sizeof(XGroup) == 80, "XGroup must be 80 bytes");
 
+
+// ---------------------------------------------------------------------------
+// Cross-GPU exchange (peer memory through CUDA IPC mappings).  The first
+// kXchgCtlBytes of every exchange buffer hold the control words: flag[r]
+// (written by rank r over NVLink: the sequence number of r's latest
+// exchange), then this rank's own exchange count and CTA counter.
+constexpr int kXchgCtlBytes = 256;
+constexpr int kXchgSeq = 16;   // u32 index of the local exchange count
+constexpr int kXchgDone = 32;  // u32 index of the local finished-CTA counter
+
+// Host-side description of one exchange launch (filled from an nsq_comm).
+struct XchgDesc {
+  int P = 1, rank = 0;
+  bool wait = true;  // the GEMV waits for the previous exchange itself
+  uint8_t* buf[NSQ_MAX_RANKS] = {};  // exchange buffer of each rank, mapped here
+  int64_t row0[NSQ_MAX_SEGMENTS] = {}, nfull[NSQ_MAX_SEGMENTS] = {}, off[NSQ_MAX_SEGMENTS] = {};
+};
+
+// Release/acquire fence at GPU scope.  The CTAs of an exchange grid order
+// their stores (peer stores included) before a counter with it; only the
+// grid's last CTA talks to other GPUs, through release stores at system
+// scope, and happens-before is transitive across the two scopes.
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Waits until *p - want >= 0 (wrapping); false (and NSQ_ERR_TIMEOUT) after
+// kWaitLimitNs.
+__device__ __forceinline__ bool wait_geq_bounded(const uint32_t* p, uint32_t want) {
+  if ((int32_t)(ld_acquire_sys(p) - want) >= 0) return true;
+  const uint64_t t0 = globaltimer();
+  for (;;) {
+    __nanosleep(128);
+    if ((int32_t)(ld_acquire_sys(p) - want) >= 0) return true;
+    if (globaltimer() - t0 > kWaitLimitNs) {
+      report_status(NSQ_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
 }  // namespace nsq

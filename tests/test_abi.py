@@ -84,6 +84,26 @@ def test_host_side_argument_errors(lib):
     assert lib.nsq_matmul_f32(al, al, al, 0, 2, 2, None) == _lib.ERR_SHAPE
 
 
+def test_exchange_argument_errors(lib):
+    assert lib.nsq_comm_handle_bytes() == 64
+    comm = ctypes.c_void_p()
+    h = ctypes.create_string_buffer(64)
+    assert lib.nsq_comm_create(0, 0, 1024, ctypes.byref(comm), h) == _lib.ERR_SHAPE
+    assert lib.nsq_comm_create(9, 0, 1024, ctypes.byref(comm), h) == _lib.ERR_SHAPE
+    assert lib.nsq_comm_create(2, 2, 1024, ctypes.byref(comm), h) == _lib.ERR_SHAPE
+    assert lib.nsq_comm_create(2, 0, 0, ctypes.byref(comm), h) == _lib.ERR_SHAPE
+    assert lib.nsq_comm_create(2, 0, 1024, None, h) == _lib.ERR_NULL
+    assert lib.nsq_comm_create(2, 0, 1024, ctypes.byref(comm), None) == _lib.ERR_NULL
+    assert lib.nsq_comm_connect(None, h) == _lib.ERR_NULL
+    assert lib.nsq_comm_wait(None, None) == _lib.ERR_NULL
+    assert lib.nsq_comm_destroy(None) == _lib.ERR_NULL
+    assert not lib.nsq_comm_buffer(None)
+    xs = (_lib.XSegment * 1)(_lib.XSegment(0x10000, 12, 0, 16, 0, 32, 0))
+    assert lib.nsq_gemv_multi_xchg(ctypes.cast(xs, ctypes.c_void_p), 1, ctypes.c_void_p(0x10000), 1, 256, None,
+                                   None, 0, None) == _lib.ERR_NULL
+    assert lib.nsq_gemv_multi_xchg(None, 1, ctypes.c_void_p(0x10000), 1, 256, None, None, 0, None) == _lib.ERR_NULL
+
+
 def test_engine_fails_loudly_without_gpu():
     import torch
     if torch.cuda.is_available():
