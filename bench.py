@@ -13,10 +13,16 @@ Per layer, one fused GEMV launch per shared activation: q|k|v (attention
 input), o, gate|up (FFN input), down -- 4 kernels, activations quantized on
 chip.  A step is captured once as a CUDA graph and replayed.
 
-With --gpus N > 1 (torchrun, one process per GPU, NCCL): every projection is
+With --gpus N > 1 (torchrun, one process per GPU): every projection is
 row-sharded across the ranks (each rank holds N_out / N rows of each matrix)
-and each GEMV is followed by an NCCL all-gather of the output slices, the
-exchange a tensor-parallel decode needs: strong scaling, total work fixed.
+and each GEMV stores its output rows into every rank's output buffer over
+NVLink (the all-gather a tensor-parallel decode needs, fused into the GEMV;
+nsq_gemv_multi_xchg), strong scaling, total work fixed.  --exchange nccl
+runs the GEMV followed by an NCCL all_gather per projection instead.
+
+--workload l2-70b-ffn --tokens {1,16}: the Llama-2-70B FFN (gate|up [28672 x 8192]
+Q4_K, down [8192 x 28672] Q4_K; 8 layer copies, 3.17 GB), the row-sharded
+configuration measured at 1/2/4/8 GPUs.
 
 metric  : decode GEMV HBM GB/s = (weight bytes + fp32 activations + fp32
           outputs) of the whole step / step time (max over ranks), all ranks.
@@ -52,18 +58,51 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 HIDDEN, KV, FFN = 4096, 1024, 14336
-LAYER_SPEC = [  # (name, N_out, K, ggml_type)
-    ("q", HIDDEN, HIDDEN, 12), ("k", KV, HIDDEN, 12), ("v", KV, HIDDEN, 14), ("o", HIDDEN, HIDDEN, 12),
-    ("gate", FFN, HIDDEN, 12), ("up", FFN, HIDDEN, 12), ("down", HIDDEN, FFN, 14)]
-# which prepared activation feeds each projection
-ACT_OF = {"q": 0, "k": 0, "v": 0, "o": 1, "gate": 2, "up": 2, "down": 3}
-ACT_K = [HIDDEN, HIDDEN, HIDDEN, FFN]
+# Workloads: projections (name, N_out, K, ggml_type) of one layer, which
+# activation feeds each, the fused launches (activation index, names).
+WORKLOADS = {
+    "l3-8b": {
+        "spec": [("q", HIDDEN, HIDDEN, 12), ("k", KV, HIDDEN, 12), ("v", KV, HIDDEN, 14), ("o", HIDDEN, HIDDEN, 12),
+                 ("gate", FFN, HIDDEN, 12), ("up", FFN, HIDDEN, 12), ("down", HIDDEN, FFN, 14)],
+        "act_of": {"q": 0, "k": 0, "v": 0, "o": 1, "gate": 2, "up": 2, "down": 3},
+        "act_k": [HIDDEN, HIDDEN, HIDDEN, FFN],
+        "groups": [(0, ["q", "k", "v"]), (1, ["o"]), (2, ["gate", "up"]), (3, ["down"])],
+        "layers": 32,
+        "metric": "decode GEMV HBM GB/s (Llama-3-8B Q4_K_M, M={m})",
+        "desc": "llama3-8b Q4_K_M decode, M={m}, {layers} layers x 7 projections per step",
+    },
+    # Llama-2-70B FFN, Q4_K (gate/up [28672 x 8192], down [8192 x 28672])
+    "l2-70b-ffn": {
+        "spec": [("gate", 28672, 8192, 12), ("up", 28672, 8192, 12), ("down", 8192, 28672, 12)],
+        "act_of": {"gate": 0, "up": 0, "down": 1},
+        "act_k": [8192, 28672],
+        "groups": [(0, ["gate", "up"]), (1, ["down"])],
+        "layers": 8,
+        "metric": "decode GEMV HBM GB/s (Llama-2-70B FFN Q4_K, M={m})",
+        "desc": "llama2-70b FFN Q4_K decode, M={m}, {layers} layers x 3 projections per step",
+    },
+}
+LAYER_SPEC = WORKLOADS["l3-8b"]["spec"]
+ACT_OF = WORKLOADS["l3-8b"]["act_of"]
+ACT_K = WORKLOADS["l3-8b"]["act_k"]
+GROUPS = WORKLOADS["l3-8b"]["groups"]
+WORKLOAD = "l3-8b"
+M_TOK = 1
 SEED_W, SEED_X = 1000, 2000
 NOMINAL_HBM_GBS = 8000.0
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
 METRIC = "decode GEMV HBM GB/s (Llama-3-8B Q4_K_M, M=1)"
 UNIT = "GB/s"
+
+
+def select_workload(name: str, m: int) -> None:
+    """Rebinds the module-level workload description (before any leg runs)."""
+    global LAYER_SPEC, ACT_OF, ACT_K, GROUPS, WORKLOAD, M_TOK, METRIC
+    w = WORKLOADS[name]
+    LAYER_SPEC, ACT_OF, ACT_K, GROUPS = w["spec"], w["act_of"], w["act_k"], w["groups"]
+    WORKLOAD, M_TOK = name, m
+    METRIC = w["metric"].format(m=m)
 
 
 def peaks():
@@ -77,8 +116,8 @@ def peaks():
 def layer_bytes_total():
     from planejaja_b200.formats import fmt
     w = sum(fmt(t).tensor_bytes(n, k) for _, n, k, t in LAYER_SPEC)
-    x = sum(k * 4 for _, n, k, t in LAYER_SPEC)
-    y = sum(n * 4 for _, n, k, t in LAYER_SPEC)
+    x = sum(M_TOK * k * 4 for _, n, k, t in LAYER_SPEC)
+    y = sum(M_TOK * n * 4 for _, n, k, t in LAYER_SPEC)
     return w, x, y
 
 
@@ -91,7 +130,7 @@ def host_layer():
 
 def host_acts():
     from planejaja_b200 import quantize as Q
-    return [Q.synthetic_activations(1, k, seed=SEED_X + i)[0] for i, k in enumerate(ACT_K)]
+    return [Q.synthetic_activations(M_TOK, k, seed=SEED_X + i).reshape(-1) for i, k in enumerate(ACT_K)]
 
 
 class ClockSampler:
@@ -163,7 +202,8 @@ def cpu_leg(layer, acts, rows_frac: float = 1.0, reps: int = 1, threads: int = 0
         nr = max(1, int(n * rows_frac))
         jobs.append((layer[name][: nr * rb], t, acts[ACT_OF[name]], nr, k))
     nbytes = sum(j[0].nbytes + j[4] * 4 + j[3] * 4 for j in jobs)
-    O.quant_matmul(jobs[0][0][: fmt(12).row_bytes(HIDDEN)], 12, acts[0], 1, HIDDEN, threads=th)  # warm
+    w0, t0_, x0, _, k0 = jobs[0]
+    O.quant_matmul(w0[: fmt(t0_).row_bytes(k0)], t0_, x0, 1, k0, threads=th)  # warm
     t0 = time.perf_counter()
     done = 0
     while done < reps or time.perf_counter() - t0 < min_seconds:
@@ -193,9 +233,10 @@ def run_reference(args, rank, world):
         "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(1e3 * secs / max(1, args.steps), 3), "higher_is_better": True,
         "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "llama3-8b Q4_K_M layer decode, M=1 (q,k,o,gate,up Q4_K; v,down Q6_K)",
-                   "sample": f"{args.ref_frac:.4f} of the rows of each of the 7 matrices of one layer per step",
-                   "layers_per_step": 1, "batch": 1},
+        "config": {"workload": WORKLOADS[WORKLOAD]["desc"].format(m=M_TOK, layers=1),
+                   "sample": f"{args.ref_frac:.4f} of the rows of each of the {len(LAYER_SPEC)} matrices of one "
+                             f"layer per step",
+                   "layers_per_step": 1, "batch": M_TOK},
         "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": th, "kind": "port",
                          "sample": f"{args.ref_frac:.4f} of one layer's rows per step "
                                    f"({(w * args.ref_frac) / 1e6:.1f} MB of weights)"},
@@ -233,8 +274,12 @@ def run_gpu(args, rank, world, local_rank):
     for li in range(L):
         layers.append({name: (rows, buf if li == 0 else buf.clone()) for name, (rows, buf) in shards.items()})
     acts = [torch.from_numpy(a).to(dev) for a in acts_h]
-    outs_local = [{name: torch.empty(rows, dtype=torch.float32, device=dev) for name, (rows, _) in layers[0].items()}
-                  for _ in range(L)]
+    M = M_TOK
+    outs_local = [{name: torch.empty(M * rows, dtype=torch.float32, device=dev)
+                   for name, (rows, _) in layers[0].items()} for _ in range(L)]
+    # scratch for prepared activations when they do not fit on chip (M > 4 or long rows)
+    ws = eng.workspace(lib.nsq_gemv_workspace_size(M, max(ACT_K)))
+    ws_ptr, ws_n = ws.data_ptr(), ws.numel()
     p2p = world > 1 and args.exchange == "p2p"
     exchange = None
     if p2p:
@@ -244,17 +289,16 @@ def run_gpu(args, rank, world, local_rank):
         layout = OutputLayout()
         for li in range(L):
             for name, n, k, t in LAYER_SPEC:
-                layout.add((li, name), 1, n)
+                layout.add((li, name), M, n)
         exchange = Exchange(layout.nbytes)
-        outs_full = [{name: exchange.view(layout.offsets[(li, name)][0], (n,)) for name, n, k, t in LAYER_SPEC}
+        outs_full = [{name: exchange.view(layout.offsets[(li, name)][0], (M * n,)) for name, n, k, t in LAYER_SPEC}
                      for li in range(L)]
     elif world > 1:
-        outs_full = [{name: torch.empty(n, dtype=torch.float32, device=dev) for name, n, k, t in LAYER_SPEC}
+        outs_full = [{name: torch.empty(M * n, dtype=torch.float32, device=dev) for name, n, k, t in LAYER_SPEC}
                      for _ in range(L)]
     else:
         outs_full = outs_local
-    # one fused launch per shared activation: q|k|v, o, gate|up, down
-    GROUPS = [(0, ["q", "k", "v"]), (1, ["o"]), (2, ["gate", "up"]), (3, ["down"])]
+    # one fused launch per shared activation (q|k|v, o, gate|up, down for Llama-3-8B)
     TYPE_OF = {name: t for name, n, k, t in LAYER_SPEC}
     N_OF = {name: n for name, n, k, t in LAYER_SPEC}
     seg_arrays = []
@@ -283,7 +327,7 @@ def run_gpu(args, rank, world, local_rank):
             for li in range(L):
                 for a, names, arr in xseg_arrays[li]:
                     rc = lib.nsq_gemv_multi_xchg(ctypes.cast(arr, ctypes.c_void_p), len(names), acts[a].data_ptr(),
-                                                 1, ACT_K[a], exchange.comm, None, 0, st)
+                                                 M, ACT_K[a], exchange.comm, ws_ptr, ws_n, st)
                     assert rc == 0, rc
                     n_launch += 1
             exchange.wait(st)  # the step ends when every rank's rows have landed here
@@ -291,8 +335,8 @@ def run_gpu(args, rank, world, local_rank):
             return
         for li in range(L):
             for a, names, arr in seg_arrays[li]:
-                rc = lib.nsq_gemv_multi(ctypes.cast(arr, ctypes.c_void_p), len(names), acts[a].data_ptr(), 1,
-                                        ACT_K[a], None, 0, st)
+                rc = lib.nsq_gemv_multi(ctypes.cast(arr, ctypes.c_void_p), len(names), acts[a].data_ptr(), M,
+                                        ACT_K[a], ws_ptr, ws_n, st)
                 assert rc == 0, rc
                 n_launch += 1
                 if world > 1:
@@ -355,10 +399,10 @@ def run_gpu(args, rank, world, local_rank):
 
     # ---- e2e: host buffers through the C-ABI calls, copies inside the timed region
     acts_pin = [torch.from_numpy(a).pin_memory() for a in acts_h]
-    outs_pin = [{name: torch.empty(n, dtype=torch.float32).pin_memory() for name, n, k, t in LAYER_SPEC}
+    outs_pin = [{name: torch.empty(M * n, dtype=torch.float32).pin_memory() for name, n, k, t in LAYER_SPEC}
                 for _ in range(L)]
     h2d = sum(a.numel() * 4 for a in acts_pin) * L
-    d2h = sum(n * 4 for _, n, k, t in LAYER_SPEC) * L
+    d2h = sum(M * n * 4 for _, n, k, t in LAYER_SPEC) * L
 
     def e2e_step():
         for li in range(L):
@@ -391,7 +435,7 @@ def run_gpu(args, rank, world, local_rank):
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
         "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "int8x2-dp4a/f32",
         "data": "synthetic (N(0,0.02) weights quantized on host; N(0,1) activations)",
-        "config": {"workload": f"llama3-8b Q4_K_M decode, M=1, {L} layers x 7 projections per step",
+        "config": {"workload": WORKLOADS[WORKLOAD]["desc"].format(m=M, layers=L),
                    "layers": L, "batch": 1, "weight_bytes_per_step": wb * L,
                    "parallelism": (f"tp{world} row-sharded, all-gather fused into the GEMV (NVLink peer stores)"
                                    if p2p else f"tp{world} row-sharded + NCCL all-gather") if world > 1 else "single GPU",
@@ -408,17 +452,21 @@ def run_gpu(args, rank, world, local_rank):
     # projection, 2 x [14336 x 4096]) over the layer copies
     if not args.skip_roofline:
         rows, _ = layers[0]["gate"]
-        gbytes = 2 * fmt(12).tensor_bytes(rows, HIDDEN) + HIDDEN * 4 + 2 * rows * 4
+        gi = [i for i, (a, names) in enumerate(GROUPS) if "gate" in names][0]
+        ga = GROUPS[gi][0]
+        KG = ACT_K[ga]
+        gbytes = 2 * fmt(12).tensor_bytes(rows, KG) + M * KG * 4 + 2 * M * rows * 4
         st = torch.cuda.current_stream(dev).cuda_stream
-        gu = [seg_arrays[li][2][2] for li in range(L)]
+        gu = [seg_arrays[li][gi][2] for li in range(L)]
         reps = max(4, 256 // L) * L
         for i in range(L):
-            lib.nsq_gemv_multi(ctypes.cast(gu[i], ctypes.c_void_p), 2, acts[2].data_ptr(), 1, HIDDEN, None, 0, st)
+            lib.nsq_gemv_multi(ctypes.cast(gu[i], ctypes.c_void_p), 2, acts[ga].data_ptr(), M, KG, ws_ptr, ws_n, st)
         torch.cuda.synchronize()
         k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         k0.record()
         for i in range(reps):
-            lib.nsq_gemv_multi(ctypes.cast(gu[i % L], ctypes.c_void_p), 2, acts[2].data_ptr(), 1, HIDDEN, None, 0, st)
+            lib.nsq_gemv_multi(ctypes.cast(gu[i % L], ctypes.c_void_p), 2, acts[ga].data_ptr(), M, KG, ws_ptr, ws_n,
+                               st)
         k1.record()
         torch.cuda.synchronize()
         kms = k0.elapsed_time(k1) / reps
@@ -426,36 +474,37 @@ def run_gpu(args, rank, world, local_rank):
         traffic = None
         tp = os.path.join(ROOT, "profiles", "traffic.json")
         if os.path.exists(tp):
-            traffic = json.load(open(tp)).get("gemv_fused_q4k_m1_gate_up")
+            key = "gemv_fused_q4k_m1_gate_up" if WORKLOAD == "l3-8b" and M == 1 and world == 1 else None
+            traffic = json.load(open(tp)).get(key) if key else None
         result["roofline"] = {"bound": "hbm",
-                              "kernel": "gemv_fused_kernel<M=1,Q4_K> gate|up 2 x [14336x4096] (FFN input projection)",
+                              "kernel": f"gemv_fused_kernel<M={M},Q4_K> gate|up 2 x [{rows}x{KG}] (FFN input projection)",
                               "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                               "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind,
                               "frac_of_nominal_8tbs": round(achieved / NOMINAL_HBM_GBS, 4),
                               "bytes_per_launch": gbytes, "us_per_launch": round(kms * 1e3, 3),
                               "traffic": traffic}
 
-        # ---- prefill GEMM (tcgen05), Q4_K [14336 x 4096] at M = 512
+        # ---- prefill GEMM (tcgen05) on the gate matrix (Q4_K [14336 x 4096] for Llama-3-8B) at M = 512
         import torch as T
         pm = args.prefill_m
         wq = layers[0]["gate"][1]
-        xp = T.randn(pm, HIDDEN, device=dev).to(T.bfloat16)
+        xp = T.randn(pm, KG, device=dev).to(T.bfloat16)
         yp = T.empty(pm, rows, dtype=T.bfloat16, device=dev)
         for _ in range(3):
-            lib.nsq_gemm_bf16(wq.data_ptr(), 12, 0, xp.data_ptr(), yp.data_ptr(), pm, rows, HIDDEN, st)
+            lib.nsq_gemm_bf16(wq.data_ptr(), 12, 0, xp.data_ptr(), yp.data_ptr(), pm, rows, KG, st)
         torch.cuda.synchronize()
         p0, p1 = T.cuda.Event(enable_timing=True), T.cuda.Event(enable_timing=True)
         preps = 20
         p0.record()
         for i in range(preps):
             lib.nsq_gemm_bf16(layers[i % L]["gate"][1].data_ptr(), 12, 0, xp.data_ptr(), yp.data_ptr(), pm, rows,
-                              HIDDEN, st)
+                              KG, st)
         p1.record()
         torch.cuda.synchronize()
         pms = p0.elapsed_time(p1) / preps
-        tflops = 2.0 * pm * rows * HIDDEN / (pms * 1e-3) / 1e12
+        tflops = 2.0 * pm * rows * KG / (pms * 1e-3) / 1e12
         result["prefill"] = {"kernel": "gemm_tc_kernel<Q4_K> (tcgen05, bf16, fp32 TMEM accumulate)",
-                             "shape": f"M={pm} N={rows} K={HIDDEN}", "tflops": round(tflops, 1),
+                             "shape": f"M={pm} N={rows} K={KG}", "tflops": round(tflops, 1),
                              "ms": round(pms, 4), "peak_tflops": bf16_peak, "peak_kind": peak_kind,
                              "frac": round(tflops / bf16_peak, 4)}
     result["clocks"] = clocks
@@ -485,7 +534,9 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="nsq", choices=["nsq", "reference"])
-    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--layers", type=int, default=None, help="layer copies per step (default: the workload's)")
+    ap.add_argument("--workload", default="l3-8b", choices=sorted(WORKLOADS))
+    ap.add_argument("--tokens", type=int, default=1, help="tokens per decode step, M (1..16)")
     ap.add_argument("--prefill-m", type=int, default=512)
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--skip-roofline", action="store_true")
@@ -499,6 +550,9 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    select_workload(args.workload, args.tokens)
+    if args.layers is None:
+        args.layers = WORKLOADS[args.workload]["layers"]
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
