@@ -21,6 +21,10 @@ int run_gemv_fused(const nsq_segment* segs, int nseg, const float* x, const XGro
 bool fused_covers(const nsq_segment* segs, int nseg, int64_t K);
 bool fused_self_prepare_fits(int64_t M, int64_t K);
 bool gemv_force_general();
+int run_gemv_mma(const nsq_segment* segs, int nseg, const XGroup* xg, int64_t M, int64_t K, cudaStream_t st,
+                 int num_sms, const XchgDesc* xd);
+int gemv_mma_min_m();
+bool gemv_mma_covers(const nsq_segment* segs, int nseg, int64_t M, int64_t K);
 int run_gemm_bf16(const uint8_t* w, int type, int layout, const void* x, void* y, int64_t M, int64_t N, int64_t K,
                   cudaStream_t st, int num_sms);
 cudaError_t launch_matmul_f32(const float* a, const float* b, float* c, int64_t M, int64_t K, int64_t N,
@@ -201,8 +205,9 @@ int nsq_gemv_multi(const nsq_segment* segs, int nseg, const float* x, int64_t M,
     // through the workspace
     if (reinterpret_cast<uintptr_t>(x) & 3) return NSQ_ERR_ALIGN;
   }
+  const bool mma = !gemv_force_general() && M >= gemv_mma_min_m() && gemv_mma_covers(segs, nseg, M, K);
   const bool fused = !gemv_force_general() && fused_covers(segs, nseg, K);
-  const bool self = fused && fused_self_prepare_fits(M, K) && !(reinterpret_cast<uintptr_t>(x) & 15);
+  const bool self = !mma && fused && fused_self_prepare_fits(M, K) && !(reinterpret_cast<uintptr_t>(x) & 15);
   if (!self) {
     if (!workspace) return NSQ_ERR_WORKSPACE;
     if (reinterpret_cast<uintptr_t>(workspace) & 15) return NSQ_ERR_ALIGN;
@@ -220,6 +225,10 @@ int nsq_gemv_multi(const nsq_segment* segs, int nseg, const float* x, int64_t M,
       return NSQ_ERR_WORKSPACE;
   }
   if (launch_prepare_x(x, static_cast<XGroup*>(workspace), M, K, st, di.num_sms) != cudaSuccess) return NSQ_ERR_CUDA;
+  if (mma) {
+    rc = run_gemv_mma(segs, nseg, static_cast<const XGroup*>(workspace), M, K, st, di.num_sms, nullptr);
+    if (rc != -1) return rc;
+  }
   if (fused) {
     rc = run_gemv_fused(segs, nseg, nullptr, static_cast<const XGroup*>(workspace), M, K, st, di.num_sms);
     if (rc != -1) return rc;
@@ -255,8 +264,9 @@ int nsq_gemv_multi_xchg(const nsq_xsegment* segs, int nseg, const float* x, int6
   }
   if (!x) return NSQ_ERR_NULL;
   if (reinterpret_cast<uintptr_t>(x) & 3) return NSQ_ERR_ALIGN;
-  if (!fused_covers(sl, nseg, K)) return NSQ_ERR_SHAPE;
-  const bool self = fused_self_prepare_fits(M, K) && !(reinterpret_cast<uintptr_t>(x) & 15);
+  const bool mma = M >= gemv_mma_min_m() && gemv_mma_covers(sl, nseg, M, K);
+  if (!mma && !fused_covers(sl, nseg, K)) return NSQ_ERR_SHAPE;
+  const bool self = !mma && fused_self_prepare_fits(M, K) && !(reinterpret_cast<uintptr_t>(x) & 15);
   if (!self) {
     if (!workspace) return NSQ_ERR_WORKSPACE;
     if (reinterpret_cast<uintptr_t>(workspace) & 15) return NSQ_ERR_ALIGN;
@@ -273,8 +283,9 @@ int nsq_gemv_multi_xchg(const nsq_xsegment* segs, int nseg, const float* x, int6
         launch_prepare_x(x, static_cast<XGroup*>(workspace), M, K, st, di.num_sms) != cudaSuccess)
       return NSQ_ERR_CUDA;
   }
-  rc = run_gemv_fused(sl, nseg, self ? x : nullptr, self ? nullptr : static_cast<const XGroup*>(workspace), M, K, st,
-                      di.num_sms, &xd);
+  rc = mma ? run_gemv_mma(sl, nseg, static_cast<const XGroup*>(workspace), M, K, st, di.num_sms, &xd)
+           : run_gemv_fused(sl, nseg, self ? x : nullptr, self ? nullptr : static_cast<const XGroup*>(workspace), M,
+                            K, st, di.num_sms, &xd);
   return rc == -1 ? NSQ_ERR_SHAPE : rc;
 }
 

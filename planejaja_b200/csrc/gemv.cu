@@ -542,6 +542,9 @@ static int run_gemv_t(const uint8_t* w, const XGroup* xg, float* y, int64_t M, i
 
 int run_gemv_fused(const nsq_segment* segs, int nseg, const float* x, const XGroup* xg, int64_t M, int64_t K,
                    cudaStream_t st, int num_sms, const XchgDesc* xd = nullptr);
+int run_gemv_mma(const nsq_segment* segs, int nseg, const XGroup* xg, int64_t M, int64_t K, cudaStream_t st,
+                 int num_sms, const XchgDesc* xd);
+int gemv_mma_min_m();
 
 bool gemv_force_general() {
   // NSQ_GEMV_GENERAL=1 forces the general kernel below (the parity tests use
@@ -550,13 +553,16 @@ bool gemv_force_general() {
   return force && force[0] == '1';
 }
 
-// GEMV on prepared activations: the fused kernel (gemv_rows.cu) in
-// workspace mode where the shape allows it, else the general kernel.
+// GEMV on prepared activations: the tensor-core kernel (gemv_mma.cu) for
+// M >= gemv_mma_min_m(), else the fused kernel (gemv_rows.cu) in workspace
+// mode where the shape allows it, else the general kernel.
 int run_gemv(const uint8_t* w, int type, int layout, const XGroup* xg, float* y, int64_t M, int64_t N, int64_t K,
              cudaStream_t st, int num_sms) {
   if (!gemv_force_general()) {
     nsq_segment sg{w, type, layout, N, y};
-    const int rc = run_gemv_fused(&sg, 1, nullptr, xg, M, K, st, num_sms);
+    int rc = -1;
+    if (M >= gemv_mma_min_m()) rc = run_gemv_mma(&sg, 1, xg, M, K, st, num_sms, nullptr);
+    if (rc == -1) rc = run_gemv_fused(&sg, 1, nullptr, xg, M, K, st, num_sms);
     if (rc != -1) return rc;
   }
   switch (type) {

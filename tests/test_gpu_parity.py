@@ -84,13 +84,17 @@ def test_dequant_empty(eng):
 
 
 # ---------------------------------------------------------------- GEMV
-@pytest.fixture(params=["rows", "general"])
+@pytest.fixture(params=["rows", "mma", "general"])
 def gemv_kernel(request, monkeypatch):
-    """Runs a test with the one-lane-per-row kernel and with the general kernel."""
+    """Runs a test with each GEMV kernel: one lane per row (dp4a, every M),
+    integer tensor cores (every M), and the general kernel."""
+    monkeypatch.delenv("NSQ_GEMV_GENERAL", raising=False)
     if request.param == "general":
         monkeypatch.setenv("NSQ_GEMV_GENERAL", "1")
+    elif request.param == "mma":
+        monkeypatch.setenv("NSQ_MMA_MIN_M", "1")
     else:
-        monkeypatch.delenv("NSQ_GEMV_GENERAL", raising=False)
+        monkeypatch.setenv("NSQ_MMA_MIN_M", "17")
     return request.param
 
 
