@@ -3,9 +3,14 @@
 //   y[M x N] (bf16) = x[M x K] (bf16) . W^T,   W: N rows of GGUF blocks
 //
 // "Swap-AB" tiling: the weights are the UMMA M side (128 rows of W per CTA),
-// the tokens the UMMA N side (TOK = 128 or 256 per CTA), so D = W_tile .
-// x_tile^T is a [128 x TOK] fp32 accumulator in tensor memory (TOK columns).
-// K advances in blocks of 64 (one 128-byte swizzle atom of bf16).
+// the tokens the UMMA N side (TOK = 128, 256 or 512 per CTA), so D = W_tile .
+// x_tile^T is a [128 x TOK] fp32 accumulator in tensor memory (TOK columns;
+// 512 is all of it, filled by two N = 256 MMAs per K step).  The kernel is
+// bound by the dequant warps, so a larger token tile, which reuses every
+// dequantized weight tile for more tokens, is worth the shallower ring: on
+// B200, Q4_K [14336 x 4096] at M = 512 runs 977 TFLOP/s with 512-token tiles
+// against 582 with 256.  K advances in blocks of 64 (one 128-byte swizzle
+// atom of bf16).
 //
 // Warp roles (384 threads):
 //   warp 0      : TMA producer -- one thread loads the x tile [TOK x 64]
@@ -271,7 +276,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_tc_kernel(const __grid_c
   constexpr uint32_t X_STAGE = TOK * 128;
   constexpr uint32_t RAW_STAGE = GEMM_BM * RawCol<TYPE>::pitch;
   constexpr int CB = RawCol<TYPE>::bytes;
-  constexpr uint32_t IDESC = umma_idesc_bf16(GEMM_BM, TOK);
+  // UMMA N is at most 256: a 512-token tile is two MMAs per K step into
+  // accumulator columns [0, 256) and [256, 512)
+  constexpr int NH = TOK > 256 ? 2 : 1;
+  constexpr int TN = TOK / NH;
+  constexpr uint32_t IDESC = umma_idesc_bf16(GEMM_BM, TN);
   constexpr int GEMM_STAGES = gemm_stages<TYPE, TOK>();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -322,7 +331,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_tc_kernel(const __grid_c
         const uint32_t par = (uint32_t)((kb / GEMM_STAGES) & 1);
         if (!mbar_wait_bounded(&empty[s], par ^ 1)) break;
         mbar_arrive_expect_tx(&full[s], X_STAGE);
-        tma_load_2d(x_sm + s * X_STAGE, &xmap, kb * GEMM_BK, m0, &full[s]);
+#pragma unroll
+        for (int h = 0; h < NH; ++h)
+          tma_load_2d(x_sm + s * X_STAGE + h * TN * 128, &xmap, kb * GEMM_BK, m0 + h * TN, &full[s]);
       }
     }
   } else if (warp == 1) {
@@ -341,8 +352,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_tc_kernel(const __grid_c
 #pragma unroll
         for (int kk = 0; kk < GEMM_BK / 16; ++kk) {
           const uint64_t ad = umma_desc_sw128(w_base + s * W_STAGE + kk * 32);
-          const uint64_t bd = umma_desc_sw128(x_base + s * X_STAGE + kk * 32);
-          tc_mma_bf16(tmem_d, ad, bd, IDESC, (kb | kk) != 0 ? 1u : 0u);
+#pragma unroll
+          for (int h = 0; h < NH; ++h) {
+            const uint64_t bd = umma_desc_sw128(x_base + s * X_STAGE + h * TN * 128 + kk * 32);
+            tc_mma_bf16(tmem_d + (uint32_t)(h * TN), ad, bd, IDESC, (kb | kk) != 0 ? 1u : 0u);
+          }
         }
         tc_commit(&empty[s]);
       }
@@ -485,6 +499,19 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return fn;
 }
 
+static int encode_xmap(CUtensorMap* map, const void* x, int64_t M, int64_t K, int box_rows) {
+  auto enc = get_encode_fn();
+  if (!enc) return NSQ_ERR_CUDA;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
+  cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  cuuint32_t box[2] = {(cuuint32_t)GEMM_BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? NSQ_OK : NSQ_ERR_CUDA;
+}
+
 template <int TYPE, int TOK>
 static size_t gemm_smem_bytes() {
   constexpr int S = gemm_stages<TYPE, TOK>();
@@ -493,8 +520,13 @@ static size_t gemm_smem_bytes() {
 }
 
 template <int TYPE, int LAYOUT, int TOK>
-static int launch_gemm_t(const CUtensorMap& map, const CUtensorMap& wmap, const GemmParams& p, cudaStream_t st) {
+static int launch_gemm_t(const void* x, const CUtensorMap& wmap, const GemmParams& p, cudaStream_t st) {
   auto kern = gemm_tc_kernel<TYPE, LAYOUT, TOK>;
+  // the x tensor map's box is the kernel's own token tile (TMA boxes hold
+  // at most 256 rows: a 512-token tile is loaded as two boxes)
+  alignas(64) CUtensorMap map{};
+  const int rc = encode_xmap(&map, x, p.M, p.K, TOK > 256 ? 256 : TOK);
+  if (rc) return rc;
   const size_t smem = gemm_smem_bytes<TYPE, TOK>();
   static bool configured[64] = {};
   int dev = 0;
@@ -511,7 +543,7 @@ static int launch_gemm_t(const CUtensorMap& map, const CUtensorMap& wmap, const 
 }
 
 template <int TYPE, int LAYOUT>
-static int run_gemm_t(const CUtensorMap& xmap, const GemmParams& p0, int tok, cudaStream_t st) {
+static int run_gemm_t(const void* x, const GemmParams& p0, int tok, cudaStream_t st) {
   GemmParams p = p0;
   alignas(64) CUtensorMap wmap{};
   p.wmap_ok = 0;
@@ -529,21 +561,11 @@ static int run_gemm_t(const CUtensorMap& xmap, const GemmParams& p0, int tok, cu
         p.wmap_ok = 1;
     }
   }
-  if (p.M <= 128 || tok == 128) return launch_gemm_t<TYPE, LAYOUT, 128>(xmap, wmap, p, st);
-  return launch_gemm_t<TYPE, LAYOUT, 256>(xmap, wmap, p, st);
-}
-
-static int encode_xmap(CUtensorMap* map, const void* x, int64_t M, int64_t K, int box_rows) {
-  auto enc = get_encode_fn();
-  if (!enc) return NSQ_ERR_CUDA;
-  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
-  cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-  cuuint32_t box[2] = {(cuuint32_t)GEMM_BK, (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? NSQ_OK : NSQ_ERR_CUDA;
+  if (tok == 128) return launch_gemm_t<TYPE, LAYOUT, 128>(x, wmap, p, st);
+  if constexpr (gemm_stages<TYPE, 512>() >= 2) {
+    if (tok == 512) return launch_gemm_t<TYPE, LAYOUT, 512>(x, wmap, p, st);
+  }
+  return launch_gemm_t<TYPE, LAYOUT, 256>(x, wmap, p, st);
 }
 
 int run_gemm_bf16(const uint8_t* w, int type, int layout, const void* x, void* y, int64_t M, int64_t N, int64_t K,
@@ -556,20 +578,20 @@ int run_gemm_bf16(const uint8_t* w, int type, int layout, const void* x, void* y
   p.N = N;
   p.K = K;
   p.RB = (K / nsq_block_weights(type)) * nsq_block_bytes(type);
-  alignas(64) CUtensorMap map{};
-  // tokens per CTA: 128 for short prompts, else 256 (NSQ_GEMM_TOK overrides)
+  // tokens per CTA: 128 for short prompts, else 256 or 512 (NSQ_GEMM_TOK
+  // overrides); a 512-token tile reuses each dequantized weight tile twice
+  // as often, where two 64-wide stages of it fit beside the raw bytes
   const char* te = getenv("NSQ_GEMM_TOK");
-  int tok = M <= 128 ? 128 : 256;
-  if (te && atoi(te) == 128) tok = 128;
-  int rc = encode_xmap(&map, x, M, K, tok);
-  if (rc) return rc;
+  int tok = M <= 128 ? 128 : (M >= 512 ? 512 : 256);
+  if (te && (atoi(te) == 128 || atoi(te) == 256 || atoi(te) == 512)) tok = atoi(te);
+  if (M <= 128) tok = 128;
   switch (type) {
-    case NSQ_TYPE_Q4_0: return run_gemm_t<NSQ_TYPE_Q4_0, 0>(map, p, tok, st);
-    case NSQ_TYPE_Q8_0: return run_gemm_t<NSQ_TYPE_Q8_0, 0>(map, p, tok, st);
-    case NSQ_TYPE_Q4_K: return run_gemm_t<NSQ_TYPE_Q4_K, 0>(map, p, tok, st);
+    case NSQ_TYPE_Q4_0: return run_gemm_t<NSQ_TYPE_Q4_0, 0>(x, p, tok, st);
+    case NSQ_TYPE_Q8_0: return run_gemm_t<NSQ_TYPE_Q8_0, 0>(x, p, tok, st);
+    case NSQ_TYPE_Q4_K: return run_gemm_t<NSQ_TYPE_Q4_K, 0>(x, p, tok, st);
     case NSQ_TYPE_Q6_K:
-      if (layout == NSQ_Q6K_NODESTOR) return run_gemm_t<NSQ_TYPE_Q6_K, NSQ_Q6K_NODESTOR>(map, p, tok, st);
-      return run_gemm_t<NSQ_TYPE_Q6_K, NSQ_Q6K_GGML>(map, p, tok, st);
+      if (layout == NSQ_Q6K_NODESTOR) return run_gemm_t<NSQ_TYPE_Q6_K, NSQ_Q6K_NODESTOR>(x, p, tok, st);
+      return run_gemm_t<NSQ_TYPE_Q6_K, NSQ_Q6K_GGML>(x, p, tok, st);
     default: return NSQ_ERR_TYPE;
   }
 }

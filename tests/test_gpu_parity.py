@@ -221,11 +221,14 @@ def test_gemv_errors_on_gpu(eng):
 
 
 # ---------------------------------------------------------------- GEMM
-@pytest.fixture(params=["tok_auto", "tok128"])
+@pytest.fixture(params=["tok_auto", "tok128", "tok512"])
 def gemm_tok(request, monkeypatch):
-    """Runs a GEMM test with the default token tile and with 128-token tiles."""
+    """Runs a GEMM test with the default token tile, 128-token tiles and
+    512-token tiles (two N = 256 MMAs per K step; Q8_0 falls back to 256)."""
     if request.param == "tok128":
         monkeypatch.setenv("NSQ_GEMM_TOK", "128")
+    elif request.param == "tok512":
+        monkeypatch.setenv("NSQ_GEMM_TOK", "512")
     else:
         monkeypatch.delenv("NSQ_GEMM_TOK", raising=False)
     return request.param
