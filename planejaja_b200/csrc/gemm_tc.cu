@@ -266,7 +266,27 @@ struct GemmParams {
   __nv_bfloat16* y;
   int64_t M, N, K, RB;
   int wmap_ok;  // 1: raw weight columns come by one 2-D TMA box per column
+  int S;        // split-K: CTAs per cluster, each over 1/S of the 256-wide K columns
 };
+
+// Split-K cluster helpers (distributed shared memory).
+__device__ __forceinline__ uint32_t gemm_cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void gemm_cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t gemm_cluster_map(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void gemm_st_cluster_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
 
 template <int TYPE, int LAYOUT, int TOK>
 __global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap xmap,
@@ -295,10 +315,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_tc_kernel(const __grid_c
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t n0 = (int64_t)blockIdx.x * GEMM_BM;
+  // split-K: the S CTAs of a cluster share one output tile, rank r taking
+  // 256-wide K columns [c0, c1)
+  const int split = p.S > 1 ? p.S : 1;
+  const int rank = split > 1 ? (int)gemm_cluster_rank() : 0;
+  const int64_t n0 = (int64_t)(blockIdx.x / split) * GEMM_BM;
   const int m0 = (int)blockIdx.y * TOK;
-  const int KB = (int)(p.K / GEMM_BK);
-  const int NCOL = KB / 4;  // 256-wide K columns
+  const int NCOL = (int)(p.K / 256);
+  const int c0 = NCOL * rank / split, c1 = NCOL * (rank + 1) / split;
+  const int kb0 = 4 * c0, kb1 = 4 * c1;
   const int rows_valid = (int)min((int64_t)GEMM_BM, p.N - n0);
 
   if (threadIdx.x == 0) {
@@ -322,13 +347,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_tc_kernel(const __grid_c
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_d = *tmem_slot;
+  bool have = false;  // epilogue warps: the accumulator is complete
 
   if (warp == 0) {
     // ---- x tiles: TMA 2-D, 128B swizzle
     if (lane == 0) {
-      for (int kb = 0; kb < KB; ++kb) {
-        const int s = kb % GEMM_STAGES;
-        const uint32_t par = (uint32_t)((kb / GEMM_STAGES) & 1);
+      for (int kb = kb0; kb < kb1; ++kb) {
+        const int s = (kb - kb0) % GEMM_STAGES;
+        const uint32_t par = (uint32_t)(((kb - kb0) / GEMM_STAGES) & 1);
         if (!mbar_wait_bounded(&empty[s], par ^ 1)) break;
         mbar_arrive_expect_tx(&full[s], X_STAGE);
 #pragma unroll
@@ -341,9 +367,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_tc_kernel(const __grid_c
     if (lane == 0) {
       const uint32_t w_base = smem_u32(w_sm), x_base = smem_u32(x_sm);
       bool ok = true;
-      for (int kb = 0; kb < KB; ++kb) {
-        const int s = kb % GEMM_STAGES;
-        const uint32_t par = (uint32_t)((kb / GEMM_STAGES) & 1);
+      for (int kb = kb0; kb < kb1; ++kb) {
+        const int s = (kb - kb0) % GEMM_STAGES;
+        const uint32_t par = (uint32_t)(((kb - kb0) / GEMM_STAGES) & 1);
         if (!mbar_wait_bounded(&full[s], par)) {
           ok = false;
           break;
@@ -355,7 +381,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_tc_kernel(const __grid_c
 #pragma unroll
           for (int h = 0; h < NH; ++h) {
             const uint64_t bd = umma_desc_sw128(x_base + s * X_STAGE + h * TN * 128 + kk * 32);
-            tc_mma_bf16(tmem_d + (uint32_t)(h * TN), ad, bd, IDESC, (kb | kk) != 0 ? 1u : 0u);
+            tc_mma_bf16(tmem_d + (uint32_t)(h * TN), ad, bd, IDESC, (kb != kb0 || kk != 0) ? 1u : 0u);
           }
         }
         tc_commit(&empty[s]);
@@ -366,9 +392,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_tc_kernel(const __grid_c
     // ---- raw GGUF bytes of the CTA's 128 rows, one 256-wide column at a time
     const int64_t total = p.N * p.RB;
     const int64_t cap = total & ~int64_t(15);
-    for (int c = 0; c < NCOL; ++c) {
-      const int rs = c % GEMM_RAW_STAGES;
-      if (!mbar_wait_bounded(&raw_empty[rs], (uint32_t)(((c / GEMM_RAW_STAGES) & 1) ^ 1))) break;
+    for (int c = c0; c < c1; ++c) {
+      const int rs = (c - c0) % GEMM_RAW_STAGES;
+      if (!mbar_wait_bounded(&raw_empty[rs], (uint32_t)((((c - c0) / GEMM_RAW_STAGES) & 1) ^ 1))) break;
       fence_proxy_async_smem();
       uint8_t* dst = raw_sm + rs * RAW_STAGE;
       if (p.wmap_ok) {
@@ -417,10 +443,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_tc_kernel(const __grid_c
     const int r = (t & 7) | ((t >> 5) << 3);
     const bool row_ok = r < rows_valid;
     bool ok = true;
-    for (int kb = 0; kb < KB; ++kb) {
-      const int c = kb >> 2, q = kb & 3, rs = c % GEMM_RAW_STAGES;
-      const int s = kb % GEMM_STAGES;
-      if (q == 0 && !mbar_wait_bounded(&raw_full[rs], (uint32_t)((c / GEMM_RAW_STAGES) & 1))) {
+    for (int kb = kb0; kb < kb1; ++kb) {
+      const int c = kb >> 2, q = kb & 3, rs = (c - c0) % GEMM_RAW_STAGES;
+      const int s = (kb - kb0) % GEMM_STAGES;
+      if (q == 0 && !mbar_wait_bounded(&raw_full[rs], (uint32_t)(((c - c0) / GEMM_RAW_STAGES) & 1))) {
         ok = false;
         break;
       }
@@ -441,7 +467,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_tc_kernel(const __grid_c
         __syncwarp();
         if (lane == 0) mbar_arrive(&raw_empty[rs]);
       }
-      if (!mbar_wait_bounded(&empty[s], (uint32_t)(((kb / GEMM_STAGES) & 1) ^ 1))) {
+      if (!mbar_wait_bounded(&empty[s], (uint32_t)((((kb - kb0) / GEMM_STAGES) & 1) ^ 1))) {
         ok = false;
         break;
       }
@@ -457,23 +483,85 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_tc_kernel(const __grid_c
     }
     // ---- epilogue: warp w reads TMEM lanes 32*(w%4).. (its W rows) for a
     // quarter of the TOK accumulator columns
-    if (ok && mbar_wait_bounded(accum, 0)) {
-      tc_fence_after();
-      const int qd = warp & 3;
-      const int part = (warp - GEMM_DQ_WARP0) >> 2;  // 0..3
-      const int64_t n = n0 + 32 * qd + lane;
+    have = ok && mbar_wait_bounded(accum, 0);
+    if (have) tc_fence_after();
+    if (split == 1) {
+      if (have) {
+        const int qd = warp & 3;
+        const int part = (warp - GEMM_DQ_WARP0) >> 2;  // 0..3
+        const int64_t n = n0 + 32 * qd + lane;
 #pragma unroll 1
-      for (int c0 = part * (TOK / 4); c0 < (part + 1) * (TOK / 4); c0 += 32) {
-        uint32_t v[32];
-        tc_ld_32x32b_x32(tmem_d + ((uint32_t)(32 * qd) << 16) + (uint32_t)c0, v);
-        if (n < p.N) {
+        for (int cc = part * (TOK / 4); cc < (part + 1) * (TOK / 4); cc += 32) {
+          uint32_t v[32];
+          tc_ld_32x32b_x32(tmem_d + ((uint32_t)(32 * qd) << 16) + (uint32_t)cc, v);
+          if (n < p.N) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int64_t m = (int64_t)m0 + c0 + j;
-            if (m < p.M) p.y[m * p.N + n] = __float2bfloat16_rn(__uint_as_float(v[j]));
+            for (int j = 0; j < 32; ++j) {
+              const int64_t m = (int64_t)m0 + cc + j;
+              if (m < p.M) p.y[m * p.N + n] = __float2bfloat16_rn(__uint_as_float(v[j]));
+            }
           }
         }
       }
+    }
+  }
+  if (split > 1) {
+    // Split-K reduction through distributed shared memory, in rounds of 32
+    // accumulator columns per epilogue warp.  The non-leader ranks store
+    // their partial sums into the leader's shared memory (the stage and raw
+    // buffers, idle once the MMAs are done; slot [rank - 1][warp][lane][32]
+    // f32), the leader adds them in rank order and writes bf16.  Every
+    // thread of every CTA passes the same cluster barriers.
+    constexpr int kRounds = TOK / 4 / 32;
+    float* slots = reinterpret_cast<float*>(smem);
+    const bool epi_warp = warp >= GEMM_DQ_WARP0;
+    const int qd = warp & 3;
+    const int part = (warp - GEMM_DQ_WARP0) >> 2;
+    const int ew = warp - GEMM_DQ_WARP0;  // 0..15
+    gemm_cluster_sync();  // every CTA of the cluster is past its main loop
+#pragma unroll 1
+    for (int rd = 0; rd < kRounds; ++rd) {
+      const int cc = part * (TOK / 4) + 32 * rd;
+      uint32_t v[32];
+      if (epi_warp) {
+        if (have) {
+          tc_ld_32x32b_x32(tmem_d + ((uint32_t)(32 * qd) << 16) + (uint32_t)cc, v);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = 0u;
+        }
+        if (rank > 0) {
+          const uint32_t dst = gemm_cluster_map(slots + ((size_t)((rank - 1) * 16 + ew) * 32 + lane) * 32, 0);
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) gemm_st_cluster_v4(dst + 4 * j, v[j], v[j + 1], v[j + 2], v[j + 3]);
+        }
+      }
+      gemm_cluster_sync();  // partials of this round have landed in the leader
+      if (epi_warp && rank == 0) {
+        const int64_t n = n0 + 32 * qd + lane;
+        float acc[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[j] = __uint_as_float(v[j]);
+        for (int r = 1; r < split; ++r) {
+          const float4* src = reinterpret_cast<const float4*>(slots + ((size_t)((r - 1) * 16 + ew) * 32 + lane) * 32);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 f = src[j];
+            acc[4 * j] += f.x;
+            acc[4 * j + 1] += f.y;
+            acc[4 * j + 2] += f.z;
+            acc[4 * j + 3] += f.w;
+          }
+        }
+        if (n < p.N && have) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int64_t m = (int64_t)m0 + cc + j;
+            if (m < p.M) p.y[m * p.N + n] = __float2bfloat16_rn(acc[j]);
+          }
+        }
+      }
+      gemm_cluster_sync();  // the leader is done with the slots of this round
     }
   }
   tc_fence_before();
@@ -520,12 +608,12 @@ static size_t gemm_smem_bytes() {
 }
 
 template <int TYPE, int LAYOUT, int TOK>
-static int launch_gemm_t(const void* x, const CUtensorMap& wmap, const GemmParams& p, cudaStream_t st) {
+static int launch_gemm_t(const void* x, const CUtensorMap& wmap, const GemmParams& p0, cudaStream_t st, int num_sms) {
   auto kern = gemm_tc_kernel<TYPE, LAYOUT, TOK>;
   // the x tensor map's box is the kernel's own token tile (TMA boxes hold
   // at most 256 rows: a 512-token tile is loaded as two boxes)
   alignas(64) CUtensorMap map{};
-  const int rc = encode_xmap(&map, x, p.M, p.K, TOK > 256 ? 256 : TOK);
+  const int rc = encode_xmap(&map, x, p0.M, p0.K, TOK > 256 ? 256 : TOK);
   if (rc) return rc;
   const size_t smem = gemm_smem_bytes<TYPE, TOK>();
   static bool configured[64] = {};
@@ -536,14 +624,43 @@ static int launch_gemm_t(const void* x, const CUtensorMap& wmap, const GemmParam
       return NSQ_ERR_CUDA;
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
-  dim3 grid((unsigned)((p.N + GEMM_BM - 1) / GEMM_BM), (unsigned)((p.M + TOK - 1) / TOK));
-  if (grid.y > 65535) return NSQ_ERR_SHAPE;
-  kern<<<grid, GEMM_THREADS, smem, st>>>(map, wmap, p);
-  return cudaGetLastError() == cudaSuccess ? NSQ_OK : NSQ_ERR_CUDA;
+  GemmParams p = p0;
+  const int64_t tiles_n = (p.N + GEMM_BM - 1) / GEMM_BM, tiles_m = (p.M + TOK - 1) / TOK;
+  if (tiles_m > 65535) return NSQ_ERR_SHAPE;
+  // Split-K when the tiles leave most SMs idle: S CTAs per tile (cluster),
+  // as many as the SMs allow, at most 4, each with >= 2 K columns, and no
+  // more partial-sum slots than the leader's stage buffers hold.
+  constexpr size_t region = (size_t)gemm_stages<TYPE, TOK>() * (GEMM_BM * 128 + TOK * 128) +
+                            (size_t)GEMM_RAW_STAGES * GEMM_BM * RawCol<TYPE>::pitch;
+  int S = 1;
+  const char* se = getenv("NSQ_GEMM_SPLIT");
+  const int64_t tiles = tiles_n * tiles_m, ncol = p.K / 256;
+  if (se && se[0]) {
+    S = atoi(se);
+  } else if (num_sms > 0 && tiles * 2 <= num_sms) {
+    S = (int)(num_sms / tiles);
+  }
+  if (S > 4) S = 4;
+  while (S > 1 && (ncol < 2 * S || (size_t)(S - 1) * 16 * 32 * 32 * 4 > region)) --S;
+  if (S < 1) S = 1;
+  p.S = S;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(tiles_n * S), (unsigned)tiles_m);
+  cfg.blockDim = dim3(GEMM_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)S;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = S > 1 ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, map, wmap, p) == cudaSuccess ? NSQ_OK : NSQ_ERR_CUDA;
 }
 
 template <int TYPE, int LAYOUT>
-static int run_gemm_t(const void* x, const GemmParams& p0, int tok, cudaStream_t st) {
+static int run_gemm_t(const void* x, const GemmParams& p0, int tok, cudaStream_t st, int num_sms) {
   GemmParams p = p0;
   alignas(64) CUtensorMap wmap{};
   p.wmap_ok = 0;
@@ -561,15 +678,15 @@ static int run_gemm_t(const void* x, const GemmParams& p0, int tok, cudaStream_t
         p.wmap_ok = 1;
     }
   }
-  if (tok == 128) return launch_gemm_t<TYPE, LAYOUT, 128>(x, wmap, p, st);
+  if (tok == 128) return launch_gemm_t<TYPE, LAYOUT, 128>(x, wmap, p, st, num_sms);
   if constexpr (gemm_stages<TYPE, 512>() >= 2) {
-    if (tok == 512) return launch_gemm_t<TYPE, LAYOUT, 512>(x, wmap, p, st);
+    if (tok == 512) return launch_gemm_t<TYPE, LAYOUT, 512>(x, wmap, p, st, num_sms);
   }
-  return launch_gemm_t<TYPE, LAYOUT, 256>(x, wmap, p, st);
+  return launch_gemm_t<TYPE, LAYOUT, 256>(x, wmap, p, st, num_sms);
 }
 
 int run_gemm_bf16(const uint8_t* w, int type, int layout, const void* x, void* y, int64_t M, int64_t N, int64_t K,
-                  cudaStream_t st, int /*num_sms*/) {
+                  cudaStream_t st, int num_sms) {
   if (K % 256) return NSQ_ERR_SHAPE;  // whole 256-weight columns
   GemmParams p{};
   p.w = w;
@@ -586,12 +703,12 @@ int run_gemm_bf16(const uint8_t* w, int type, int layout, const void* x, void* y
   if (te && (atoi(te) == 128 || atoi(te) == 256 || atoi(te) == 512)) tok = atoi(te);
   if (M <= 128) tok = 128;
   switch (type) {
-    case NSQ_TYPE_Q4_0: return run_gemm_t<NSQ_TYPE_Q4_0, 0>(x, p, tok, st);
-    case NSQ_TYPE_Q8_0: return run_gemm_t<NSQ_TYPE_Q8_0, 0>(x, p, tok, st);
-    case NSQ_TYPE_Q4_K: return run_gemm_t<NSQ_TYPE_Q4_K, 0>(x, p, tok, st);
+    case NSQ_TYPE_Q4_0: return run_gemm_t<NSQ_TYPE_Q4_0, 0>(x, p, tok, st, num_sms);
+    case NSQ_TYPE_Q8_0: return run_gemm_t<NSQ_TYPE_Q8_0, 0>(x, p, tok, st, num_sms);
+    case NSQ_TYPE_Q4_K: return run_gemm_t<NSQ_TYPE_Q4_K, 0>(x, p, tok, st, num_sms);
     case NSQ_TYPE_Q6_K:
-      if (layout == NSQ_Q6K_NODESTOR) return run_gemm_t<NSQ_TYPE_Q6_K, NSQ_Q6K_NODESTOR>(x, p, tok, st);
-      return run_gemm_t<NSQ_TYPE_Q6_K, NSQ_Q6K_GGML>(x, p, tok, st);
+      if (layout == NSQ_Q6K_NODESTOR) return run_gemm_t<NSQ_TYPE_Q6_K, NSQ_Q6K_NODESTOR>(x, p, tok, st, num_sms);
+      return run_gemm_t<NSQ_TYPE_Q6_K, NSQ_Q6K_GGML>(x, p, tok, st, num_sms);
     default: return NSQ_ERR_TYPE;
   }
 }

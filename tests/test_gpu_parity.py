@@ -221,16 +221,19 @@ def test_gemv_errors_on_gpu(eng):
 
 
 # ---------------------------------------------------------------- GEMM
-@pytest.fixture(params=["tok_auto", "tok128", "tok512"])
+@pytest.fixture(params=["tok_auto", "tok128", "tok512", "nosplit"])
 def gemm_tok(request, monkeypatch):
-    """Runs a GEMM test with the default token tile, 128-token tiles and
-    512-token tiles (two N = 256 MMAs per K step; Q8_0 falls back to 256)."""
+    """Runs a GEMM test with the default token tile (and the default split-K,
+    which small grids get), 128-token tiles, 512-token tiles (two N = 256
+    MMAs per K step; Q8_0 falls back to 256), and split-K switched off."""
+    monkeypatch.delenv("NSQ_GEMM_TOK", raising=False)
+    monkeypatch.delenv("NSQ_GEMM_SPLIT", raising=False)
     if request.param == "tok128":
         monkeypatch.setenv("NSQ_GEMM_TOK", "128")
     elif request.param == "tok512":
         monkeypatch.setenv("NSQ_GEMM_TOK", "512")
-    else:
-        monkeypatch.delenv("NSQ_GEMM_TOK", raising=False)
+    elif request.param == "nosplit":
+        monkeypatch.setenv("NSQ_GEMM_SPLIT", "1")
     return request.param
 
 
