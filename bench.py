@@ -27,8 +27,10 @@ configuration measured at 1/2/4/8 GPUs.
 metric  : decode GEMV HBM GB/s = (weight bytes + fp32 activations + fp32
           outputs) of the whole step / step time (max over ranks), all ranks.
 e2e     : the same step through the C-ABI engine calls with host buffers:
-          pinned-host -> device copy of every activation vector, the GEMVs,
-          device -> pinned-host copy of every output, stream sync per step.
+          pinned-host -> device copy of the step's activation vectors (the
+          inputs every layer copy reads), the GEMVs, one device ->
+          pinned-host copy of all outputs of all layers (one contiguous
+          buffer), stream sync per step.
 roofline: dominant kernel = the fused M = 1 Q4_K gate|up launch (FFN input
           projection, 2 x [14336 x 4096], 66.06 MB), timed alone with CUDA
           events rotating over the 32 layer copies; bound = HBM, peak =
@@ -275,8 +277,19 @@ def run_gpu(args, rank, world, local_rank):
         layers.append({name: (rows, buf if li == 0 else buf.clone()) for name, (rows, buf) in shards.items()})
     acts = [torch.from_numpy(a).to(dev) for a in acts_h]
     M = M_TOK
-    outs_local = [{name: torch.empty(M * rows, dtype=torch.float32, device=dev)
-                   for name, (rows, _) in layers[0].items()} for _ in range(L)]
+    def flat_views(sizes):
+        # one contiguous device buffer per step's outputs (one read-back per step)
+        flat = torch.empty(L * sum(M * n for _, n in sizes), dtype=torch.float32, device=dev)
+        views, off = [], 0
+        for _ in range(L):
+            d = {}
+            for name, n in sizes:
+                d[name] = flat[off:off + M * n]
+                off += M * n
+            views.append(d)
+        return flat, views
+
+    outs_local_flat, outs_local = flat_views([(name, rows) for name, (rows, _) in layers[0].items()])
     # scratch for prepared activations when they do not fit on chip (M > 4 or long rows)
     ws = eng.workspace(lib.nsq_gemv_workspace_size(M, max(ACT_K)))
     ws_ptr, ws_n = ws.data_ptr(), ws.numel()
@@ -294,10 +307,9 @@ def run_gpu(args, rank, world, local_rank):
         outs_full = [{name: exchange.view(layout.offsets[(li, name)][0], (M * n,)) for name, n, k, t in LAYER_SPEC}
                      for li in range(L)]
     elif world > 1:
-        outs_full = [{name: torch.empty(M * n, dtype=torch.float32, device=dev) for name, n, k, t in LAYER_SPEC}
-                     for _ in range(L)]
+        outs_full_flat, outs_full = flat_views([(name, n) for name, n, k, t in LAYER_SPEC])
     else:
-        outs_full = outs_local
+        outs_full_flat, outs_full = outs_local_flat, outs_local
     # one fused launch per shared activation (q|k|v, o, gate|up, down for Llama-3-8B)
     TYPE_OF = {name: t for name, n, k, t in LAYER_SPEC}
     N_OF = {name: n for name, n, k, t in LAYER_SPEC}
@@ -398,22 +410,23 @@ def run_gpu(args, rank, world, local_rank):
     value = step_bytes / (ms * 1e-3) / 1e9
 
     # ---- e2e: host buffers through the C-ABI calls, copies inside the timed region
+    # the step's inputs are its activation vectors (every layer copy reads
+    # the same ones); its result is every output of every layer, read back
+    # in one copy from the contiguous output buffer
     acts_pin = [torch.from_numpy(a).pin_memory() for a in acts_h]
-    outs_pin = [{name: torch.empty(M * n, dtype=torch.float32).pin_memory() for name, n, k, t in LAYER_SPEC}
-                for _ in range(L)]
-    h2d = sum(a.numel() * 4 for a in acts_pin) * L
-    d2h = sum(M * n * 4 for _, n, k, t in LAYER_SPEC) * L
+    if p2p:
+        out_dev = torch.as_tensor(exchange.view(0, (layout.nbytes // 4,)))
+    else:
+        out_dev = outs_full_flat
+    out_pin = torch.empty(out_dev.numel(), dtype=torch.float32).pin_memory()
+    h2d = sum(a.numel() * 4 for a in acts_pin)
+    d2h = out_pin.numel() * 4
 
     def e2e_step():
-        for li in range(L):
-            for a, src in enumerate(acts_pin):
-                acts[a].copy_(src, non_blocking=True)
-            if graph is None:
-                pass
+        for a, src in enumerate(acts_pin):
+            acts[a].copy_(src, non_blocking=True)
         run_step()
-        for li in range(L):
-            for name, n, k, t in LAYER_SPEC:
-                outs_pin[li][name].copy_(outs_full[li][name], non_blocking=True)
+        out_pin.copy_(out_dev, non_blocking=True)
         torch.cuda.current_stream(dev).synchronize()
 
     for _ in range(args.warmup):
