@@ -168,6 +168,28 @@ int nsq_gemv_multi(const nsq_segment *segs, int nseg, const float *x, int64_t M,
                    void *workspace, size_t workspace_bytes, void *stream);
 
 /*
+ * Fused FFN input projection: h[M x N] = silu(x . W_gate^T) * (x . W_up^T),
+ * one launch that streams both matrices (same format and shape) and never
+ * writes gate or up.  Replaces the reference's matmul(gate), matmul(up),
+ * silu, mul sequence (crates/nodestor-vulkan/src/transformer.rs:311-314,
+ * shaders/silu.comp:14-21, shaders/mul.comp), silu(g) = g * (1 / (1 +
+ * exp(-g))).  Same workspace rule as nsq_gemv_multi; needs K % 256 == 0.
+ */
+int nsq_gemv_swiglu(const void *w_gate, const void *w_up, int ggml_type, int q6k_layout, const float *x,
+                    float *h, int64_t M, int64_t N, int64_t K, void *workspace, size_t workspace_bytes,
+                    void *stream);
+
+/*
+ * GEMV with the residual add fused: y[M x N] = residual + x . W^T (residual
+ * may be y itself).  Replaces matmul followed by add
+ * (crates/nodestor-vulkan/src/transformer.rs:314-319, shaders/add.comp).
+ * Same workspace rule as nsq_gemv_multi; needs K % 256 == 0.
+ */
+int nsq_gemv_residual(const void *w, int ggml_type, int q6k_layout, const float *x, const float *residual,
+                      float *y, int64_t M, int64_t N, int64_t K, void *workspace, size_t workspace_bytes,
+                      void *stream);
+
+/*
  * Prefill GEMM on tcgen05 tensor cores: y[M x N] bf16 = x[M x K] bf16 . W^T,
  * weights dequantized to bf16 in shared memory, fp32 accumulation in TMEM.
  * Within 2e-2 relative error of the reference composition on the same

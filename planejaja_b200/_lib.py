@@ -45,6 +45,8 @@ SIGNATURES = [
     ("nsq_gemv_noalloc", _int, [_vp, _int, _int, _vp, _vp, _i64, _i64, _i64, _vp]),
     ("nsq_gemm_bf16", _int, [_vp, _int, _int, _vp, _vp, _i64, _i64, _i64, _vp]),
     ("nsq_matmul_f32", _int, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    ("nsq_gemv_swiglu", _int, [_vp, _vp, _int, _int, _vp, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),
+    ("nsq_gemv_residual", _int, [_vp, _int, _int, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),
     ("nsq_comm_handle_bytes", _sz, []),
     ("nsq_comm_create", _int, [_int, _int, _sz, ctypes.POINTER(ctypes.c_void_p), _vp]),
     ("nsq_comm_connect", _int, [_vp, _vp]),

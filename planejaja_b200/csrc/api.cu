@@ -17,7 +17,8 @@ cudaError_t launch_prepare_x(const float* x, XGroup* xg, int64_t M, int64_t K, c
 int run_gemv(const uint8_t* w, int type, int layout, const XGroup* xg, float* y, int64_t M, int64_t N, int64_t K,
              cudaStream_t st, int num_sms);
 int run_gemv_fused(const nsq_segment* segs, int nseg, const float* x, const XGroup* xg, int64_t M, int64_t K,
-                   cudaStream_t st, int num_sms, const XchgDesc* xd = nullptr);
+                   cudaStream_t st, int num_sms, const XchgDesc* xd = nullptr, int epi = 0,
+                   const float* const* res = nullptr);
 bool fused_covers(const nsq_segment* segs, int nseg, int64_t K);
 bool fused_self_prepare_fits(int64_t M, int64_t K);
 bool gemv_force_general();
@@ -239,6 +240,54 @@ int nsq_gemv_multi(const nsq_segment* segs, int nseg, const float* x, int64_t M,
     if (rc) return rc;
   }
   return NSQ_OK;
+}
+
+// Shared body of the fused-epilogue entry points: fused kernel only.
+static int gemv_epilogue(const nsq_segment* segs, int nseg, const float* x, int64_t M, int64_t K, void* workspace,
+                         size_t workspace_bytes, void* stream, int epi, const float* const* res) {
+  if (M < 1 || M > NSQ_GEMV_MAX_M || K % 256) return NSQ_ERR_SHAPE;
+  if (!x) return NSQ_ERR_NULL;
+  if (reinterpret_cast<uintptr_t>(x) & 3) return NSQ_ERR_ALIGN;
+  if (!fused_covers(segs, nseg, K)) return NSQ_ERR_SHAPE;
+  const bool self = fused_self_prepare_fits(M, K) && !(reinterpret_cast<uintptr_t>(x) & 15);
+  if (!self) {
+    if (!workspace) return NSQ_ERR_WORKSPACE;
+    if (reinterpret_cast<uintptr_t>(workspace) & 15) return NSQ_ERR_ALIGN;
+    if (workspace_bytes < nsq_gemv_workspace_size(M, K)) return NSQ_ERR_WORKSPACE;
+  }
+  DevInfo di;
+  int rc;
+  if ((rc = check_device(di))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (!self && launch_prepare_x(x, static_cast<XGroup*>(workspace), M, K, st, di.num_sms) != cudaSuccess)
+    return NSQ_ERR_CUDA;
+  rc = run_gemv_fused(segs, nseg, self ? x : nullptr, self ? nullptr : static_cast<const XGroup*>(workspace), M, K, st,
+                      di.num_sms, nullptr, epi, res);
+  return rc == -1 ? NSQ_ERR_SHAPE : rc;
+}
+
+int nsq_gemv_swiglu(const void* w_gate, const void* w_up, int ggml_type, int q6k_layout, const float* x, float* h,
+                    int64_t M, int64_t N, int64_t K, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc;
+  if ((rc = check_weights(w_gate, ggml_type, q6k_layout, K))) return rc;
+  if ((rc = check_weights(w_up, ggml_type, q6k_layout, K))) return rc;
+  if (N < 1) return NSQ_ERR_SHAPE;
+  if (!h) return NSQ_ERR_NULL;
+  if (reinterpret_cast<uintptr_t>(h) & 3) return NSQ_ERR_ALIGN;
+  const nsq_segment segs[2] = {{w_gate, ggml_type, q6k_layout, N, h}, {w_up, ggml_type, q6k_layout, N, h}};
+  return gemv_epilogue(segs, 2, x, M, K, workspace, workspace_bytes, stream, 2, nullptr);
+}
+
+int nsq_gemv_residual(const void* w, int ggml_type, int q6k_layout, const float* x, const float* residual, float* y,
+                      int64_t M, int64_t N, int64_t K, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc;
+  if ((rc = check_weights(w, ggml_type, q6k_layout, K))) return rc;
+  if (N < 1) return NSQ_ERR_SHAPE;
+  if (!y || !residual) return NSQ_ERR_NULL;
+  if ((reinterpret_cast<uintptr_t>(y) & 3) || (reinterpret_cast<uintptr_t>(residual) & 3)) return NSQ_ERR_ALIGN;
+  const nsq_segment seg{w, ggml_type, q6k_layout, N, y};
+  const float* res[1] = {residual};
+  return gemv_epilogue(&seg, 1, x, M, K, workspace, workspace_bytes, stream, 1, res);
 }
 
 int nsq_gemv_multi_xchg(const nsq_xsegment* segs, int nseg, const float* x, int64_t M, int64_t K, nsq_comm* comm,

@@ -541,7 +541,8 @@ static int run_gemv_t(const uint8_t* w, const XGroup* xg, float* y, int64_t M, i
 }
 
 int run_gemv_fused(const nsq_segment* segs, int nseg, const float* x, const XGroup* xg, int64_t M, int64_t K,
-                   cudaStream_t st, int num_sms, const XchgDesc* xd = nullptr);
+                   cudaStream_t st, int num_sms, const XchgDesc* xd = nullptr, int epi = 0,
+                   const float* const* res = nullptr);
 int run_gemv_mma(const nsq_segment* segs, int nseg, const XGroup* xg, int64_t M, int64_t K, cudaStream_t st,
                  int num_sms, const XchgDesc* xd);
 int gemv_mma_min_m();

@@ -285,6 +285,8 @@ struct FusedParams {
   int R, KS, PPS, npieces, nchunks;
   int xstride;          // bytes per token of per-stage activation records (workspace mode)
   int stage_bytes, nstages, max_pitch;
+  int Rblk;             // rows per block walked by the cursor: R, or R / 2 with the SwiGLU epilogue
+  const float* res[NSQ_MAX_SEGMENTS];  // residual-add epilogue: y = res + x . W^T (may alias y)
   int C;                // self-prepared mode: CTAs per cluster sharing the activation quantisation
   int64_t nrb;          // row blocks of R rows in the concatenated row space
   // Row-sharded exchange (P > 1): every output row is stored into the
@@ -383,7 +385,7 @@ struct ItemCursor {
     while (seg < p.nseg - 1 && r_begin >= p.seg[seg].row0 + p.seg[seg].N) ++seg;
     row0 = r_begin - p.seg[seg].row0;
     const int64_t seg_end = min(r_end, p.seg[seg].row0 + p.seg[seg].N) - p.seg[seg].row0;
-    rows = min((int64_t)p.R, seg_end - row0);
+    rows = min((int64_t)p.Rblk, seg_end - row0);
     c = 0;
   }
   // advance; returns false when the CTA's rows are done
@@ -398,12 +400,16 @@ struct ItemCursor {
       row0 = 0;
     }
     const int64_t seg_end = min(r_end, p.seg[seg].row0 + p.seg[seg].N) - p.seg[seg].row0;
-    rows = min((int64_t)p.R, seg_end - row0);
+    rows = min((int64_t)p.Rblk, seg_end - row0);
     return rows > 0;
   }
 };
 
-template <int M, bool XSELF, int CODE>
+// EPI: 0 = y, 1 = y = residual + x . W^T, 2 = SwiGLU pair: segments 0 (gate)
+// and 1 (up) have the same rows; a block holds Rblk = R/2 rows of each (gate
+// in shared rows [0, R/2), up in [R/2, R)) and the output is
+// h = silu(gate) * up into segment 0's y.
+template <int M, bool XSELF, int CODE, int EPI>
 __global__ void __launch_bounds__(kRowsThreads, 4) gemv_fused_kernel(const __grid_constant__ FusedParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* stages = smem;
@@ -417,8 +423,8 @@ __global__ void __launch_bounds__(kRowsThreads, 4) gemv_fused_kernel(const __gri
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // rows per CTA: whole row blocks (nrb > 0; the counts differ by at most
   // one) or an even split of the rows
-  const int64_t r_begin = p.nrb > 0 ? min(p.T, p.R * (p.nrb * blockIdx.x / gridDim.x)) : p.T * blockIdx.x / gridDim.x;
-  const int64_t r_end = p.nrb > 0 ? min(p.T, p.R * (p.nrb * (blockIdx.x + 1) / gridDim.x))
+  const int64_t r_begin = p.nrb > 0 ? min(p.T, p.Rblk * (p.nrb * blockIdx.x / gridDim.x)) : p.T * blockIdx.x / gridDim.x;
+  const int64_t r_end = p.nrb > 0 ? min(p.T, p.Rblk * (p.nrb * (blockIdx.x + 1) / gridDim.x))
                                   : p.T * (blockIdx.x + 1) / gridDim.x;
   const bool clustered = XSELF && p.C > 1;
 
@@ -447,10 +453,22 @@ __global__ void __launch_bounds__(kRowsThreads, 4) gemv_fused_kernel(const __gri
         uint8_t* slot = stages + (size_t)s * p.stage_bytes;
         if (with_w) {
           if (lane == 0)
-            mbar_arrive_expect_tx(&full[s], (uint32_t)(it.rows * rbytes + (XSELF ? 0 : M * ng * 80)));
+            mbar_arrive_expect_tx(&full[s],
+                                  (uint32_t)((EPI == 2 ? 2 : 1) * it.rows * rbytes + (XSELF ? 0 : M * ng * 80)));
           __syncwarp();
-          for (int r = lane; r < (int)it.rows; r += 32)
-            bulk_g2s(slot + r * sg.pitch, sg.w + (it.row0 + r) * sg.RB + off, rbytes, &full[s]);
+          if constexpr (EPI == 2) {
+            // the block's gate rows and the same rows of up
+            const FSeg& su = p.seg[1];
+            for (int r = lane; r < 2 * (int)it.rows; r += 32) {
+              const bool up = r >= (int)it.rows;
+              const int rr = up ? r - (int)it.rows : r;
+              bulk_g2s(slot + (up ? rr + p.Rblk : rr) * sg.pitch, (up ? su.w : sg.w) + (it.row0 + rr) * sg.RB + off,
+                       rbytes, &full[s]);
+            }
+          } else {
+            for (int r = lane; r < (int)it.rows; r += 32)
+              bulk_g2s(slot + r * sg.pitch, sg.w + (it.row0 + r) * sg.RB + off, rbytes, &full[s]);
+          }
         }
         if (!XSELF && with_x && lane == 0) {
           uint8_t* xs = slot + p.R * p.max_pitch;
@@ -568,7 +586,7 @@ __global__ void __launch_bounds__(kRowsThreads, 4) gemv_fused_kernel(const __gri
           const int np = (int)min((int64_t)p.PPS, (int64_t)p.npieces - (int64_t)it.c * p.PPS);
           const uint8_t* slot = stages + (size_t)s * p.stage_bytes;
           const uint8_t* xbase = XSELF ? xsm + (int64_t)it.c * p.PPS * 8 * 80 : slot + p.R * p.max_pitch;
-          if (r < it.rows) {
+          if ((EPI == 2 ? (r & (p.Rblk - 1)) : r) < it.rows) {
             for (int j = cw * p.KS + ks; j < np; j += lanes_per_piece)
               run_piece<M, CODE>(sg.code, slot + r * sg.pitch + j * sg.piece_bytes, xbase + j * 8 * 80, xstride, acc);
           }
@@ -592,6 +610,15 @@ __global__ void __launch_bounds__(kRowsThreads, 4) gemv_fused_kernel(const __gri
             float v = 0.f;
 #pragma unroll
             for (int w = 0; w < kRowsConsumers; ++w) v += rd[(w * 32 + rr) * M + m];
+            if constexpr (EPI == 1) v += p.res[it.seg][(int64_t)m * sg.N + it.row0 + rr];
+            if constexpr (EPI == 2) {
+              float u = 0.f;
+#pragma unroll
+              for (int w = 0; w < kRowsConsumers; ++w) u += rd[(w * 32 + rr + p.Rblk) * M + m];
+              // silu.comp:18-20 then mul.comp: (g * sigmoid(g)) * up
+              const float sig = 1.0f / (1.0f + expf(-v));
+              v = v * sig * u;
+            }
             if (p.P > 1) {
               const int64_t idx = (int64_t)m * p.xnfull[it.seg] + p.xrow0[it.seg] + it.row0 + rr;
               for (int pr = 0; pr < p.P; ++pr)
@@ -654,7 +681,7 @@ static int piece_bytes_of(int type) {
 // Plans a fused launch; false if a segment's shape is not covered (K % 256,
 // Q6_K needs K % 2048, 16-byte row alignment).
 static bool plan_fused(const nsq_segment* segs, int nseg, int64_t K, int M, bool xself, int num_sms,
-                       int max_clusters, FusedParams& p, int& blocks, size_t& smem) {
+                       int max_clusters, FusedParams& p, int& blocks, size_t& smem, int min_r = 4) {
   if (nseg < 1 || nseg > NSQ_MAX_SEGMENTS || K % 256) return false;
   const int64_t npieces = K / 256;
   bool any_q6k = false;
@@ -677,7 +704,8 @@ static bool plan_fused(const nsq_segment* segs, int nseg, int64_t K, int M, bool
   const bool long_k = K >= 8192;
   int R = env_int("NSQ_ROWS_R", many_rows ? 16 : 8);
   if (R != 4 && R != 8 && R != 16 && R != 32) R = 8;
-  while (R > 4 && (T + R - 1) / R < (int64_t)num_sms) R >>= 1;
+  if (R < min_r) R = min_r;
+  while (R > min_r && (T + R - 1) / R < (int64_t)num_sms) R >>= 1;
   const int KS = 32 / R;
   int PPS = env_int("NSQ_ROWS_PPSM", many_rows ? 2 : 1) * kRowsConsumers * KS;
   if (PPS < 1) PPS = kRowsConsumers * KS;
@@ -721,7 +749,7 @@ static bool plan_fused(const nsq_segment* segs, int nseg, int64_t K, int M, bool
     acc_rows += p.seg[i].N;
   }
   p.nseg = nseg; p.T = T; p.K = K; p.GX = K / 32;
-  p.R = R; p.KS = KS; p.PPS = PPS; p.npieces = (int)npieces; p.nchunks = (int)((npieces + PPS - 1) / PPS);
+  p.R = R; p.Rblk = R; p.KS = KS; p.PPS = PPS; p.npieces = (int)npieces; p.nchunks = (int)((npieces + PPS - 1) / PPS);
   p.xstride = xstride; p.stage_bytes = stage_bytes; p.nstages = nstages; p.max_pitch = max_pitch;
   int per_sm = (int)((220 * 1024) / (smem + 1024));
   if (per_sm > 4) per_sm = 4;
@@ -753,9 +781,9 @@ static bool plan_fused(const nsq_segment* segs, int nseg, int64_t K, int M, bool
 
 static constexpr int kNoRoom = -2;  // launch_fused: the clusters do not all fit at once
 
-template <int M, bool XSELF, int CODE>
+template <int M, bool XSELF, int CODE, int EPI>
 static cudaError_t launch_fused(const FusedParams& p, int blocks, size_t smem, cudaStream_t st, int* max_clusters) {
-  auto kern = gemv_fused_kernel<M, XSELF, CODE>;
+  auto kern = gemv_fused_kernel<M, XSELF, CODE, EPI>;
   static size_t configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -807,28 +835,40 @@ static cudaError_t launch_fused(const FusedParams& p, int blocks, size_t smem, c
   return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
-template <bool XSELF, int CODE>
+template <bool XSELF, int CODE, int EPI>
 static cudaError_t launch_fused_mc(int M, const FusedParams& p, int blocks, size_t smem, cudaStream_t st, int* mc) {
   switch (M) {
-    case 1: return launch_fused<1, XSELF, CODE>(p, blocks, smem, st, mc);
-    case 2: return launch_fused<2, XSELF, CODE>(p, blocks, smem, st, mc);
-    case 3: return launch_fused<3, XSELF, CODE>(p, blocks, smem, st, mc);
-    default: return launch_fused<4, XSELF, CODE>(p, blocks, smem, st, mc);
+    case 1: return launch_fused<1, XSELF, CODE, EPI>(p, blocks, smem, st, mc);
+    case 2: return launch_fused<2, XSELF, CODE, EPI>(p, blocks, smem, st, mc);
+    case 3: return launch_fused<3, XSELF, CODE, EPI>(p, blocks, smem, st, mc);
+    default: return launch_fused<4, XSELF, CODE, EPI>(p, blocks, smem, st, mc);
   }
 }
 
-template <bool XSELF>
+template <bool XSELF, int EPI>
 static cudaError_t launch_fused_m(int M, const FusedParams& p, int blocks, size_t smem, cudaStream_t st, int* mc) {
   int code = p.seg[0].code;
   for (int i = 1; i < p.nseg; ++i)
     if (p.seg[i].code != code) code = kMixed;
   switch (code) {
-    case kQ4K: return launch_fused_mc<XSELF, kQ4K>(M, p, blocks, smem, st, mc);
-    case kQ6KG: return launch_fused_mc<XSELF, kQ6KG>(M, p, blocks, smem, st, mc);
-    case kQ6KN: return launch_fused_mc<XSELF, kQ6KN>(M, p, blocks, smem, st, mc);
-    case kQ40: return launch_fused_mc<XSELF, kQ40>(M, p, blocks, smem, st, mc);
-    case kQ80: return launch_fused_mc<XSELF, kQ80>(M, p, blocks, smem, st, mc);
-    default: return launch_fused_mc<XSELF, kMixed>(M, p, blocks, smem, st, mc);
+    case kQ4K: return launch_fused_mc<XSELF, kQ4K, EPI>(M, p, blocks, smem, st, mc);
+    case kQ6KG: return launch_fused_mc<XSELF, kQ6KG, EPI>(M, p, blocks, smem, st, mc);
+    case kQ6KN: return launch_fused_mc<XSELF, kQ6KN, EPI>(M, p, blocks, smem, st, mc);
+    case kQ40: return launch_fused_mc<XSELF, kQ40, EPI>(M, p, blocks, smem, st, mc);
+    case kQ80: return launch_fused_mc<XSELF, kQ80, EPI>(M, p, blocks, smem, st, mc);
+    default:
+      if constexpr (EPI == 0) return launch_fused_mc<XSELF, kMixed, 0>(M, p, blocks, smem, st, mc);
+      return cudaErrorInvalidValue;  // the epilogue forms take one format
+  }
+}
+
+template <bool XSELF>
+static cudaError_t launch_fused_e(int epi, int M, const FusedParams& p, int blocks, size_t smem, cudaStream_t st,
+                                  int* mc) {
+  switch (epi) {
+    case 1: return launch_fused_m<XSELF, 1>(M, p, blocks, smem, st, mc);
+    case 2: return launch_fused_m<XSELF, 2>(M, p, blocks, smem, st, mc);
+    default: return launch_fused_m<XSELF, 0>(M, p, blocks, smem, st, mc);
   }
 }
 
@@ -838,9 +878,16 @@ bool fused_self_prepare_fits(int64_t M, int64_t K) { return M <= 4 && M * (K / 3
 // Fused decode GEMV.  xg == nullptr: activations are prepared on chip from x
 // (requires fused_self_prepare_fits); otherwise xg holds prepared records.
 // Returns NSQ_OK / an error, or -1 if a shape is not covered.
+// epi: 0 plain; 1 residual add (res[i] per segment, [M x N_i], may alias y);
+// 2 SwiGLU (segments gate, up with equal formats and rows; h = silu(gate) *
+// up into segment 0's y).
 int run_gemv_fused(const nsq_segment* segs, int nseg, const float* x, const XGroup* xg, int64_t M, int64_t K,
-                   cudaStream_t st, int num_sms, const XchgDesc* xd) {
+                   cudaStream_t st, int num_sms, const XchgDesc* xd, int epi, const float* const* res) {
   const bool xself = (xg == nullptr);
+  if (epi == 2 && (nseg != 2 || segs[0].N != segs[1].N || segs[0].ggml_type != segs[1].ggml_type ||
+                   segs[0].q6k_layout != segs[1].q6k_layout))
+    return -1;
+  if (epi == 1 && !res) return -1;
   for (int64_t m0 = 0; m0 < M; m0 += 4) {
     const int mm = (int)((M - m0) < 4 ? (M - m0) : 4);
     nsq_segment sl[NSQ_MAX_SEGMENTS];
@@ -854,7 +901,16 @@ int run_gemv_fused(const nsq_segment* segs, int nseg, const float* x, const XGro
       FusedParams p{};
       int blocks;
       size_t smem;
-      if (!plan_fused(sl, nseg, K, mm, xself, num_sms, max_clusters, p, blocks, smem)) return -1;
+      if (!plan_fused(sl, nseg, K, mm, xself, num_sms, max_clusters, p, blocks, smem, epi == 2 ? 8 : 4)) return -1;
+      if (epi == 2) {
+        // walk the gate rows in half blocks; each block also carries up's rows
+        if (p.R < 8) return -1;
+        p.Rblk = p.R / 2;
+        p.T = sl[0].N;
+        p.nseg = 1;
+      }
+      if (epi == 1)
+        for (int i = 0; i < nseg; ++i) p.res[i] = res[i] + m0 * segs[i].N;
       p.x = x ? x + m0 * K : nullptr;
       p.xg = xg ? xg + m0 * (K / 32) : nullptr;
       p.P = 1;
@@ -869,8 +925,8 @@ int run_gemv_fused(const nsq_segment* segs, int nseg, const float* x, const XGro
           p.xoff[i] = xd->off[i] + m0 * xd->nfull[i] * 4;
         }
       }
-      e = xself ? launch_fused_m<true>(mm, p, blocks, smem, st, &max_clusters)
-                : launch_fused_m<false>(mm, p, blocks, smem, st, &max_clusters);
+      e = xself ? launch_fused_e<true>(epi, mm, p, blocks, smem, st, &max_clusters)
+                : launch_fused_e<false>(epi, mm, p, blocks, smem, st, &max_clusters);
       if (e != static_cast<cudaError_t>(kNoRoom)) break;  // else re-plan with fewer clusters
     }
     if (e != cudaSuccess) return NSQ_ERR_CUDA;

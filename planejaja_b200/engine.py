@@ -127,6 +127,32 @@ class CudaEngine:
         self._sync(sync)
         return outs
 
+    def gemv_swiglu(self, w_gate: torch.Tensor, w_up: torch.Tensor, ggml_type: int, x: torch.Tensor, n: int, k: int,
+                    q6k_layout: int = Q6K_GGML, out: Optional[torch.Tensor] = None, sync: bool = True) -> torch.Tensor:
+        """h[m, n] = silu(x . Wg^T) * (x . Wu^T) in one launch (the FFN input
+        projection with the reference's silu + mul fused in)."""
+        m = x.numel() // k
+        h = out if out is not None else torch.empty(m, n, dtype=torch.float32, device=self.device)
+        x = x.contiguous().float()
+        ws = self.workspace(self.lib.nsq_gemv_workspace_size(m, k))
+        check(self.lib.nsq_gemv_swiglu(_ptr(w_gate), _ptr(w_up), ggml_type, q6k_layout, _ptr(x), _ptr(h), m, n, k,
+                                       _ptr(ws), ws.numel(), self._stream()), "nsq_gemv_swiglu")
+        self._sync(sync)
+        return h
+
+    def gemv_residual(self, w: torch.Tensor, ggml_type: int, x: torch.Tensor, residual: torch.Tensor, n: int, k: int,
+                      q6k_layout: int = Q6K_GGML, out: Optional[torch.Tensor] = None, sync: bool = True) -> torch.Tensor:
+        """y = residual + x . W^T in one launch; `out` may be `residual` (in place)."""
+        m = x.numel() // k
+        y = out if out is not None else torch.empty(m, n, dtype=torch.float32, device=self.device)
+        x = x.contiguous().float()
+        residual = residual.contiguous().float()
+        ws = self.workspace(self.lib.nsq_gemv_workspace_size(m, k))
+        check(self.lib.nsq_gemv_residual(_ptr(w), ggml_type, q6k_layout, _ptr(x), _ptr(residual), _ptr(y), m, n, k,
+                                         _ptr(ws), ws.numel(), self._stream()), "nsq_gemv_residual")
+        self._sync(sync)
+        return y
+
     def prepare(self, x: torch.Tensor, k: int, ws: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Prepare activations once for several GEMVs (q|k|v, gate|up)."""
         m = x.numel() // k

@@ -271,3 +271,50 @@ def test_matmul_f32(eng, oracle):
     c = eng.matmul(torch.tensor([[1., 2.], [3., 4.]], device=eng.device),
                    torch.tensor([[5., 6.], [7., 8.]], device=eng.device), 2, 2, 2)
     assert c.cpu().tolist() == [[19.0, 22.0], [43.0, 50.0]]
+
+
+# ---------------------------------------------------------------- fused epilogues
+def _silu(v):
+    return v * (1.0 / (1.0 + np.exp(-v)))
+
+
+@pytest.mark.parametrize("tid,layout", ALL, ids=IDS)
+@pytest.mark.parametrize("m", [1, 3, 6])
+def test_gemv_swiglu_parity(eng, oracle, tid, layout, m):
+    """h = silu(x Wg^T) * (x Wu^T) in one launch, against the oracle GEMVs
+    composed with the reference's silu and mul (in f64)."""
+    n, k = 300, 2048
+    wg = Q.synthetic_weights(n, k, tid, seed=500 + tid, q6k_layout=layout)
+    wu = Q.synthetic_weights(n, k, tid, seed=600 + tid, q6k_layout=layout)
+    x = Q.synthetic_activations(m, k, seed=700 + m)
+    g = oracle.quant_matmul(wg, tid, x, n, k, layout, threads=8).astype(np.float64)
+    u = oracle.quant_matmul(wu, tid, x, n, k, layout, threads=8).astype(np.float64)
+    ref = _silu(g) * u
+    h = eng.gemv_swiglu(eng.upload(wg), eng.upload(wu), tid, torch.from_numpy(x).to(eng.device), n, k, layout)
+    assert rel_err(h.cpu().numpy(), ref) <= 2 * GEMV_TOL
+
+
+@pytest.mark.parametrize("tid,layout", ALL, ids=IDS)
+@pytest.mark.parametrize("m", [1, 5])
+def test_gemv_residual_parity(eng, oracle, tid, layout, m):
+    n, k = 257, 4096
+    w = Q.synthetic_weights(n, k, tid, seed=800 + tid, q6k_layout=layout)
+    x = Q.synthetic_activations(m, k, seed=801)
+    res = np.random.default_rng(9).standard_normal((m, n)).astype(np.float32)
+    ref = oracle.quant_matmul(w, tid, x, n, k, layout, threads=8).astype(np.float64) + res
+    wd = eng.upload(w)
+    xd = torch.from_numpy(x).to(eng.device)
+    y = eng.gemv_residual(wd, tid, xd, torch.from_numpy(res).to(eng.device), n, k, layout)
+    assert rel_err(y.cpu().numpy(), ref) <= GEMV_TOL
+    # in place: the residual buffer receives the sum
+    buf = torch.from_numpy(res).to(eng.device)
+    eng.gemv_residual(wd, tid, xd, buf, n, k, layout, out=buf)
+    assert rel_err(buf.cpu().numpy(), ref) <= GEMV_TOL
+
+
+def test_gemv_swiglu_rejects_mismatched_pairs(eng):
+    wg = eng.upload(Q.synthetic_weights(64, 512, Q4_K, seed=1))
+    wu = eng.upload(Q.synthetic_weights(64, 512, Q4_K, seed=2))
+    x = torch.zeros(1, 300, device=eng.device)
+    with pytest.raises(_lib.NsqError):  # K % 256
+        eng.gemv_swiglu(wg, wu, Q4_K, x, 64, 300)
