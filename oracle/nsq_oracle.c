@@ -17,6 +17,11 @@
  *   orc_dequant_q4_k        crates/nodestor-inference/src/dequant/q4_k.rs:56-131
  *   orc_dequant_q4_k_avx2   crates/nodestor-inference/src/dequant/simd_x86.rs:84-158
  *                           (timing variant; unfused mul then sub, :131)
+ *   orc_dequant_q5_k (layout NODESTOR)
+ *                           crates/nodestor-inference/src/dequant/q5_k.rs:33-88
+ *   orc_dequant_q5_k (layout GGML)
+ *                           third-party: ggml's Q5_K as implemented by gguf-py
+ *                           0.19.0 gguf/quants.py class Q5_K.dequantize_blocks
  *   orc_dequant_q6_k (layout NODESTOR)
  *                           crates/nodestor-vulkan/shaders/dequant_q6k.comp:50-99
  *   orc_dequant_q6_k (layout GGML)
@@ -48,6 +53,7 @@
 #define NSQ_T_Q8_0 8
 #define NSQ_T_Q4_K 12
 #define NSQ_T_Q6_K 14
+#define NSQ_T_Q5_K 13
 
 #define Q6K_LAYOUT_GGML 0
 #define Q6K_LAYOUT_NODESTOR 1
@@ -192,6 +198,35 @@ void orc_dequant_q4_k_avx2(const uint8_t *raw, int64_t nblocks, float *out) {
 #endif
 }
 
+/*
+ * Q5_K, 176-byte block: d(f16) | dmin(f16) | scales[12] | qh[32] | qs[128].
+ * Weight (chunk c, half h, l) = d * sc(2c+h) * q - dmin * m(2c+h), with
+ * q = nibble h of qs[32c + l] plus 16 * the high bit:
+ *   NODESTOR (q5_k.rs:57-70): bit l%8 of qh[8c + 4h + l/8];
+ *   GGML (gguf-py Q5_K):      bit 2c+h of qh[l].
+ */
+void orc_dequant_q5_k(const uint8_t *raw, int64_t nblocks, float *out, int layout, int fp16_mode) {
+    for (int64_t b = 0; b < nblocks; ++b) {
+        const uint8_t *blk = raw + b * 176;
+        float d = h2f(blk, fp16_mode), dmin = h2f(blk + 2, fp16_mode);
+        const uint8_t *scales = blk + 4, *qh = blk + 16, *qs = blk + 48;
+        float *o = out + b * 256;
+        for (int c = 0; c < 4; ++c) {
+            for (int h = 0; h < 2; ++h) {
+                uint8_t sc, m;
+                get_scale_min_k4(2 * c + h, scales, &sc, &m);
+                float d1 = d * (float)sc, m1 = dmin * (float)m;
+                for (int l = 0; l < 32; ++l) {
+                    uint32_t nib = h ? (uint32_t)(qs[32 * c + l] >> 4) : (uint32_t)(qs[32 * c + l] & 0x0F);
+                    uint32_t hb = layout == Q6K_LAYOUT_NODESTOR ? (qh[8 * c + 4 * h + l / 8] >> (l % 8)) & 1u
+                                                                : (qh[l] >> (2 * c + h)) & 1u;
+                    *o++ = d1 * (float)(nib | (hb << 4)) - m1;
+                }
+            }
+        }
+    }
+}
+
 /* Q6_K, 210-byte block: ql[128] | qh[64] | scales[16] | d(f16) at 208. */
 void orc_dequant_q6_k(const uint8_t *raw, int64_t nblocks, float *out, int layout, int fp16_mode) {
     for (int64_t b = 0; b < nblocks; ++b) {
@@ -234,7 +269,7 @@ void orc_dequant_q6_k(const uint8_t *raw, int64_t nblocks, float *out, int layou
 int64_t orc_block_weights(int type) {
     switch (type) {
     case NSQ_T_Q4_0: case NSQ_T_Q8_0: return 32;
-    case NSQ_T_Q4_K: case NSQ_T_Q6_K: return 256;
+    case NSQ_T_Q4_K: case NSQ_T_Q5_K: case NSQ_T_Q6_K: return 256;
     default: return 0;
     }
 }
@@ -244,6 +279,7 @@ int64_t orc_block_bytes(int type) {
     case NSQ_T_Q4_0: return 18;
     case NSQ_T_Q8_0: return 34;
     case NSQ_T_Q4_K: return 144;
+    case NSQ_T_Q5_K: return 176;
     case NSQ_T_Q6_K: return 210;
     default: return 0;
     }
@@ -255,6 +291,7 @@ int orc_dequant(const uint8_t *raw, int type, int layout, int64_t nblocks, float
     case NSQ_T_Q4_0: orc_dequant_q4_0(raw, nblocks, out, fp16_mode); return 0;
     case NSQ_T_Q8_0: orc_dequant_q8_0(raw, nblocks, out, fp16_mode); return 0;
     case NSQ_T_Q4_K: orc_dequant_q4_k(raw, nblocks, out, fp16_mode); return 0;
+    case NSQ_T_Q5_K: orc_dequant_q5_k(raw, nblocks, out, layout, fp16_mode); return 0;
     case NSQ_T_Q6_K: orc_dequant_q6_k(raw, nblocks, out, layout, fp16_mode); return 0;
     default: return -1;
     }

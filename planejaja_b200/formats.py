@@ -13,11 +13,14 @@ from dataclasses import dataclass
 Q4_0 = 2
 Q8_0 = 8
 Q4_K = 12
+Q5_K = 13
 Q6_K = 14
 
-# Q6_K byte layouts.  GGML is what llama.cpp writes; NODESTOR is the element
-# mapping of the reference's own shader (nodestor/crates/nodestor-vulkan/
-# shaders/dequant_q6k.comp:50-99): same field offsets, different unpacking.
+# Q6_K / Q5_K byte layouts.  GGML is what llama.cpp writes; NODESTOR is the
+# element mapping of the reference's own code (Q6_K: nodestor/crates/
+# nodestor-vulkan/shaders/dequant_q6k.comp:50-99; Q5_K: the high-bit mapping
+# of nodestor/crates/nodestor-inference/src/dequant/q5_k.rs:57-70): same
+# field offsets, different unpacking.
 Q6K_GGML = 0
 Q6K_NODESTOR = 1
 
@@ -42,6 +45,7 @@ FORMATS = {
     Q4_0: BlockFormat("Q4_0", Q4_0, 32, 18),
     Q8_0: BlockFormat("Q8_0", Q8_0, 32, 34),
     Q4_K: BlockFormat("Q4_K", Q4_K, 256, 144),
+    Q5_K: BlockFormat("Q5_K", Q5_K, 256, 176),
     Q6_K: BlockFormat("Q6_K", Q6_K, 256, 210),
 }
 

@@ -11,6 +11,7 @@ Block byte layouts (little-endian, ggml's):
   Q4_0  18 B / 32 w : d f16 | qs u8[16] (lo nibble = w[i], hi = w[i+16])
                                                                y = (q-8)*d
   Q4_K 144 B / 256 w: d f16 | dmin f16 | scales u8[12] | qs u8[128]
+  Q5_K 176 B / 256 w: d f16 | dmin f16 | scales u8[12] | qh u8[32] | qs u8[128]
                       8 sub-blocks of 32, 6-bit scale/min each  y = d*sc*q - dmin*m
   Q6_K 210 B / 256 w: ql u8[128] | qh u8[64] | scales [16] | d f16
                       GGML layout: int8 scales per 16 weights   y = d*sc*(q-32)
@@ -21,7 +22,7 @@ from __future__ import annotations
 
 import numpy as np
 
-from .formats import Q4_0, Q4_K, Q6_K, Q8_0, Q6K_GGML, Q6K_NODESTOR, fmt
+from .formats import Q4_0, Q4_K, Q5_K, Q6_K, Q8_0, Q6K_GGML, Q6K_NODESTOR, fmt
 
 F16_MIN_NORMAL = np.float32(2.0 ** -14)
 
@@ -98,6 +99,50 @@ def quantize_q4_k(w: np.ndarray) -> np.ndarray:
     return out.reshape(-1)
 
 
+def quantize_q5_k(w: np.ndarray, layout: int = Q6K_GGML) -> np.ndarray:
+    """Q5_K: Q4_K's scheme with 5-bit values; qs holds the low nibbles as in
+    Q4_K, qh the high bits in the ggml or the NodeStor mapping."""
+    b = w.reshape(-1, 8, 32).astype(np.float32)
+    nb = b.shape[0]
+    lo = np.minimum(b.min(axis=2), 0.0)
+    hi = b.max(axis=2)
+    scale = (hi - lo) / 31.0
+    mins = -lo
+    d = _f16_normal(scale.max(axis=1) / 63.0)
+    dmin = _f16_normal(mins.max(axis=1) / 63.0)
+    df, dmf = d.astype(np.float32)[:, None], dmin.astype(np.float32)[:, None]
+    sc = np.clip(np.rint(scale / df), 0, 63).astype(np.uint8)
+    mn = np.clip(np.rint(mins / dmf), 0, 63).astype(np.uint8)
+    d1 = (df * sc.astype(np.float32))[:, :, None]
+    m1 = (dmf * mn.astype(np.float32))[:, :, None]
+    safe = np.where(d1 > 0, d1, 1.0)
+    q = np.where(d1 > 0, np.clip(np.rint((b + m1) / safe), 0, 31), 0).astype(np.uint8)  # [nb, 8 sub-blocks, 32]
+    low = q & 15
+    qs = low[:, 0::2, :] | (low[:, 1::2, :] << 4)  # [nb, 4 chunks, 32]
+    hbit = (q >> 4) & 1                               # sub-block 2c+h, element l
+    if layout == Q6K_GGML:
+        # qh[l] bit (2c + h) = high bit of sub-block 2c + h, element l
+        qh = np.zeros((nb, 32), np.uint8)
+        for s8 in range(8):
+            qh |= (hbit[:, s8, :] << s8).astype(np.uint8)
+    elif layout == Q6K_NODESTOR:
+        # qh[8c + 4h + l/8] bit (l % 8)
+        bits = hbit.reshape(nb, 4, 2, 4, 8)  # [nb, c, h, l/8, l%8]
+        qh = np.zeros((nb, 4, 2, 4), np.uint8)
+        for t in range(8):
+            qh |= (bits[..., t] << t).astype(np.uint8)
+        qh = qh.reshape(nb, 32)
+    else:
+        raise ValueError(f"unknown Q5_K layout {layout}")
+    out = np.empty((nb, 176), np.uint8)
+    out[:, 0:2] = _f16_bytes(d)
+    out[:, 2:4] = _f16_bytes(dmin)
+    out[:, 4:16] = _pack_q4k_scales(sc, mn)
+    out[:, 16:48] = qh
+    out[:, 48:] = qs.reshape(nb, 128)
+    return out.reshape(-1)
+
+
 def _q6k_pack_ggml(q: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
     """q: [nb, 256] uint8 in 0..63 in element order -> (ql[nb,128], qh[nb,64])."""
     nb = q.shape[0]
@@ -162,6 +207,8 @@ def quantize(w: np.ndarray, type_id: int, q6k_layout: int = Q6K_GGML) -> np.ndar
         return quantize_q4_0(w)
     if type_id == Q4_K:
         return quantize_q4_k(w)
+    if type_id == Q5_K:
+        return quantize_q5_k(w, q6k_layout)
     if type_id == Q6_K:
         return quantize_q6_k(w, q6k_layout)
     raise ValueError(f"unsupported type {type_id}")

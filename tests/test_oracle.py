@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 
 from planejaja_b200 import quantize as Q
-from planejaja_b200.formats import Q4_0, Q4_K, Q6_K, Q8_0, Q6K_GGML, Q6K_NODESTOR
+from planejaja_b200.formats import Q4_0, Q4_K, Q5_K, Q6_K, Q8_0, Q6K_GGML, Q6K_NODESTOR
 
 
 def bits(a):
@@ -75,12 +75,26 @@ def test_q8_reference_known_answers(oracle, golden):
 
 # ---- every format against the golden vectors ----
 @pytest.mark.parametrize("name,tid,layout", [
-    ("Q4_0", Q4_0, 0), ("Q8_0", Q8_0, 0), ("Q4_K", Q4_K, 0), ("Q6_K", Q6_K, Q6K_GGML),
-    ("Q6_K_NODESTOR", Q6_K, Q6K_NODESTOR)])
+    ("Q4_0", Q4_0, 0), ("Q8_0", Q8_0, 0), ("Q4_K", Q4_K, 0), ("Q5_K", Q5_K, Q6K_GGML),
+    ("Q5_K_NODESTOR", Q5_K, Q6K_NODESTOR), ("Q6_K", Q6_K, Q6K_GGML), ("Q6_K_NODESTOR", Q6_K, Q6K_NODESTOR)])
 def test_oracle_bit_exact_vs_golden(oracle, golden, name, tid, layout):
     raw, ref = golden[f"{name}_raw"], golden[f"{name}_f32"]
     out = oracle.dequant(raw, tid, layout)
     assert np.array_equal(bits(out), bits(ref))
+
+
+def test_q5k_reference_known_answers(oracle, golden):
+    """q5_k.rs unit tests: zero weights; nibble 15 + high bit = 31 with
+    dmin = 0 gives only non-negative weights (scale 1 on sub-blocks 0..3)."""
+    out = oracle.dequant(golden["kat_q5k_zero_raw"], Q5_K, Q6K_NODESTOR)
+    assert out.size == 256 and np.all(np.isfinite(out)) and np.all(np.abs(out) < 1e-4)
+    out = oracle.dequant(golden["kat_q5k_high_raw"], Q5_K, Q6K_NODESTOR)
+    assert np.all(out >= 0) and np.all(out[:128] == 31.0)
+
+
+def test_q5k_layouts_differ(oracle, golden):
+    raw = golden["Q5_K_raw"]
+    assert not np.array_equal(oracle.dequant(raw, Q5_K, Q6K_GGML), oracle.dequant(raw, Q5_K, Q6K_NODESTOR))
 
 
 def test_q6k_layouts_differ(oracle, golden):
