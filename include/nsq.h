@@ -12,7 +12,7 @@
  *     ggml_type is the GGUF/ggml type id: 2 = Q4_0, 8 = Q8_0, 12 = Q4_K,
  *     14 = Q6_K.  The weight pointer must be 16-byte aligned (GGUF tensor
  *     data is 32-byte aligned in the file; cudaMalloc gives 256).
- *   - q6k_layout selects the meaning of Q6_K bytes: NSQ_Q6K_GGML (what
+ *   - q6k_layout selects the meaning of Q6_K and Q5_K bytes: NSQ_Q6K_GGML (what
  *     llama.cpp writes) or NSQ_Q6K_NODESTOR (the element mapping of the
  *     reference shader nodestor/crates/nodestor-vulkan/shaders/
  *     dequant_q6k.comp:50-99).  Ignored for the other types.
@@ -53,6 +53,7 @@ extern "C" {
 #define NSQ_TYPE_Q4_0 2
 #define NSQ_TYPE_Q8_0 8
 #define NSQ_TYPE_Q4_K 12
+#define NSQ_TYPE_Q5_K 13
 #define NSQ_TYPE_Q6_K 14
 
 #define NSQ_Q6K_GGML 0

@@ -56,7 +56,7 @@ static DevInfo dev_info() {
 }
 
 static bool type_ok(int t) {
-  return t == NSQ_TYPE_Q4_0 || t == NSQ_TYPE_Q8_0 || t == NSQ_TYPE_Q4_K || t == NSQ_TYPE_Q6_K;
+  return t == NSQ_TYPE_Q4_0 || t == NSQ_TYPE_Q8_0 || t == NSQ_TYPE_Q4_K || t == NSQ_TYPE_Q5_K || t == NSQ_TYPE_Q6_K;
 }
 
 static int check_device(DevInfo& di) {
@@ -68,7 +68,8 @@ static int check_device(DevInfo& di) {
 
 static int check_weights(const void* w, int type, int layout, int64_t K) {
   if (!type_ok(type)) return NSQ_ERR_TYPE;
-  if (type == NSQ_TYPE_Q6_K && layout != NSQ_Q6K_GGML && layout != NSQ_Q6K_NODESTOR) return NSQ_ERR_TYPE;
+  if ((type == NSQ_TYPE_Q6_K || type == NSQ_TYPE_Q5_K) && layout != NSQ_Q6K_GGML && layout != NSQ_Q6K_NODESTOR)
+    return NSQ_ERR_TYPE;
   if (!w) return NSQ_ERR_NULL;
   if (reinterpret_cast<uintptr_t>(w) & 15) return NSQ_ERR_ALIGN;
   const int64_t qk = nsq_block_weights(type);
@@ -105,6 +106,7 @@ int64_t nsq_block_bytes(int ggml_type) {
     case NSQ_TYPE_Q4_0: return 18;
     case NSQ_TYPE_Q8_0: return 34;
     case NSQ_TYPE_Q4_K: return 144;
+    case NSQ_TYPE_Q5_K: return 176;
     case NSQ_TYPE_Q6_K: return 210;
     default: return 0;
   }
@@ -115,6 +117,7 @@ int64_t nsq_block_weights(int ggml_type) {
     case NSQ_TYPE_Q4_0:
     case NSQ_TYPE_Q8_0: return 32;
     case NSQ_TYPE_Q4_K:
+    case NSQ_TYPE_Q5_K: return 256;
     case NSQ_TYPE_Q6_K: return 256;
     default: return 0;
   }

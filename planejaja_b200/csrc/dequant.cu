@@ -9,6 +9,7 @@
 //   Q8_0  y = d*q                 crates/nodestor-inference/src/dequant/q8_0.rs:14-28
 //   Q4_0  y = (q-8)*d             crates/nodestor-vulkan/shaders/dequant_q4.comp:40-61
 //   Q4_K  y = (d*sc)*q - dmin*m   crates/nodestor-inference/src/dequant/q4_k.rs:75-131
+//   Q5_K  y = (d*sc)*q - dmin*m   q5_k.rs:33-88 (NODESTOR high bits) or ggml's layout
 //   Q6_K  y = (d*s)*q             dequant_q6k.comp:50-99 (NODESTOR) or ggml's layout
 #include "nsq_common.cuh"
 
@@ -30,6 +31,29 @@ __device__ __forceinline__ float q4k_value(const uint8_t* blk, int j, int l) {
   const uint32_t q = (j & 1) ? (qb >> 4) : (qb & 0xF);
   const float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)mn);
   return __fsub_rn(__fmul_rn(d1, (float)q), m1);
+}
+
+// Q5_K [d][dmin][scales 12][qh 32][qs 128]: sub-block j (0..7), element l:
+// nibble (j & 1) of qs[32 (j >> 1) + l] plus 16 * the high bit, which is bit
+// j of qh[l] (ggml) or bit l % 8 of qh[8 (j >> 1) + 4 (j & 1) + l / 8]
+// (NODESTOR, q5_k.rs:57-70).
+__device__ __forceinline__ float q5k_value(const uint8_t* blk, int layout, int j, int l) {
+  const uint8_t* s = blk + 4;
+  uint32_t sc, mn;
+  if (j < 4) {
+    sc = s[j] & 63;
+    mn = s[j + 4] & 63;
+  } else {
+    sc = (s[j + 4] & 0xF) | ((s[j - 4] >> 6) << 4);
+    mn = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+  }
+  const float d = h2f(ld_u16(blk)), dmin = h2f(ld_u16(blk + 2));
+  const uint32_t qb = blk[48 + 32 * (j >> 1) + l];
+  const uint32_t nib = (j & 1) ? (qb >> 4) : (qb & 0xF);
+  const uint32_t hb = layout == NSQ_Q6K_NODESTOR ? (blk[16 + 8 * (j >> 1) + 4 * (j & 1) + (l >> 3)] >> (l & 7)) & 1
+                                                 : (blk[16 + l] >> j) & 1;
+  const float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)mn);
+  return __fsub_rn(__fmul_rn(d1, (float)(nib | (hb << 4))), m1);
 }
 
 __device__ __forceinline__ float q6k_value(const uint8_t* blk, int layout, int i) {
@@ -71,6 +95,9 @@ __global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict_
     } else if constexpr (TYPE == NSQ_TYPE_Q4_K) {
       const uint8_t* blk = w + (g >> 3) * 144;
       v = q4k_value(blk, (int)(g & 7), lane);
+    } else if constexpr (TYPE == NSQ_TYPE_Q5_K) {
+      const uint8_t* blk = w + (g >> 3) * 176;
+      v = q5k_value(blk, layout, (int)(g & 7), lane);
     } else {
       const uint8_t* blk = w + (g >> 3) * 210;
       v = q6k_value(blk, layout, (int)(g & 7) * 32 + lane);
@@ -106,6 +133,7 @@ cudaError_t launch_dequant(const uint8_t* w, int type, int layout, int out_dtype
     case NSQ_TYPE_Q4_0: return launch_dequant_t<NSQ_TYPE_Q4_0>(w, layout, out_dtype, out, n_groups, st, num_sms);
     case NSQ_TYPE_Q8_0: return launch_dequant_t<NSQ_TYPE_Q8_0>(w, layout, out_dtype, out, n_groups, st, num_sms);
     case NSQ_TYPE_Q4_K: return launch_dequant_t<NSQ_TYPE_Q4_K>(w, layout, out_dtype, out, n_groups, st, num_sms);
+    case NSQ_TYPE_Q5_K: return launch_dequant_t<NSQ_TYPE_Q5_K>(w, layout, out_dtype, out, n_groups, st, num_sms);
     case NSQ_TYPE_Q6_K: return launch_dequant_t<NSQ_TYPE_Q6_K>(w, layout, out_dtype, out, n_groups, st, num_sms);
     default: return cudaErrorInvalidValue;
   }

@@ -57,6 +57,7 @@ constexpr int GEMM_DQ_THREADS = 512;
 // even offset, so their copies carry up to 15 bytes of slack on each side.
 template <int TYPE> struct RawCol;
 template <> struct RawCol<NSQ_TYPE_Q4_K> { static constexpr int bytes = 144, pitch = 144; };
+template <> struct RawCol<NSQ_TYPE_Q5_K> { static constexpr int bytes = 176, pitch = 176; };
 template <> struct RawCol<NSQ_TYPE_Q4_0> { static constexpr int bytes = 144, pitch = 144; };
 template <> struct RawCol<NSQ_TYPE_Q8_0> { static constexpr int bytes = 272, pitch = 272; };
 template <> struct RawCol<NSQ_TYPE_Q6_K> { static constexpr int bytes = 210, pitch = 240; };
@@ -190,6 +191,61 @@ __device__ __forceinline__ void dequant_col_kblock(const uint8_t* raw, int q, in
       for (int b = 0; b < 4; ++b) {
         v[4 * w2 + b] = __fmaf_rn(d1, (float)((lo >> (8 * b)) & 0xFF), -m1);
         v[8 + 4 * w2 + b] = __fmaf_rn(d2, (float)((hi >> (8 * b)) & 0xFF), -m2);
+      }
+    }
+    chunk[0] = qq;
+    chunk[1] = 4 + qq;
+  } else if constexpr (TYPE == NSQ_TYPE_Q5_K) {
+    // Q4_K's nibbles (qs at byte 48) plus one high bit per weight from
+    // qh[32]: ggml: bit 2q (low) / 2q+1 (high) of qh[8qq + i]; NODESTOR
+    // (q5_k.rs:57-70): bit i of qh[8q + qq] (low) / qh[8q + 4 + qq] (high)
+    const uint4 hdr = *reinterpret_cast<const uint4*>(raw);
+    const uint2 qv = *reinterpret_cast<const uint2*>(raw + 48 + 32 * q + 8 * qq);
+    const float d = h2f((uint16_t)(hdr.x & 0xFFFF)), dmin = h2f((uint16_t)(hdr.x >> 16));
+    uint32_t sc[2], mn[2];
+#pragma unroll
+    for (int s2 = 0; s2 < 2; ++s2) {
+      const int j = 2 * q + s2;
+      if (j < 4) {
+        sc[s2] = (hdr.y >> (8 * j)) & 63;
+        mn[s2] = (hdr.z >> (8 * j)) & 63;
+      } else {
+        const int sh = 8 * (j - 4);
+        const uint32_t b2 = (hdr.w >> sh) & 0xFF, b0 = (hdr.y >> sh) & 0xFF, b1 = (hdr.z >> sh) & 0xFF;
+        sc[s2] = (b2 & 0xF) | ((b0 >> 6) << 4);
+        mn[s2] = (b2 >> 4) | ((b1 >> 6) << 4);
+      }
+    }
+    const float d1 = __fmul_rn(d, (float)sc[0]), m1 = __fmul_rn(dmin, (float)mn[0]);
+    const float d2 = __fmul_rn(d, (float)sc[1]), m2 = __fmul_rn(dmin, (float)mn[1]);
+    uint32_t hlo[8], hhi[8];
+    if constexpr (LAYOUT == NSQ_Q6K_NODESTOR) {
+      const uint32_t bl = raw[16 + 8 * q + qq], bh = raw[16 + 8 * q + 4 + qq];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        hlo[i] = (bl >> i) & 1;
+        hhi[i] = (bh >> i) & 1;
+      }
+    } else {
+      const uint2 hv = *reinterpret_cast<const uint2*>(raw + 16 + 8 * qq);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t byte = ((i < 4 ? hv.x : hv.y) >> (8 * (i & 3))) & 0xFF;
+        hlo[i] = (byte >> (2 * q)) & 1;
+        hhi[i] = (byte >> (2 * q + 1)) & 1;
+      }
+    }
+    // d1*q is exact (<= 22 significant bits): fma rounds once, like d1*q - m1
+#pragma unroll
+    for (int w2 = 0; w2 < 2; ++w2) {
+      const uint32_t wv = w2 ? qv.y : qv.x;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const int i = 4 * w2 + b;
+        const uint32_t lo = ((wv >> (8 * b)) & 0x0F) | (hlo[i] << 4);
+        const uint32_t hi = ((wv >> (8 * b + 4)) & 0x0F) | (hhi[i] << 4);
+        v[i] = __fmaf_rn(d1, (float)lo, -m1);
+        v[8 + i] = __fmaf_rn(d2, (float)hi, -m2);
       }
     }
     chunk[0] = qq;
@@ -706,6 +762,9 @@ int run_gemm_bf16(const uint8_t* w, int type, int layout, const void* x, void* y
     case NSQ_TYPE_Q4_0: return run_gemm_t<NSQ_TYPE_Q4_0, 0>(x, p, tok, st, num_sms);
     case NSQ_TYPE_Q8_0: return run_gemm_t<NSQ_TYPE_Q8_0, 0>(x, p, tok, st, num_sms);
     case NSQ_TYPE_Q4_K: return run_gemm_t<NSQ_TYPE_Q4_K, 0>(x, p, tok, st, num_sms);
+    case NSQ_TYPE_Q5_K:
+      if (layout == NSQ_Q6K_NODESTOR) return run_gemm_t<NSQ_TYPE_Q5_K, NSQ_Q6K_NODESTOR>(x, p, tok, st, num_sms);
+      return run_gemm_t<NSQ_TYPE_Q5_K, NSQ_Q6K_GGML>(x, p, tok, st, num_sms);
     case NSQ_TYPE_Q6_K:
       if (layout == NSQ_Q6K_NODESTOR) return run_gemm_t<NSQ_TYPE_Q6_K, NSQ_Q6K_NODESTOR>(x, p, tok, st, num_sms);
       return run_gemm_t<NSQ_TYPE_Q6_K, NSQ_Q6K_GGML>(x, p, tok, st, num_sms);

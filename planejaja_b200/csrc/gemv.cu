@@ -194,6 +194,54 @@ struct Unit<NSQ_TYPE_Q4_K, LAYOUT> {
   }
 };
 
+// 4 high bits (one per byte, for 4 consecutive weights) from a nibble.
+
+template <int LAYOUT>
+struct Unit<NSQ_TYPE_Q5_K, LAYOUT> {
+  // Q4_K's units (qs at byte 48) with the fifth bit of every weight from
+  // qh[32]: ggml: bit j of qh[l]; NODESTOR (q5_k.rs:57-70): bit l%8 of
+  // qh[8(j>>1) + 4(j&1) + l/8], j the sub-block, l the element
+  static constexpr int NG = 2, UPB = 4, OFF = 0;
+  static constexpr bool SIGNED = false;
+  __device__ static int64_t group(int64_t u, int gi) { return 2 * u + gi; }
+  __device__ static void decode(const uint8_t* blk, int p, DGroup (&g)[NG]) {
+    const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
+    const float d = h2f((uint16_t)(hdr.x & 0xFFFF)), dmin = h2f((uint16_t)(hdr.x >> 16));
+    uint32_t sc0, m0, sc1, m1;
+    Unit<NSQ_TYPE_Q4_K, 0>::scale_min(hdr.y, hdr.z, hdr.w, 2 * p, sc0, m0);
+    Unit<NSQ_TYPE_Q4_K, 0>::scale_min(hdr.y, hdr.z, hdr.w, 2 * p + 1, sc1, m1);
+    const uint4 qa = *reinterpret_cast<const uint4*>(blk + 48 + 32 * p);
+    const uint4 qb = *reinterpret_cast<const uint4*>(blk + 64 + 32 * p);
+    const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+    uint32_t hl[8], hh[8];
+    if constexpr (LAYOUT == NSQ_Q6K_NODESTOR) {
+      const uint2 h = *reinterpret_cast<const uint2*>(blk + 16 + 8 * p);  // bytes 8p .. 8p+7
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        hl[i] = spread4(((h.x >> (8 * (i >> 1))) >> (4 * (i & 1))) & 0xF);
+        hh[i] = spread4(((h.y >> (8 * (i >> 1))) >> (4 * (i & 1))) & 0xF);
+      }
+    } else {
+      const uint4 ha = *reinterpret_cast<const uint4*>(blk + 16), hb = *reinterpret_cast<const uint4*>(blk + 32);
+      const uint32_t hw[8] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        hl[i] = (hw[i] >> (2 * p)) & 0x01010101u;
+        hh[i] = (hw[i] >> (2 * p + 1)) & 0x01010101u;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      g[0].q[i] = (qw[i] & 0x0F0F0F0Fu) | (hl[i] << 4);
+      g[1].q[i] = ((qw[i] >> 4) & 0x0F0F0F0Fu) | (hh[i] << 4);
+    }
+    g[0].a0 = g[0].a1 = d * (float)sc0;
+    g[0].bmin = dmin * (float)m0;
+    g[1].a0 = g[1].a1 = d * (float)sc1;
+    g[1].bmin = dmin * (float)m1;
+  }
+};
+
 template <>
 struct Unit<NSQ_TYPE_Q6_K, NSQ_Q6K_GGML> {
   // unit (n, jj), ub = 2n + jj: groups j = jj and j = jj + 2 of half n share
@@ -570,6 +618,10 @@ int run_gemv(const uint8_t* w, int type, int layout, const XGroup* xg, float* y,
     case NSQ_TYPE_Q4_0: return run_gemv_t<NSQ_TYPE_Q4_0, 0>(w, xg, y, M, N, K, st, num_sms);
     case NSQ_TYPE_Q8_0: return run_gemv_t<NSQ_TYPE_Q8_0, 0>(w, xg, y, M, N, K, st, num_sms);
     case NSQ_TYPE_Q4_K: return run_gemv_t<NSQ_TYPE_Q4_K, 0>(w, xg, y, M, N, K, st, num_sms);
+    case NSQ_TYPE_Q5_K:
+      if (layout == NSQ_Q6K_NODESTOR)
+        return run_gemv_t<NSQ_TYPE_Q5_K, NSQ_Q6K_NODESTOR>(w, xg, y, M, N, K, st, num_sms);
+      return run_gemv_t<NSQ_TYPE_Q5_K, NSQ_Q6K_GGML>(w, xg, y, M, N, K, st, num_sms);
     case NSQ_TYPE_Q6_K:
       if (layout == NSQ_Q6K_NODESTOR)
         return run_gemv_t<NSQ_TYPE_Q6_K, NSQ_Q6K_NODESTOR>(w, xg, y, M, N, K, st, num_sms);

@@ -33,7 +33,7 @@ constexpr int kMmaConsumers = 4;
 constexpr int kMmaThreads = 32 * (1 + kMmaConsumers);
 constexpr int kMmaRows = 16 * kMmaConsumers;  // rows per block
 
-enum : int { kMQ4K = 0, kMQ6KG = 1, kMQ6KN = 2, kMQ40 = 3, kMQ80 = 4, kMMixed = -1 };
+enum : int { kMQ4K = 0, kMQ6KG = 1, kMQ6KN = 2, kMQ40 = 3, kMQ80 = 4, kMQ5KG = 5, kMQ5KN = 6, kMMixed = -1 };
 
 struct MSeg {
   const uint8_t* w;
@@ -193,6 +193,71 @@ struct MmaPieces {
     }
   }
 
+  // Q5_K [d][dmin][scales 12][qh 32][qs 128]: Q4_K's nibbles at byte 48 and
+  // a fifth bit per weight, element l of sub-block j: ggml bit j of qh[l];
+  // NodeStor (q5_k.rs:57-70) bit l%8 of qh[8(j>>1) + 4(j&1) + l/8].
+  template <int LAYOUT>
+  __device__ static void q5k(const uint8_t* p0, const uint8_t* p1, const uint8_t* xp, int xstride, int M, int g,
+                             int t, float (&acc)[NOCT][4]) {
+    const uint4 h0 = *reinterpret_cast<const uint4*>(p0), h1 = *reinterpret_cast<const uint4*>(p1);
+    const float d0 = h2f((uint16_t)(h0.x & 0xFFFF)), m0 = h2f((uint16_t)(h0.x >> 16));
+    const float d1 = h2f((uint16_t)(h1.x & 0xFFFF)), m1 = h2f((uint16_t)(h1.x >> 16));
+    const uint32_t sl0 = h0.y & 0x3F3F3F3Fu, ml0 = h0.z & 0x3F3F3F3Fu;
+    const uint32_t sh0 = (h0.w & 0x0F0F0F0Fu) | ((h0.y >> 2) & 0x30303030u);
+    const uint32_t mh0 = ((h0.w >> 4) & 0x0F0F0F0Fu) | ((h0.z >> 2) & 0x30303030u);
+    const uint32_t sl1 = h1.y & 0x3F3F3F3Fu, ml1 = h1.z & 0x3F3F3F3Fu;
+    const uint32_t sh1 = (h1.w & 0x0F0F0F0Fu) | ((h1.y >> 2) & 0x30303030u);
+    const uint32_t mh1 = ((h1.w >> 4) & 0x0F0F0F0Fu) | ((h1.z >> 2) & 0x30303030u);
+    // ggml: the qh words of elements 4t.. and 16+4t.., shared by all sub-blocks
+    uint32_t q00 = 0, q01 = 0, q10 = 0, q11 = 0;
+    if constexpr (LAYOUT != NSQ_Q6K_NODESTOR) {
+      q00 = lds32(p0 + 16 + 4 * t); q01 = lds32(p1 + 16 + 4 * t);
+      q10 = lds32(p0 + 32 + 4 * t); q11 = lds32(p1 + 32 + 4 * t);
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const uint32_t w00 = lds32(p0 + 48 + 32 * c + 4 * t), w01 = lds32(p1 + 48 + 32 * c + 4 * t);
+      const uint32_t w10 = lds32(p0 + 64 + 32 * c + 4 * t), w11 = lds32(p1 + 64 + 32 * c + 4 * t);
+#pragma unroll
+      for (int nib = 0; nib < 2; ++nib) {
+        const int sb = 2 * c + nib;
+        const int sh = 4 * nib;
+        uint32_t hb[4];
+        if constexpr (LAYOUT == NSQ_Q6K_NODESTOR) {
+          const int hb0 = 16 + 8 * c + 4 * nib + (t >> 1), ns = 4 * (t & 1);
+          hb[0] = spread4(((uint32_t)p0[hb0] >> ns) & 0xF);
+          hb[1] = spread4(((uint32_t)p1[hb0] >> ns) & 0xF);
+          hb[2] = spread4(((uint32_t)p0[hb0 + 2] >> ns) & 0xF);
+          hb[3] = spread4(((uint32_t)p1[hb0 + 2] >> ns) & 0xF);
+        } else {
+          hb[0] = (q00 >> sb) & 0x01010101u;
+          hb[1] = (q01 >> sb) & 0x01010101u;
+          hb[2] = (q10 >> sb) & 0x01010101u;
+          hb[3] = (q11 >> sb) & 0x01010101u;
+        }
+        const uint32_t a[4] = {((w00 >> sh) & 0x0F0F0F0Fu) | (hb[0] << 4), ((w01 >> sh) & 0x0F0F0F0Fu) | (hb[1] << 4),
+                               ((w10 >> sh) & 0x0F0F0F0Fu) | (hb[2] << 4), ((w11 >> sh) & 0x0F0F0F0Fu) | (hb[3] << 4)};
+        const int bs = 8 * (sb & 3);
+        const uint32_t s0w = sb < 4 ? sl0 : sh0, m0w = sb < 4 ? ml0 : mh0;
+        const uint32_t s1w = sb < 4 ? sl1 : sh1, m1w = sb < 4 ? ml1 : mh1;
+        const float a0 = d0 * (float)((s0w >> bs) & 0xFF), b0 = m0 * (float)((m0w >> bs) & 0xFF);
+        const float a1 = d1 * (float)((s1w >> bs) & 0xFF), b1 = m1 * (float)((m1w >> bs) & 0xFF);
+#pragma unroll
+        for (int o = 0; o < NOCT; ++o) {
+          const int tb = 8 * o + g, te = 8 * o + 2 * t;
+          uint32_t bh0, bh1, bl0, bl1;
+          b_k32(xp + (size_t)tb * xstride + sb * 80, tb < M, t, bh0, bh1, bl0, bl1);
+          int dh[4], dl[4];
+          mma_k32_u8s8(dh, a, bh0, bh1);
+          mma_k32_u8u8(dl, a, bl0, bl1);
+          const TokG e0 = tok_group(xp + (size_t)te * xstride + sb * 80, te < M);
+          const TokG e1 = tok_group(xp + (size_t)(te + 1) * xstride + sb * 80, te + 1 < M);
+          epi(acc[o], dh, dl, a0, b0, a1, b1, e0, e1, e0.t0 + e0.t1, e1.t0 + e1.t1);
+        }
+      }
+    }
+  }
+
   // Q6_K, ggml layout: element 128n + 32j + l: ql[64n + 32(j&1) + l] nibble
   // (j>>1), qh[32n + l] bits 2j; int8 scale sc[(128n + 32j + l) / 16].
   __device__ static void q6k_ggml(const uint8_t* p0, const uint8_t* p1, const uint8_t* xp, int xstride, int M, int g,
@@ -329,6 +394,8 @@ __device__ __forceinline__ void mma_piece(int code, const uint8_t* p0, const uin
     case kMQ6KG: MmaPieces<NOCT>::q6k_ggml(p0, p1, xp, xstride, M, g, t, acc); break;
     case kMQ6KN: MmaPieces<NOCT>::q6k_nodestor(p0, p1, xp, xstride, M, g, t, acc); break;
     case kMQ40: MmaPieces<NOCT>::q40(p0, p1, xp, xstride, M, g, t, acc); break;
+    case kMQ5KG: MmaPieces<NOCT>::template q5k<NSQ_Q6K_GGML>(p0, p1, xp, xstride, M, g, t, acc); break;
+    case kMQ5KN: MmaPieces<NOCT>::template q5k<NSQ_Q6K_NODESTOR>(p0, p1, xp, xstride, M, g, t, acc); break;
     default: MmaPieces<NOCT>::q80(p0, p1, xp, xstride, M, g, t, acc); break;
   }
 }
@@ -552,6 +619,7 @@ static int mcode(int type, int layout) {
     case NSQ_TYPE_Q6_K: return layout == NSQ_Q6K_NODESTOR ? kMQ6KN : kMQ6KG;
     case NSQ_TYPE_Q4_0: return kMQ40;
     case NSQ_TYPE_Q8_0: return kMQ80;
+    case NSQ_TYPE_Q5_K: return layout == NSQ_Q6K_NODESTOR ? kMQ5KN : kMQ5KG;
     default: return -2;
   }
 }
@@ -559,6 +627,7 @@ static int mpiece_bytes(int type) {
   switch (type) {
     case NSQ_TYPE_Q4_K: return 144;
     case NSQ_TYPE_Q6_K: return 210;
+    case NSQ_TYPE_Q5_K: return 176;
     case NSQ_TYPE_Q4_0: return 144;
     case NSQ_TYPE_Q8_0: return 272;
     default: return 0;
@@ -691,6 +760,8 @@ static cudaError_t launch_mma_c(const MmaParams& p, int blocks, size_t smem, cud
     case kMQ6KN: return launch_mma<NOCT, kMQ6KN>(p, blocks, smem, st);
     case kMQ40: return launch_mma<NOCT, kMQ40>(p, blocks, smem, st);
     case kMQ80: return launch_mma<NOCT, kMQ80>(p, blocks, smem, st);
+    case kMQ5KG: return launch_mma<NOCT, kMQ5KG>(p, blocks, smem, st);
+    case kMQ5KN: return launch_mma<NOCT, kMQ5KN>(p, blocks, smem, st);
     default: return launch_mma<NOCT, kMMixed>(p, blocks, smem, st);
   }
 }

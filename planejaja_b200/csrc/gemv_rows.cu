@@ -133,6 +133,64 @@ struct Piece<NSQ_TYPE_Q4_K, LAYOUT, M> {
   }
 };
 
+// Q5_K super-block [d][dmin][scales 12][qh 32][qs 128]: Q4_K's nibbles (at
+// byte 48) plus the fifth bit of each weight: ggml: bit j of qh[l];
+// NODESTOR (q5_k.rs:57-70): bit l%8 of qh[8(j>>1) + 4(j&1) + l/8].
+template <int LAYOUT, int M>
+struct Piece<NSQ_TYPE_Q5_K, LAYOUT, M> {
+  __device__ static void run(const uint8_t* pc, const uint8_t* xp, int xstride, float (&acc)[M]) {
+    const uint4 hdr = *reinterpret_cast<const uint4*>(pc);
+    const float d = h2f((uint16_t)(hdr.x & 0xFFFF)), dmin = h2f((uint16_t)(hdr.x >> 16));
+    const uint32_t S0 = hdr.y, S1 = hdr.z, S2 = hdr.w;
+    const uint32_t sclo = S0 & 0x3F3F3F3Fu, mnlo = S1 & 0x3F3F3F3Fu;
+    const uint32_t schi = (S2 & 0x0F0F0F0Fu) | ((S0 >> 2) & 0x30303030u);
+    const uint32_t mnhi = ((S2 >> 4) & 0x0F0F0F0Fu) | ((S1 >> 2) & 0x30303030u);
+    uint32_t hw[8];
+    if constexpr (LAYOUT != NSQ_Q6K_NODESTOR) {
+      const uint4 ha = *reinterpret_cast<const uint4*>(pc + 16), hb = *reinterpret_cast<const uint4*>(pc + 32);
+      hw[0] = ha.x; hw[1] = ha.y; hw[2] = ha.z; hw[3] = ha.w;
+      hw[4] = hb.x; hw[5] = hb.y; hw[6] = hb.z; hw[7] = hb.w;
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const uint32_t scw = c < 2 ? sclo : schi, mnw = c < 2 ? mnlo : mnhi;
+      const int sh0 = 16 * (c & 1), sh1 = sh0 + 8;
+      const float a0 = d * (float)((scw >> sh0) & 0xFF), b0 = dmin * (float)((mnw >> sh0) & 0xFF);
+      const float a1 = d * (float)((scw >> sh1) & 0xFF), b1 = dmin * (float)((mnw >> sh1) & 0xFF);
+      const uint4 qa = *reinterpret_cast<const uint4*>(pc + 48 + 32 * c);
+      const uint4 qb = *reinterpret_cast<const uint4*>(pc + 64 + 32 * c);
+      const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+      uint32_t ql[8], qh[8];
+      if constexpr (LAYOUT == NSQ_Q6K_NODESTOR) {
+        const uint2 h = *reinterpret_cast<const uint2*>(pc + 16 + 8 * c);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          ql[i] = (qw[i] & 0x0F0F0F0Fu) | (spread4(((h.x >> (8 * (i >> 1))) >> (4 * (i & 1))) & 0xF) << 4);
+          qh[i] = ((qw[i] >> 4) & 0x0F0F0F0Fu) | (spread4(((h.y >> (8 * (i >> 1))) >> (4 * (i & 1))) & 0xF) << 4);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          ql[i] = (qw[i] & 0x0F0F0F0Fu) | (((hw[i] >> (2 * c)) & 0x01010101u) << 4);
+          qh[i] = ((qw[i] >> 4) & 0x0F0F0F0Fu) | (((hw[i] >> (2 * c + 1)) & 0x01010101u) << 4);
+        }
+      }
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        XG x0, x1;
+        lds_xg(xp + m * xstride + (2 * c) * 80, x0);
+        lds_xg(xp + m * xstride + (2 * c + 1) * 80, x1);
+        int s00, s01, s10, s11;
+        dot8<false>(ql, x0, s00, s01);
+        dot8<false>(qh, x1, s10, s11);
+        float r = x0.sx * fmaf(a0, (float)(s00 + s01), -b0 * (float)(x0.t0 + x0.t1));
+        r = fmaf(x1.sx, fmaf(a1, (float)(s10 + s11), -b1 * (float)(x1.t0 + x1.t1)), r);
+        acc[m] += r;
+      }
+    }
+  }
+};
+
 // Q6_K, ggml layout: half n, group j (0..3), element l: ql[64n + 32(j&1) + l]
 // nibble (j>>1), qh[32n + l] bits 2j, int8 scale sc[8n + 2j + l/16].
 template <int M>
@@ -266,7 +324,7 @@ struct Piece<NSQ_TYPE_Q8_0, LAYOUT, M> {
 // ---------------------------------------------------------------------------
 // Fused kernel: several segments (weight matrices sharing the activation),
 // rows concatenated, walked by persistent CTAs in row blocks x K chunks.
-enum : int { kQ4K = 0, kQ6KG = 1, kQ6KN = 2, kQ40 = 3, kQ80 = 4 };
+enum : int { kQ4K = 0, kQ6KG = 1, kQ6KN = 2, kQ40 = 3, kQ80 = 4, kQ5KG = 5, kQ5KN = 6 };
 
 struct FSeg {
   const uint8_t* w;
@@ -309,11 +367,15 @@ __device__ __forceinline__ void run_piece(int code, const uint8_t* pc, const uin
   if constexpr (CODE == kQ6KN) { Piece<NSQ_TYPE_Q6_K, NSQ_Q6K_NODESTOR, M>::run(pc, xp, xstride, acc); return; }
   if constexpr (CODE == kQ40) { Piece<NSQ_TYPE_Q4_0, 0, M>::run(pc, xp, xstride, acc); return; }
   if constexpr (CODE == kQ80) { Piece<NSQ_TYPE_Q8_0, 0, M>::run(pc, xp, xstride, acc); return; }
+  if constexpr (CODE == kQ5KG) { Piece<NSQ_TYPE_Q5_K, NSQ_Q6K_GGML, M>::run(pc, xp, xstride, acc); return; }
+  if constexpr (CODE == kQ5KN) { Piece<NSQ_TYPE_Q5_K, NSQ_Q6K_NODESTOR, M>::run(pc, xp, xstride, acc); return; }
   switch (code) {
     case kQ4K: Piece<NSQ_TYPE_Q4_K, 0, M>::run(pc, xp, xstride, acc); break;
     case kQ6KG: Piece<NSQ_TYPE_Q6_K, NSQ_Q6K_GGML, M>::run(pc, xp, xstride, acc); break;
     case kQ6KN: Piece<NSQ_TYPE_Q6_K, NSQ_Q6K_NODESTOR, M>::run(pc, xp, xstride, acc); break;
     case kQ40: Piece<NSQ_TYPE_Q4_0, 0, M>::run(pc, xp, xstride, acc); break;
+    case kQ5KG: Piece<NSQ_TYPE_Q5_K, NSQ_Q6K_GGML, M>::run(pc, xp, xstride, acc); break;
+    case kQ5KN: Piece<NSQ_TYPE_Q5_K, NSQ_Q6K_NODESTOR, M>::run(pc, xp, xstride, acc); break;
     default: Piece<NSQ_TYPE_Q8_0, 0, M>::run(pc, xp, xstride, acc); break;
   }
 }
@@ -663,6 +725,7 @@ static int seg_code(int type, int layout) {
   switch (type) {
     case NSQ_TYPE_Q4_K: return kQ4K;
     case NSQ_TYPE_Q6_K: return layout == NSQ_Q6K_NODESTOR ? kQ6KN : kQ6KG;
+    case NSQ_TYPE_Q5_K: return layout == NSQ_Q6K_NODESTOR ? kQ5KN : kQ5KG;
     case NSQ_TYPE_Q4_0: return kQ40;
     case NSQ_TYPE_Q8_0: return kQ80;
     default: return -1;
@@ -672,6 +735,7 @@ static int piece_bytes_of(int type) {
   switch (type) {
     case NSQ_TYPE_Q4_K: return 144;
     case NSQ_TYPE_Q6_K: return 210;
+    case NSQ_TYPE_Q5_K: return 176;
     case NSQ_TYPE_Q4_0: return 144;
     case NSQ_TYPE_Q8_0: return 272;
     default: return 0;
@@ -856,6 +920,8 @@ static cudaError_t launch_fused_m(int M, const FusedParams& p, int blocks, size_
     case kQ6KN: return launch_fused_mc<XSELF, kQ6KN, EPI>(M, p, blocks, smem, st, mc);
     case kQ40: return launch_fused_mc<XSELF, kQ40, EPI>(M, p, blocks, smem, st, mc);
     case kQ80: return launch_fused_mc<XSELF, kQ80, EPI>(M, p, blocks, smem, st, mc);
+    case kQ5KG: return launch_fused_mc<XSELF, kQ5KG, EPI>(M, p, blocks, smem, st, mc);
+    case kQ5KN: return launch_fused_mc<XSELF, kQ5KN, EPI>(M, p, blocks, smem, st, mc);
     default:
       if constexpr (EPI == 0) return launch_fused_mc<XSELF, kMixed, 0>(M, p, blocks, smem, st, mc);
       return cudaErrorInvalidValue;  // the epilogue forms take one format

@@ -51,6 +51,10 @@ struct Fmt<NSQ_TYPE_Q4_K> {
   static constexpr int QK = 256, BB = 144, UW = 64;
 };
 template <>
+struct Fmt<NSQ_TYPE_Q5_K> {
+  static constexpr int QK = 256, BB = 176, UW = 64;
+};
+template <>
 struct Fmt<NSQ_TYPE_Q6_K> {
   static constexpr int QK = 256, BB = 210, UW = 64;
 };
@@ -58,6 +62,9 @@ struct Fmt<NSQ_TYPE_Q6_K> {
 // Exact IEEE fp16 -> f32 (subnormals included), the reference's half_to_f32
 // (crates/nodestor-inference/src/dequant/mod.rs:234-260).
 __device__ __forceinline__ float h2f(uint16_t bits) { return __half2float(__ushort_as_half(bits)); }
+// Bits 0..3 of nib to bit 0 of bytes 0..3 (the four products land on
+// disjoint bit ranges, so no carries).
+__device__ __forceinline__ uint32_t spread4(uint32_t nib) { return (nib * 0x00204081u) & 0x01010101u; }
 
 // ---------------------------------------------------------------------------
 // Byte access helpers.  Blocks of Q4_0 / Q8_0 / Q6_K are only 2-byte aligned,

@@ -6,9 +6,9 @@ of the file (magic "GGUF", versions 2 and 3, little-endian counts, the
 13 metadata value types, tensor-info records of name / dims / ggml type /
 offset; gguf.rs:58-160, 184-266).  What it fixes:
 
-* ggml type ids 12 (Q4_K) and 14 (Q6_K) are mapped and sized (144 / 210
-  bytes per 256 weights); the reference has no entry for them and sizes any
-  unknown id as F32 (gguf.rs:268-304);
+* ggml type ids 12 (Q4_K), 13 (Q5_K) and 14 (Q6_K) are mapped and sized
+  (144 / 176 / 210 bytes per 256 weights); the reference has no entry for
+  them and sizes any unknown id as F32 (gguf.rs:268-304);
 * Q8_0 is 34 bytes per 32 weights, not 36 (gguf.rs:297);
 * id 9 is Q8_1 (36 bytes per 32), not Q8_0 (gguf.rs:277);
 * an unknown type id is an error, not a silent F32;
@@ -37,14 +37,14 @@ from .formats import FORMATS
 GGUF_MAGIC = b"GGUF"
 DEFAULT_ALIGNMENT = 32
 
-# ggml type id -> (name, weights per block, bytes per block).  The four
-# block formats of the matmul path come from formats.FORMATS; the rest are
+# ggml type id -> (name, weights per block, bytes per block).  The block
+# formats of the matmul path come from formats.FORMATS; the rest are
 # sized so that files holding them parse correctly, and marked unsupported
 # for compute.
 _EXTRA_TYPES = {
     0: ("F32", 1, 4), 1: ("F16", 1, 2), 30: ("BF16", 1, 2),
     3: ("Q4_1", 32, 20), 6: ("Q5_0", 32, 22), 7: ("Q5_1", 32, 24), 9: ("Q8_1", 32, 36),
-    10: ("Q2_K", 256, 84), 11: ("Q3_K", 256, 110), 13: ("Q5_K", 256, 176), 15: ("Q8_K", 256, 292),
+    10: ("Q2_K", 256, 84), 11: ("Q3_K", 256, 110), 15: ("Q8_K", 256, 292),
     24: ("I8", 1, 1), 25: ("I16", 1, 2), 26: ("I32", 1, 4), 27: ("I64", 1, 8), 28: ("F64", 1, 8),
 }
 TYPES: Dict[int, Tuple[str, int, int]] = dict(_EXTRA_TYPES)

@@ -12,7 +12,7 @@ import pytest
 
 from planejaja_b200 import gguf as G
 from planejaja_b200 import quantize as Q
-from planejaja_b200.formats import Q4_0, Q4_K, Q6_K, Q8_0, fmt
+from planejaja_b200.formats import Q4_0, Q4_K, Q5_K, Q6_K, Q8_0, fmt
 
 gguf_py = pytest.importorskip("gguf")
 
@@ -32,9 +32,10 @@ def _write_with_gguf_py(path, alignment=None):
     f32 = rng.standard_normal((3, 5)).astype(np.float32)
     w.add_tensor("f32", f32)
     tens["f32"] = (f32.tobytes(), (5, 3), 0)
-    for name, tid, n, k in (("q4k", Q4_K, 6, 512), ("q6k", Q6_K, 4, 256), ("q8", Q8_0, 5, 64), ("q40", Q4_0, 3, 96)):
+    for name, tid, n, k in (("q4k", Q4_K, 6, 512), ("q6k", Q6_K, 4, 256), ("q8", Q8_0, 5, 64), ("q40", Q4_0, 3, 96),
+                            ("q5k", Q5_K, 2, 768)):
         raw = Q.synthetic_weights(n, k, tid, seed=n + k)
-        qt = {Q4_K: T.Q4_K, Q6_K: T.Q6_K, Q8_0: T.Q8_0, Q4_0: T.Q4_0}[tid]
+        qt = {Q4_K: T.Q4_K, Q5_K: T.Q5_K, Q6_K: T.Q6_K, Q8_0: T.Q8_0, Q4_0: T.Q4_0}[tid]
         rb = fmt(tid).row_bytes(k)
         w.add_tensor(name, raw.reshape(n, rb), raw_dtype=qt)
         tens[name] = (raw.tobytes(), (k, n), tid)
@@ -87,6 +88,7 @@ def test_fixed_sizes_against_reference_table():
     assert G.tensor_nbytes((4096,), Q8_0) == 128 * 34       # reference: 128 * 36
     assert G.tensor_nbytes((4096,), Q4_K) == 16 * 144       # reference: 4096 * 4 (F32 fallback)
     assert G.tensor_nbytes((4096,), Q6_K) == 16 * 210       # reference: 4096 * 4
+    assert G.tensor_nbytes((4096,), Q5_K) == 16 * 176       # reference: 4096 * 4
     assert G.tensor_nbytes((4096,), 9) == 128 * 36          # Q8_1, which the reference reads as Q8_0
     assert G.TYPES[9][0] == "Q8_1"
     with pytest.raises(G.GGUFError):

@@ -7,7 +7,7 @@ import torch
 
 from planejaja_b200 import gguf as G
 from planejaja_b200 import quantize as Q
-from planejaja_b200.formats import Q4_K, Q6_K, Q8_0
+from planejaja_b200.formats import Q4_K, Q5_K, Q6_K, Q8_0
 
 pytestmark = pytest.mark.gpu
 
@@ -16,7 +16,7 @@ def test_gguf_tensors_through_the_kernels(tmp_path, oracle):
     from planejaja_b200.engine import CudaEngine
     eng = CudaEngine(0)
     specs = [("blk.0.ffn_gate.weight", Q4_K, 320, 2048), ("blk.0.ffn_down.weight", Q6_K, 256, 2304),
-             ("blk.0.attn_q.weight", Q8_0, 96, 512)]
+             ("blk.0.attn_q.weight", Q8_0, 96, 512), ("blk.0.attn_v.weight", Q5_K, 128, 1024)]
     recs = [(name, (k, n), t, Q.synthetic_weights(n, k, t, seed=n)) for name, t, n, k in specs]
     path = tmp_path / "m.gguf"
     G.write_minimal(str(path), recs, {"general.architecture": "llama"}, alignment=64)

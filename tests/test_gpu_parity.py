@@ -11,14 +11,15 @@ import torch
 
 from planejaja_b200 import quantize as Q
 from planejaja_b200 import _lib
-from planejaja_b200.formats import FORMATS, Q4_0, Q4_K, Q6_K, Q8_0, Q6K_GGML, Q6K_NODESTOR
+from planejaja_b200.formats import FORMATS, Q4_0, Q4_K, Q5_K, Q6_K, Q8_0, Q6K_GGML, Q6K_NODESTOR
 
 pytestmark = pytest.mark.gpu
 
 GEMV_TOL = 1e-3
 GEMM_TOL = 2e-2
-ALL = [(Q4_0, 0), (Q8_0, 0), (Q4_K, 0), (Q6_K, Q6K_GGML), (Q6_K, Q6K_NODESTOR)]
-IDS = ["Q4_0", "Q8_0", "Q4_K", "Q6_K", "Q6_K_nodestor"]
+ALL = [(Q4_0, 0), (Q8_0, 0), (Q4_K, 0), (Q5_K, Q6K_GGML), (Q5_K, Q6K_NODESTOR), (Q6_K, Q6K_GGML),
+       (Q6_K, Q6K_NODESTOR)]
+IDS = ["Q4_0", "Q8_0", "Q4_K", "Q5_K", "Q5_K_nodestor", "Q6_K", "Q6_K_nodestor"]
 
 
 @pytest.fixture(scope="module")
@@ -54,6 +55,7 @@ def test_dequant_bit_exact_random(eng, oracle, tid, layout):
 
 
 @pytest.mark.parametrize("name,tid,layout", [("Q4_0", Q4_0, 0), ("Q8_0", Q8_0, 0), ("Q4_K", Q4_K, 0),
+                                             ("Q5_K", Q5_K, 0), ("Q5_K_NODESTOR", Q5_K, 1),
                                              ("Q6_K", Q6_K, 0), ("Q6_K_NODESTOR", Q6_K, 1)])
 def test_dequant_golden_and_fuzz(eng, golden, name, tid, layout):
     raw, ref = golden[f"{name}_raw"], golden[f"{name}_f32"]
@@ -66,6 +68,8 @@ def test_dequant_reference_known_answers(eng, golden):
     assert np.all(out[:128] == 28.0)
     out = eng.dequant(eng.upload(golden["kat_q8_raw"]), Q8_0, 96).cpu().numpy().reshape(3, 32)
     assert np.all(out[0] == 0) and np.all(out[1] == 5.0) and out[2, 0] == -1.0
+    out = eng.dequant(eng.upload(golden["kat_q5k_high_raw"]), Q5_K, 256, "f32", Q6K_NODESTOR).cpu().numpy()
+    assert np.all(out >= 0) and np.all(out[:128] == 31.0)
 
 
 def test_dequant_subnormal_scale_follows_rust_conversion(eng, oracle):
@@ -151,6 +155,20 @@ def test_gemv_multi_mixed_segments(eng, oracle, m):
                           torch.from_numpy(x).to(eng.device), k)
     for w, (t, l, n), y in zip(ws, specs, outs):
         assert rel_err(y.cpu().numpy(), oracle.quant_matmul(w, t, x, n, k, l)) <= GEMV_TOL
+
+
+@pytest.mark.parametrize("layout", [Q6K_GGML, Q6K_NODESTOR])
+@pytest.mark.parametrize("m", [1, 3, 12])
+def test_gemv_multi_q5k_mix(eng, oracle, gemv_kernel, layout, m):
+    """Q5_K_M-style q|k|v: two Q5_K segments and a Q6_K one, one launch."""
+    k = 2048
+    specs = [(Q5_K, layout, 136), (Q5_K, layout, 40), (Q6_K, layout, 40)]
+    ws = [Q.synthetic_weights(n, k, t, seed=80 + i, q6k_layout=l) for i, (t, l, n) in enumerate(specs)]
+    x = Q.synthetic_activations(m, k, seed=81)
+    outs = eng.gemv_multi([(eng.upload(w), t, n, l) for w, (t, l, n) in zip(ws, specs)],
+                          torch.from_numpy(x).to(eng.device), k)
+    for w, (t, l, n), y in zip(ws, specs, outs):
+        assert rel_err(y.cpu().numpy(), oracle.quant_matmul(w, t, x, n, k, l, threads=8)) <= GEMV_TOL
 
 
 def test_gemv_multi_workspace_mode(eng, oracle):
