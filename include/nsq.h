@@ -49,6 +49,7 @@ extern "C" {
 #define NSQ_ERR_TIMEOUT 7   /* a bounded device-side wait gave up */
 #define NSQ_ERR_WORKSPACE 8 /* workspace missing or too small */
 #define NSQ_ERR_DEVICE 9    /* current device is not sm_100 */
+#define NSQ_ERR_FORMAT 10   /* malformed NSZ tile stream */
 
 #define NSQ_TYPE_Q4_0 2
 #define NSQ_TYPE_Q8_0 8
@@ -266,6 +267,49 @@ typedef struct nsq_xsegment {
  * contract and workspace rule as nsq_gemv_multi; needs K % 256 == 0. */
 int nsq_gemv_multi_xchg(const nsq_xsegment *segs, int nseg, const float *x, int64_t M, int64_t K,
                         nsq_comm *comm, void *workspace, size_t workspace_bytes, void *stream);
+
+/* ---- NSZ (NodeStor Zip) lossless tensors and ZipGEMM ----
+ *
+ * An NSZ tensor is the tile stream one index entry of an .nsz file points at
+ * (crates/nodestor-formats/src/nsz_format.rs:13-44; written by
+ * nsz_encoder.rs and nodestor-cli/src/bin/nsz_convert.rs): ceil(count/512)
+ * tiles of 512 weights (the last may be shorter), each [header 8][match
+ * bitmap][near bitmap][near deltas][residual exponents][mantissas][signs]
+ * padded to 64 bytes.  Decoding is lossless: the original FP32 / FP16 / BF16
+ * bits come back exactly as nsz_decoder.rs:19-218 restores them. */
+#define NSQ_NSZ_FP32 0
+#define NSQ_NSZ_FP16 1
+#define NSQ_NSZ_BF16 2
+#define NSQ_NSZ_TILE_WEIGHTS 512
+
+/* Tiles of a tensor of num_weights weights; its offset table has one more entry. */
+int64_t nsq_nsz_num_tiles(int64_t num_weights);
+
+/* HOST function (no GPU): walks the tile headers of a tile stream in host
+ * memory (e.g. the mmap of the .nsz file), checks each tile against its
+ * bitmaps (dtype byte, near and residual counts, sizes, total length) and
+ * writes num_tiles + 1 tile offsets in units of 64 bytes.  The table is what
+ * the device entry points take (replaces the reference's fixed tile_stride /
+ * tile_meta arguments, lib.rs:124-151, which cannot address variable-size
+ * tiles).  NSQ_ERR_FORMAT on any inconsistency. */
+int nsq_nsz_index(const void *tiles_host, int64_t nbytes, int64_t num_weights, int dtype, uint32_t *offsets_host);
+
+/* Lossless decode of a whole tensor on the device: out receives num_weights
+ * values in the original dtype (uint32 bits for FP32, uint16 for FP16/BF16);
+ * bit-exact to nsz_decoder.rs.  tiles and out 16-byte aligned; offsets is the
+ * device copy of the nsq_nsz_index table. */
+int nsq_nsz_decode(const void *tiles, const uint32_t *offsets, int64_t num_weights, int dtype, void *out,
+                   void *stream);
+
+/* ZipGEMM (VulkanEngine::zipgemm, lib.rs:124-151; zipgemm.comp): fused
+ * decompress + matmul, y[M x N] f32 = x[M x K] f32 . W^T with W [N x K] the
+ * tensor's weights in stream order (GGUF ne0 = K contiguous).  The decoded
+ * weights live only in registers.  fp32 accumulation; accuracy contract:
+ * max_i |y_i - r_i| / max(|r_i|, rms(r)) <= 1e-3 against the sequential f32
+ * oracle.  Any M >= 1 (tokens are processed 8 at a time); fastest with
+ * K % 16 == 0 and x 16-byte aligned. */
+int nsq_zipgemm(const void *tiles, const uint32_t *offsets, int dtype, const float *x, float *y, int64_t M,
+                int64_t N, int64_t K, void *stream);
 
 #ifdef __cplusplus
 }

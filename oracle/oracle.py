@@ -24,8 +24,8 @@ _i64 = ctypes.c_int64
 
 
 def build(force: bool = False) -> str:
-    src = os.path.join(_HERE, "nsq_oracle.c")
-    if force or not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < os.path.getmtime(src):
+    srcs = [os.path.join(_HERE, f) for f in ("nsq_oracle.c", "nsz_oracle.c")]
+    if force or not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < max(map(os.path.getmtime, srcs)):
         subprocess.run(["make", "-s", "-C", _HERE, "liboracle.so"], check=True)
     return _LIB_PATH
 
@@ -60,6 +60,20 @@ def lib():
         L.orc_block_weights.argtypes = [ctypes.c_int]
         L.orc_block_bytes.restype = _i64
         L.orc_block_bytes.argtypes = [ctypes.c_int]
+        L.orc_nsz_max_tile_bytes.restype = _i64
+        L.orc_nsz_max_tile_bytes.argtypes = [ctypes.c_int]
+        L.orc_nsz_encode_tile.restype = _i64
+        L.orc_nsz_encode_tile.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, _u8p]
+        L.orc_nsz_decode_tile.restype = _i64
+        L.orc_nsz_decode_tile.argtypes = [_u8p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+        L.orc_nsz_encode.restype = _i64
+        L.orc_nsz_encode.argtypes = [ctypes.c_void_p, _i64, ctypes.c_int, ctypes.c_int, _u8p, _i64]
+        L.orc_nsz_offsets.restype = ctypes.c_int
+        L.orc_nsz_offsets.argtypes = [_u8p, _i64, _i64, ctypes.c_int, ctypes.POINTER(_i64)]
+        L.orc_nsz_decode.restype = ctypes.c_int
+        L.orc_nsz_decode.argtypes = [_u8p, _i64, _i64, ctypes.c_int, ctypes.c_void_p]
+        L.orc_nsz_matmul.restype = ctypes.c_int
+        L.orc_nsz_matmul.argtypes = [_u8p, _i64, _f32p, _f32p, _i64, _i64, _i64]
         _lib = L
     return _lib
 
@@ -140,3 +154,63 @@ def quant_matmul(w: np.ndarray, type_id: int, x: np.ndarray, n: int, k: int,
 
 def num_threads() -> int:
     return lib().orc_num_threads()
+
+
+# ---------------------------------------------------------------- NSZ (TCA-TBE)
+NSZ_FP32, NSZ_FP16, NSZ_BF16 = 0, 1, 2
+NSZ_TILE = 512
+
+
+def _nsz_words(w: np.ndarray, dtype: int) -> np.ndarray:
+    """FP32 weights as uint32 bits, FP16 / BF16 as uint16 bits."""
+    w = np.ascontiguousarray(w)
+    if dtype == NSZ_FP32:
+        return w.view(np.uint32) if w.dtype != np.uint32 else w
+    return w.view(np.uint16) if w.dtype != np.uint16 else w
+
+
+def nsz_encode_tile(w: np.ndarray, dtype: int = NSZ_FP32, reference_quirks: bool = True) -> bytes:
+    b = _nsz_words(w, dtype).reshape(-1)
+    assert 1 <= b.size <= NSZ_TILE
+    out = np.zeros(lib().orc_nsz_max_tile_bytes(dtype), np.uint8)
+    size = lib().orc_nsz_encode_tile(b.ctypes.data, b.size, dtype, int(reference_quirks), _p(out, _u8p))
+    return out[:size].tobytes()
+
+
+def nsz_encode(w: np.ndarray, dtype: int = NSZ_FP32, reference_quirks: bool = True) -> np.ndarray:
+    """The tensor's tile stream (uint8), as the reference's encoder writes it."""
+    b = _nsz_words(w, dtype).reshape(-1)
+    L = lib()
+    cap = max(1, -(-b.size // NSZ_TILE)) * L.orc_nsz_max_tile_bytes(dtype)
+    out = np.zeros(cap, np.uint8)
+    size = L.orc_nsz_encode(b.ctypes.data, b.size, dtype, int(reference_quirks), _p(out, _u8p), cap)
+    if size < 0:
+        raise ValueError("orc_nsz_encode failed")
+    return out[:size].copy()
+
+
+def nsz_offsets(data: np.ndarray, count: int, dtype: int = NSZ_FP32) -> np.ndarray:
+    data = np.ascontiguousarray(data, np.uint8)
+    off = np.zeros(-(-count // NSZ_TILE) + 1, np.int64)
+    if lib().orc_nsz_offsets(_p(data, _u8p), data.size, count, dtype, off.ctypes.data_as(ctypes.POINTER(_i64))):
+        raise ValueError("NSZ stream does not hold the given weight count")
+    return off
+
+
+def nsz_decode(data: np.ndarray, count: int, dtype: int = NSZ_FP32) -> np.ndarray:
+    """Decoded weights: float32 for FP32, raw uint16 bits for FP16 / BF16."""
+    data = np.ascontiguousarray(data, np.uint8)
+    out = np.zeros(count, np.uint32 if dtype == NSZ_FP32 else np.uint16)
+    if lib().orc_nsz_decode(_p(data, _u8p), data.size, count, dtype, out.ctypes.data):
+        raise ValueError("orc_nsz_decode failed")
+    return out.view(np.float32) if dtype == NSZ_FP32 else out
+
+
+def nsz_matmul(data: np.ndarray, x: np.ndarray, n: int, k: int) -> np.ndarray:
+    """y[M, N] = cpu_matmul_f32(x[M, K], transpose(decode(W[N, K]))), FP32 weights."""
+    data = np.ascontiguousarray(data, np.uint8)
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, k)
+    y = np.empty((x.shape[0], n), np.float32)
+    if lib().orc_nsz_matmul(_p(data, _u8p), data.size, _p(x, _f32p), _p(y, _f32p), x.shape[0], n, k):
+        raise ValueError("orc_nsz_matmul failed")
+    return y

@@ -23,6 +23,10 @@ ERR_NCCL = 6
 ERR_TIMEOUT = 7
 ERR_WORKSPACE = 8
 ERR_DEVICE = 9
+ERR_FORMAT = 10
+
+NSZ_FP32, NSZ_FP16, NSZ_BF16 = 0, 1, 2
+NSZ_TILE_WEIGHTS = 512
 
 OUT_F32 = 0
 OUT_BF16 = 1
@@ -54,6 +58,10 @@ SIGNATURES = [
     ("nsq_comm_wait", _int, [_vp, _vp]),
     ("nsq_comm_destroy", _int, [_vp]),
     ("nsq_gemv_multi_xchg", _int, [ctypes.c_void_p, _int, _vp, _i64, _i64, _vp, _vp, _sz, _vp]),
+    ("nsq_nsz_num_tiles", _i64, [_i64]),
+    ("nsq_nsz_index", _int, [_vp, _i64, _i64, _int, _vp]),
+    ("nsq_nsz_decode", _int, [_vp, _vp, _i64, _int, _vp, _vp]),
+    ("nsq_zipgemm", _int, [_vp, _vp, _int, _vp, _vp, _i64, _i64, _i64, _vp]),
 ]
 
 

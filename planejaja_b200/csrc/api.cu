@@ -66,6 +66,14 @@ static int check_device(DevInfo& di) {
   return NSQ_OK;
 }
 
+// For the other translation units (nsz.cu): NSQ_OK and the SM count.
+int device_check(int* num_sms) {
+  DevInfo di;
+  const int rc = check_device(di);
+  *num_sms = di.num_sms;
+  return rc;
+}
+
 static int check_weights(const void* w, int type, int layout, int64_t K) {
   if (!type_ok(type)) return NSQ_ERR_TYPE;
   if ((type == NSQ_TYPE_Q6_K || type == NSQ_TYPE_Q5_K) && layout != NSQ_Q6K_GGML && layout != NSQ_Q6K_NODESTOR)
@@ -97,6 +105,7 @@ const char* nsq_strerror(int status) {
     case NSQ_ERR_TIMEOUT: return "device-side wait timed out";
     case NSQ_ERR_WORKSPACE: return "workspace missing or too small";
     case NSQ_ERR_DEVICE: return "current device is not sm_100";
+    case NSQ_ERR_FORMAT: return "malformed NSZ tile stream";
     default: return "unknown status";
   }
 }

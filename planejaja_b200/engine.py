@@ -11,6 +11,10 @@
                                    src/operator_registry.rs:43-49, 246-259)
   dequant(w, t, n)              -> f32 / bf16 weights (DequantDispatcher::dequantize,
                                    crates/nodestor-inference/src/dequant/mod.rs:142-191)
+  zipgemm(w, x, m, k, n)        -> y = x . W^T from an NSZ (TCA-TBE) tensor,
+                                   decompressed in registers (lib.rs:124-151)
+  nsz_decode(w)                 -> the NSZ tensor's original weights, bit-exact
+                                   (nsz_decoder.rs:19-218)
 
 Device memory, streams and the output buffers come from PyTorch; every
 computation is a call into libnsq.so.  Like the reference, calls are
@@ -202,6 +206,43 @@ class CudaEngine:
             return self.gemv(w, ggml_type, x.reshape(m, k).float().contiguous(), n, k, q6k_layout, sync=sync)
         xb = x.reshape(m, k).to(torch.bfloat16).contiguous()
         return self.gemm_bf16(w, ggml_type, xb, n, k, q6k_layout, sync=sync).float()
+
+    # ---- NSZ (TCA-TBE) tensors and ZipGEMM --------------------------------
+    def nsz_upload(self, stream, num_weights: int, dtype: int = _lib.NSZ_FP32, shape=()) -> "NszTensor":
+        """One-time upload of an NSZ tile stream and its validated offset table."""
+        from .nsz import NszTensor, index
+        stream = np.ascontiguousarray(stream, np.uint8).reshape(-1)
+        off = index(stream, num_weights, dtype)
+        tiles = torch.from_numpy(stream.copy()).to(self.device) if stream.size else \
+            torch.empty(16, dtype=torch.uint8, device=self.device)
+        offsets = torch.from_numpy(off.view(np.int32)).to(self.device)
+        return NszTensor(tiles, offsets, int(num_weights), int(dtype), tuple(shape))
+
+    def nsz_decode(self, t, out: Optional[torch.Tensor] = None, sync: bool = True) -> torch.Tensor:
+        """Lossless decode: float32 / float16 / bfloat16 weights, bit-exact."""
+        dt = {_lib.NSZ_FP32: torch.float32, _lib.NSZ_FP16: torch.float16, _lib.NSZ_BF16: torch.bfloat16}[t.dtype]
+        if out is None:
+            out = torch.empty(max(t.count, 1), dtype=dt, device=self.device)[:t.count]
+        check(self.lib.nsq_nsz_decode(_ptr(t.tiles), _ptr(t.offsets), t.count, t.dtype, _ptr(out),
+                                      self._stream()), "nsq_nsz_decode")
+        self._sync(sync)
+        return out
+
+    def zipgemm(self, w, x: torch.Tensor, m: int, k: int, n: int, out: Optional[torch.Tensor] = None,
+                sync: bool = True) -> torch.Tensor:
+        """ZipGEMM (VulkanEngine::zipgemm, lib.rs:124-151): y[m, n] f32 =
+        x[m, k] . W^T, W [n x k] decompressed on the fly from an NszTensor."""
+        if w.count != n * k:
+            raise NsqError(_lib.ERR_SHAPE, f"zipgemm: tensor holds {w.count} weights, not {n} x {k}")
+        x = x.reshape(m, k)
+        if x.dtype != torch.float32 or not x.is_contiguous():
+            x = x.float().contiguous()
+        if out is None:
+            out = torch.empty((m, n), dtype=torch.float32, device=self.device)
+        check(self.lib.nsq_zipgemm(_ptr(w.tiles), _ptr(w.offsets), w.dtype, _ptr(x), _ptr(out), m, n, k,
+                                   self._stream()), "nsq_zipgemm")
+        self._sync(sync)
+        return out
 
     def device_status(self, clear: bool = True) -> int:
         """NSQ_ERR_TIMEOUT if a bounded device-side wait gave up, else 0."""
