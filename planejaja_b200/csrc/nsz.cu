@@ -18,14 +18,16 @@
 //   * each lane's 16 match / near / sign bits are one 16-bit load;
 //   * its first near-delta and residual ranks come from one warp prefix sum
 //     of its (near, residual) popcounts;
-//   * per group of 4 weights, the next 4 delta bits and the next 4 residual
-//     bytes are expanded to their positions with one byte permute each (a
-//     16-entry selector table in shared memory maps a 4-bit mask to the
-//     permute that places the k-th source byte at the k-th set bit), so the
-//     exponent bytes of 4 weights come out of a few word-wide operations;
-//   * the lane's mantissas are 16-byte loads (48 / 32 / 16 bytes per lane;
-//     the section offset is the same modulo 16 for every lane) realigned by
-//     a warp-uniform funnel shift.
+//   * per group of 4 weights, shared-memory tables turn the 4-bit near and
+//     residual masks into byte masks and byte-permute selectors, and the
+//     next 4 near-delta bits into a byte mask; the next 4 residual bytes are
+//     placed on their weights by one byte permute of the two aligned words
+//     around them, so the 4 exponent bytes come out of three word selects;
+//   * the lane's mantissas (48 / 32 / 16 bytes) are 8-byte loads; the
+//     section's offset modulo 8 is the same for every lane, so a
+//     warp-uniform switch picks constant-offset shifts for all 16 fields;
+//   * an FP32 weight is assembled by one byte permute (exponent byte to the
+//     top) and one funnel shift that brings in the sign bit.
 // ZipGEMM splits the output rows evenly over CTAs (a CTA owns rows [r0, r1)
 // and writes them once; tiles that straddle its boundary are decoded by both
 // neighbours and masked), accumulates each lane's 16 products per token in
@@ -42,7 +44,7 @@ namespace {
 
 constexpr int kNszW = NSQ_NSZ_TILE_WEIGHTS;
 constexpr int kNszWarps = 8;
-constexpr int kNszDepth = 4;
+constexpr int kNszDepth = 3;
 
 template <int DT>
 struct NszFmt;
@@ -83,23 +85,75 @@ __device__ __forceinline__ uint32_t lds_u32_any(const uint8_t* q) {
   return __funnelshift_r(w[0], w[1], 8u * (uint32_t)(a & 3));
 }
 
-// Selector for __byte_perm(src, 0, sel[m]): byte i of the result is source
-// byte popc(m & ((1 << i) - 1)) where bit i of m is set, else 0.
-__device__ __forceinline__ void init_sel_table(uint32_t* sel) {
-  if (threadIdx.x < 16) {
-    uint32_t s = 0, r = 0;
-    for (int i = 0; i < 4; ++i) s |= ((threadIdx.x >> i) & 1 ? r++ : 4u) << (4 * i);
-    sel[threadIdx.x] = s;
+// Shared-memory tables, built once per CTA (indexed by 4-bit masks of the
+// weights of one group of 4):
+//   m4[b].x: byte-permute selector placing source byte k at the position of
+//            the k-th set bit of b (other nibbles 4), popc(b) in bits 16..
+//   m4[b].y: byte mask, 0xFF at the set bits of b
+//   dx[b * 16 + d]: byte mask, 0xFF at the position of the k-th set bit of b
+//            where bit k of d is set (the near deltas placed on the near weights)
+struct NszLut {
+  uint2 m4[16];
+  uint32_t dx[256];
+};
+
+__device__ __forceinline__ void init_nsz_lut(NszLut* L) {
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+    const uint32_t b = (uint32_t)i >> 4, d = (uint32_t)i & 15;
+    uint32_t mask = 0, k = 0;
+    for (int j = 0; j < 4; ++j)
+      if ((b >> j) & 1) {
+        if ((d >> k) & 1) mask |= 0xFFu << (8 * j);
+        ++k;
+      }
+    L->dx[i] = mask;
+    if (i < 16) {
+      uint32_t sel = 0, r = 0;
+      for (int j = 0; j < 4; ++j) sel |= ((i >> j) & 1 ? r++ : 4u) << (4 * j);
+      L->m4[i] = make_uint2(sel | (r << 16), spread4((uint32_t)i) * 0xFFu);
+    }
+  }
+}
+
+// NB little-endian bytes starting at byte O of the word array W.
+template <int O, int NB, int NW>
+__device__ __forceinline__ uint32_t bytes_at(const uint32_t (&W)[NW]) {
+  constexpr int w = O >> 2, sh = 8 * (O & 3);
+  static_assert(w < NW && ((O & 3) + NB <= 4 || w + 1 < NW), "read past the loaded words");
+  if constexpr ((O & 3) + NB <= 4) return W[w] >> sh;
+  else return __funnelshift_r(W[w], W[w + 1], sh);
+}
+
+// The lane's 16 mantissas from its words W (byte D = first mantissa byte);
+// FP32 fields keep the bits above 23 (cleared when the weight is assembled).
+template <int DT, int D, int NW>
+__device__ __forceinline__ void mant_extract(const uint32_t (&W)[NW], uint32_t (&mant)[16]) {
+  if constexpr (DT == NSQ_NSZ_FP32) {
+#define NSZ_M3(j) mant[j] = bytes_at<D + 3 * (j), 3>(W);  // bits 23.. masked at assembly
+    NSZ_M3(0) NSZ_M3(1) NSZ_M3(2) NSZ_M3(3) NSZ_M3(4) NSZ_M3(5) NSZ_M3(6) NSZ_M3(7)
+    NSZ_M3(8) NSZ_M3(9) NSZ_M3(10) NSZ_M3(11) NSZ_M3(12) NSZ_M3(13) NSZ_M3(14) NSZ_M3(15)
+#undef NSZ_M3
+  } else if constexpr (DT == NSQ_NSZ_FP16) {
+#define NSZ_M2(j) mant[j] = bytes_at<D + 2 * (j), 2>(W) & 0x3FFu;
+    NSZ_M2(0) NSZ_M2(1) NSZ_M2(2) NSZ_M2(3) NSZ_M2(4) NSZ_M2(5) NSZ_M2(6) NSZ_M2(7)
+    NSZ_M2(8) NSZ_M2(9) NSZ_M2(10) NSZ_M2(11) NSZ_M2(12) NSZ_M2(13) NSZ_M2(14) NSZ_M2(15)
+#undef NSZ_M2
+  } else {
+#define NSZ_M1(j) mant[j] = bytes_at<D + (j), 1>(W) & 0x7Fu;
+    NSZ_M1(0) NSZ_M1(1) NSZ_M1(2) NSZ_M1(3) NSZ_M1(4) NSZ_M1(5) NSZ_M1(6) NSZ_M1(7)
+    NSZ_M1(8) NSZ_M1(9) NSZ_M1(10) NSZ_M1(11) NSZ_M1(12) NSZ_M1(13) NSZ_M1(14) NSZ_M1(15)
+#undef NSZ_M1
   }
 }
 
 // Decodes the 16 weights [16 * lane, 16 * lane + 16) of the n-weight tile at
 // p (shared memory, 16-byte aligned) into their original bit patterns (FP16 /
 // BF16 in the low half).  vmask: weights that exist (< n).  Warp-collective.
-template <int DT>
-__device__ __forceinline__ void nsz_decode16(const uint8_t* __restrict__ p, int n, int lane,
-                                             const uint32_t* __restrict__ sel, uint32_t (&v)[16],
+template <int DT, bool FULL>
+__device__ __forceinline__ void nsz_decode16(const uint8_t* __restrict__ p, int n_, int lane,
+                                             const NszLut& L, uint32_t (&v)[16],
                                              uint32_t& vmask) {
+  const int n = FULL ? kNszW : n_;  // FULL: a 512-weight tile, offsets fold to constants
   constexpr int MB = NszFmt<DT>::MB;
   const uint2 h = *reinterpret_cast<const uint2*>(p);
   // counts clamped to the tile size: a malformed header cannot move a read
@@ -107,11 +161,13 @@ __device__ __forceinline__ void nsz_decode16(const uint8_t* __restrict__ p, int 
   const uint32_t modal = h.x & 0xFF, nres = min((h.x >> 8) & 0xFFFFu, (uint32_t)kNszW),
                  nnear = min(h.y & 0xFFFFu, (uint32_t)kNszW);
   const int B = (n + 7) >> 3;
-  const int nv = min(max(n - 16 * lane, 0), 16);
+  const int nv = FULL ? 16 : min(max(n - 16 * lane, 0), 16);
   const uint32_t vm = nv >= 16 ? 0xFFFFu : ((1u << nv) - 1u);
-  const uint32_t M16 = lds_u16_any(p + 8 + 2 * lane) & vm;
+  const uint32_t M16 = (FULL ? (uint32_t)*reinterpret_cast<const uint16_t*>(p + 8 + 2 * lane)
+                             : lds_u16_any(p + 8 + 2 * lane)) & vm;
   // a weight marked both match and near is a match and takes no delta
-  const uint32_t N16 = lds_u16_any(p + 8 + B + 2 * lane) & vm & ~M16;
+  const uint32_t N16 = (FULL ? (uint32_t)*reinterpret_cast<const uint16_t*>(p + 8 + B + 2 * lane)
+                             : lds_u16_any(p + 8 + B + 2 * lane)) & vm & ~M16;
   const uint32_t R16 = vm & ~(M16 | N16);
   // exclusive prefix over lanes of (near count, residual count << 16)
   const uint32_t cnt = (uint32_t)__popc(N16) | ((uint32_t)__popc(R16) << 16);
@@ -131,49 +187,29 @@ __device__ __forceinline__ void nsz_decode16(const uint8_t* __restrict__ p, int 
   const uint32_t dw = lds_u32_any(p + DO + (nc0 >> 3)) >> (nc0 & 7);
   const uint32_t S16 = lds_u16_any(p + SO + 2 * lane);
 
-  // mantissas: bytes [MO + 16 * MB * lane, + 16 * MB)
+  // mantissas: bytes [MO + 16 * MB * lane, + 16 * MB), read as 8-byte words
+  // from the 8-aligned address below them; the byte offset d = MO & 7 is the
+  // same for every lane, so each d gets its own constant-offset extraction.
   uint32_t mant[16];
   {
-    constexpr int LB = 16 * MB, NW = LB / 4, NV = LB / 16 + 1;
-    const int sh = MO & 15;
-    const uint8_t* base = p + (MO & ~15) + LB * lane;
-    uint32_t W[4 * NV];
+    constexpr int LB = 16 * MB, NW = (LB + 8) / 4;
+    const uint8_t* base = p + (MO & ~7) + LB * lane;
+    uint32_t W[NW];
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const uint4 q = *reinterpret_cast<const uint4*>(base + 16 * i);
-      W[4 * i] = q.x;
-      W[4 * i + 1] = q.y;
-      W[4 * i + 2] = q.z;
-      W[4 * i + 3] = q.w;
+    for (int i = 0; i < NW / 2; ++i) {
+      const uint2 q = *reinterpret_cast<const uint2*>(base + 8 * i);
+      W[2 * i] = q.x;
+      W[2 * i + 1] = q.y;
     }
-    const int qw = sh >> 2;  // warp-uniform
-    uint32_t U[NW + 1];
-#pragma unroll
-    for (int i = 0; i <= NW; ++i) U[i] = qw == 0 ? W[i] : qw == 1 ? W[i + 1] : qw == 2 ? W[i + 2] : W[i + 3];
-    const uint32_t bs = 8u * (uint32_t)(sh & 3);
-    uint32_t L[NW];
-#pragma unroll
-    for (int i = 0; i < NW; ++i) L[i] = __funnelshift_r(U[i], U[i + 1], bs);
-    if constexpr (DT == NSQ_NSZ_FP32) {
-#pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        const uint32_t a0 = L[3 * g], a1 = L[3 * g + 1], a2 = L[3 * g + 2];
-        mant[4 * g] = a0 & 0x7FFFFFu;
-        mant[4 * g + 1] = __funnelshift_r(a0, a1, 24) & 0x7FFFFFu;
-        mant[4 * g + 2] = __funnelshift_r(a1, a2, 16) & 0x7FFFFFu;
-        mant[4 * g + 3] = (a2 >> 8) & 0x7FFFFFu;
-      }
-    } else if constexpr (DT == NSQ_NSZ_FP16) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        mant[2 * i] = L[i] & 0x3FFu;
-        mant[2 * i + 1] = (L[i] >> 16) & 0x3FFu;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int b = 0; b < 4; ++b) mant[4 * i + b] = (L[i] >> (8 * b)) & 0x7Fu;
+    switch (MO & 7) {
+      case 0: mant_extract<DT, 0>(W, mant); break;
+      case 1: mant_extract<DT, 1>(W, mant); break;
+      case 2: mant_extract<DT, 2>(W, mant); break;
+      case 3: mant_extract<DT, 3>(W, mant); break;
+      case 4: mant_extract<DT, 4>(W, mant); break;
+      case 5: mant_extract<DT, 5>(W, mant); break;
+      case 6: mant_extract<DT, 6>(W, mant); break;
+      default: mant_extract<DT, 7>(W, mant); break;
     }
   }
 
@@ -182,24 +218,38 @@ __device__ __forceinline__ void nsz_decode16(const uint8_t* __restrict__ p, int 
   int nq = 0, rq = 0;
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
-    const uint32_t m4 = (M16 >> (4 * q)) & 15u, n4 = (N16 >> (4 * q)) & 15u, r4 = (R16 >> (4 * q)) & 15u;
-    const uint32_t dex = __byte_perm(spread4((dw >> nq) & 15u), 0u, sel[n4]);
-    const uint32_t dmask = dex * 0xFFu;
-    const uint32_t en = (dmask & plus4) | (~dmask & minus4);
-    const uint32_t rex = __byte_perm(lds_u32_any(p + RO + rc0 + rq), 0u, sel[r4]);
-    const uint32_t E = ((spread4(m4) * 0xFFu) & modal4) | ((spread4(n4) * 0xFFu) & en) | rex;
-    nq += __popc(n4);
-    rq += __popc(r4);
+    const uint32_t n4 = (N16 >> (4 * q)) & 15u, r4 = (R16 >> (4 * q)) & 15u;
+    const uint2 ln = L.m4[n4], lr = L.m4[r4];
+    // near: modal + 1 where the weight's delta bit is set, else modal - 1
+    const uint32_t dm = L.dx[n4 * 16 + ((dw >> nq) & 15u)];
+    const uint32_t ne = (dm & plus4) | (~dm & minus4);
+    // residual: the next 4 residual bytes (from two aligned words) placed on
+    // the residual weights; the other bytes are masked off below
+    const int o = RO + rc0 + rq;
+    const uint32_t* rw = reinterpret_cast<const uint32_t*>(p + (o & ~3));
+    const uint32_t rex = __byte_perm(rw[0], rw[1], lr.x + (uint32_t)(o & 3) * 0x1111u);
+    const uint32_t E = (lr.y & rex) | (~lr.y & ((ln.y & ne) | (~ln.y & modal4)));
+    nq += (int)(ln.x >> 16);
+    rq += (int)(lr.x >> 16);
+    if constexpr (DT == NSQ_NSZ_FP32) {
+      // byte 0: exponent i, byte 1: sign i (0/1); times 2^23 puts them at
+      // bits 23..30 and 31 (the garbage in bytes 2..3 leaves the word)
+      const uint32_t sb = spread4((S16 >> (4 * q)) & 15u);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int k = 4 * q + i;
-      const uint32_t e = (E >> (8 * i)) & 0xFFu, s = (S16 >> k) & 1u;
-      if constexpr (DT == NSQ_NSZ_FP32) {
-        v[k] = (s << 31) | (e << 23) | mant[k];
-      } else if constexpr (DT == NSQ_NSZ_FP16) {
-        v[k] = (s << 15) | ((e & 0x1Fu) << 10) | mant[k];
-      } else {
-        v[k] = (s << 15) | (e << 7) | mant[k];
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t se = __byte_perm(E, sb, (uint32_t)(i | ((4 + i) << 4)));
+        v[4 * q + i] = (mant[4 * q + i] & 0x7FFFFFu) | (se * 8388608u);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int k = 4 * q + i;
+        const uint32_t e = (E >> (8 * i)) & 0xFFu, sg = (S16 >> k) & 1u;
+        if constexpr (DT == NSQ_NSZ_FP16) {
+          v[k] = (sg << 15) | ((e & 0x1Fu) << 10) | mant[k];
+        } else {
+          v[k] = (sg << 15) | (e << 7) | mant[k];
+        }
       }
     }
   }
@@ -260,13 +310,13 @@ struct DecodeParams {
 };
 
 template <int DT>
-__global__ void __launch_bounds__(kNszWarps * 32) nsz_decode_kernel(DecodeParams p) {
+__global__ void __launch_bounds__(kNszWarps * 32, 3) nsz_decode_kernel(DecodeParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ uint32_t sel[16];
+  __shared__ NszLut lut;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   WarpRing<DT> ring;
   ring_setup<DT>(smem, warp, ring);
-  init_sel_table(sel);
+  init_nsz_lut(&lut);
   if (lane == 0)
     for (int s = 0; s < kNszDepth; ++s) mbar_init(&ring.bar[s], 1);
   fence_mbar_init();
@@ -280,9 +330,10 @@ __global__ void __launch_bounds__(kNszWarps * 32) nsz_decode_kernel(DecodeParams
   if (nt <= 0) return;
   if (lane == 0)
     for (int64_t i = 0; i < imin64(nt, kNszDepth); ++i) ring.issue(p.tiles, p.off, wa + i, (int)i);
-  for (int64_t i = 0; i < nt; ++i) {
-    const int s = (int)(i % kNszDepth);
-    const bool ok = __all_sync(0xFFFFFFFFu, mbar_wait_bounded(&ring.bar[s], (uint32_t)((i / kNszDepth) & 1)));
+  int s = 0;
+  uint32_t phase = 0;  // stage s of tile i: i % kNszDepth, phase (i / kNszDepth) & 1
+  for (int64_t i = 0; i < nt; ++i, s = s + 1 == kNszDepth ? 0 : s + 1, phase ^= s == 0 ? 1u : 0u) {
+    const bool ok = __all_sync(0xFFFFFFFFu, mbar_wait_bounded(&ring.bar[s], phase));
     if (!ok) {
       if (lane == 0) ring_drain<DT>(ring, i + 1, imin64(nt, i + kNszDepth));
       return;
@@ -290,7 +341,10 @@ __global__ void __launch_bounds__(kNszWarps * 32) nsz_decode_kernel(DecodeParams
     const int64_t t = wa + i;
     const int n = (int)imin64(kNszW, p.count - t * kNszW);
     uint32_t v[16], vm;
-    nsz_decode16<DT>(ring.at(s), n, lane, sel, v, vm);
+    if (n == kNszW)
+      nsz_decode16<DT, true>(ring.at(s), n, lane, lut, v, vm);
+    else
+      nsz_decode16<DT, false>(ring.at(s), n, lane, lut, v, vm);
     __syncwarp();
     if (lane == 0 && i + kNszDepth < nt) {
       fence_proxy_async_smem();
@@ -361,19 +415,25 @@ __device__ __forceinline__ void flush_rows(float (&acc)[MT], int64_t cur, int64_
   }
 }
 
-// ALIGNED: K % 16 == 0 and x 16-byte aligned (a lane's 16 weights lie in one
-// row; x read as float4).  Otherwise every weight is placed on its own.
-template <int DT, int MT, bool ALIGNED>
-__global__ void __launch_bounds__(kNszWarps * 32) zipgemm_kernel(ZipParams p) {
+// Placement modes.  kRowTile: K % 512 == 0 and x 16-byte aligned: every
+// tile is 512 weights of one row, so the row and column of a tile are
+// warp-uniform and no weight needs a range check.  kAligned: K % 16 == 0 and
+// x 16-byte aligned: a lane's 16 weights lie in one row (x read as float4).
+// kGeneral: every weight is placed on its own.
+enum : int { kGeneral = 0, kAligned = 1, kRowTile = 2 };
+
+template <int DT, int MT, int MODE>
+__global__ void __launch_bounds__(kNszWarps * 32, MT <= 2 ? 3 : 2) zipgemm_kernel(ZipParams p) {
+  constexpr bool ALIGNED = MODE == kAligned;
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ uint32_t sel[16];
+  __shared__ NszLut lut;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   WarpRing<DT> ring;
   ring_setup<DT>(smem, warp, ring);
   float* ys = reinterpret_cast<float*>(smem + ring_bytes(NszFmt<DT>::kStage));
   const int64_t r0 = (int64_t)blockIdx.x * p.rpc, r1 = min(p.N, r0 + p.rpc);
   if (r0 >= r1) return;  // whole CTA: nothing below synchronizes yet
-  init_sel_table(sel);
+  init_nsz_lut(&lut);
   if (lane == 0)
     for (int s = 0; s < kNszDepth; ++s) mbar_init(&ring.bar[s], 1);
   for (int64_t i = threadIdx.x; i < MT * p.rpc; i += blockDim.x) ys[i] = 0.f;
@@ -395,23 +455,75 @@ __global__ void __launch_bounds__(kNszWarps * 32) zipgemm_kernel(ZipParams p) {
     int64_t cur = -1;
     int64_t e0 = wa * kNszW + 16 * lane;
     int64_t row = e0 / p.K, col = e0 - row * p.K;
-    for (int64_t i = 0; i < nt; ++i) {
-      const int s = (int)(i % kNszDepth);
-      if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(&ring.bar[s], (uint32_t)((i / kNszDepth) & 1)))) {
+    // kRowTile: warp-uniform position of the tile: output row (relative to
+    // r0) and first column
+    const int kt = (int)(p.K / kNszW), K32 = (int)p.K;
+    int trow = MODE == kRowTile ? (int)(wa / kt - r0) : 0;
+    int tcol = MODE == kRowTile ? (int)(wa % kt) * kNszW : 0;
+    bool pending = false;
+    auto flush_tile_row = [&]() {
+#pragma unroll
+      for (int m = 0; m < MT; ++m) {
+        float a = acc[m];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xFFFFFFFFu, a, o);
+        if (lane == 0 && m < p.mv) atomicAdd(&ys[m * p.rpc + trow], a);
+        acc[m] = 0.f;
+      }
+    };
+    int s = 0;
+    uint32_t phase = 0;  // stage s of tile i: i % kNszDepth, phase (i / kNszDepth) & 1
+    for (int64_t i = 0; i < nt; ++i, s = s + 1 == kNszDepth ? 0 : s + 1, phase ^= s == 0 ? 1u : 0u) {
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(&ring.bar[s], phase))) {
         if (lane == 0) ring_drain<DT>(ring, i + 1, imin64(nt, i + kNszDepth));
         ok = false;
         break;
       }
       const int64_t t = wa + i;
-      const int n = (int)imin64(kNszW, p.count - t * kNszW);
       uint32_t v[16], vm;
-      nsz_decode16<DT>(ring.at(s), n, lane, sel, v, vm);
+      if constexpr (MODE == kRowTile) {
+        nsz_decode16<DT, true>(ring.at(s), kNszW, lane, lut, v, vm);
+      } else {
+        const int n = (int)imin64(kNszW, p.count - t * kNszW);
+        if (n == kNszW)
+          nsz_decode16<DT, true>(ring.at(s), n, lane, lut, v, vm);
+        else
+          nsz_decode16<DT, false>(ring.at(s), n, lane, lut, v, vm);
+      }
       __syncwarp();
       if (lane == 0 && i + kNszDepth < nt) {
         fence_proxy_async_smem();
         ring.issue(p.tiles, p.off, t + kNszDepth, s);
       }
-      if constexpr (ALIGNED) {
+      if constexpr (MODE == kRowTile) {
+        float w[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) w[j] = nsz_value<DT>(v[j]);
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          if (m < p.mv) {
+            const float4* xp = reinterpret_cast<const float4*>(p.x + (size_t)m * K32 + tcol + 16 * lane);
+            float a = acc[m];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float4 xv = __ldg(xp + j);
+              a = fmaf(w[4 * j], xv.x, a);
+              a = fmaf(w[4 * j + 1], xv.y, a);
+              a = fmaf(w[4 * j + 2], xv.z, a);
+              a = fmaf(w[4 * j + 3], xv.w, a);
+            }
+            acc[m] = a;
+          }
+        }
+        pending = true;
+        tcol += kNszW;
+        if (tcol == K32) {
+          flush_tile_row();
+          pending = false;
+          tcol = 0;
+          ++trow;
+        }
+      } else if constexpr (ALIGNED) {
         const bool valid = vm != 0 && e0 >= E0 && e0 < E1;
         const int64_t r = valid ? row : -1;
         if (__any_sync(0xFFFFFFFFu, r != cur)) {
@@ -467,6 +579,9 @@ __global__ void __launch_bounds__(kNszWarps * 32) zipgemm_kernel(ZipParams p) {
     if constexpr (ALIGNED) {
       if (ok) flush_rows<MT>(acc, cur, -1, lane, ys, p.rpc, r0);
     }
+    if constexpr (MODE == kRowTile) {
+      if (ok && pending) flush_tile_row();
+    }
   }
   if (!__syncthreads_and(ok)) return;
   const int64_t rows = r1 - r0;
@@ -502,7 +617,7 @@ static int run_decode(const uint8_t* tiles, const uint32_t* off, int64_t count, 
   return cudaGetLastError() == cudaSuccess ? NSQ_OK : NSQ_ERR_CUDA;
 }
 
-template <int DT, int MT, bool AL>
+template <int DT, int MT, int AL>
 static int launch_zip(ZipParams p, cudaStream_t st, int num_sms) {
   constexpr size_t kYsMax = 48 * 1024;  // row buffer bound (floats: MT * rpc)
   const size_t base = ring_bytes(NszFmt<DT>::kStage);
@@ -522,7 +637,7 @@ static int launch_zip(ZipParams p, cudaStream_t st, int num_sms) {
   return cudaGetLastError() == cudaSuccess ? NSQ_OK : NSQ_ERR_CUDA;
 }
 
-template <int DT, bool AL>
+template <int DT, int AL>
 static int launch_zip_m(ZipParams p, int mt, cudaStream_t st, int num_sms) {
   switch (mt) {
     case 1: return launch_zip<DT, 1, AL>(p, st, num_sms);
@@ -535,12 +650,15 @@ static int launch_zip_m(ZipParams p, int mt, cudaStream_t st, int num_sms) {
 template <int DT>
 static int run_zip(const uint8_t* tiles, const uint32_t* off, const float* x, float* y, int64_t M, int64_t N,
                    int64_t K, cudaStream_t st, int num_sms) {
-  const bool al = K % 16 == 0 && !(reinterpret_cast<uintptr_t>(x) & 15);
+  const bool xa = !(reinterpret_cast<uintptr_t>(x) & 15);
+  const int mode = xa && K % kNszW == 0 && K < (1ll << 30) ? kRowTile : xa && K % 16 == 0 ? kAligned : kGeneral;
   for (int64_t m0 = 0; m0 < M; m0 += 8) {
     const int mv = (int)imin64(8, M - m0);
     const int mt = mv == 1 ? 1 : mv == 2 ? 2 : mv <= 4 ? 4 : 8;
     ZipParams p{tiles, off, x + m0 * K, y + m0 * N, N, K, N * K, 0, mv};
-    const int rc = al ? launch_zip_m<DT, true>(p, mt, st, num_sms) : launch_zip_m<DT, false>(p, mt, st, num_sms);
+    const int rc = mode == kRowTile  ? launch_zip_m<DT, kRowTile>(p, mt, st, num_sms)
+                   : mode == kAligned ? launch_zip_m<DT, kAligned>(p, mt, st, num_sms)
+                                      : launch_zip_m<DT, kGeneral>(p, mt, st, num_sms);
     if (rc) return rc;
   }
   return NSQ_OK;
