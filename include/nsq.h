@@ -276,7 +276,7 @@ int nsq_gemv_multi_xchg(const nsq_xsegment *segs, int nseg, const float *x, int6
  * tiles of 512 weights (the last may be shorter), each [header 8][match
  * bitmap][near bitmap][near deltas][residual exponents][mantissas][signs]
  * padded to 64 bytes.  Decoding is lossless: the original FP32 / FP16 / BF16
- * bits come back exactly as nsz_decoder.rs:19-218 restores them. */
+ * bits come back exactly as nsz_decoder.rs:19-196 restores them. */
 #define NSQ_NSZ_FP32 0
 #define NSQ_NSZ_FP16 1
 #define NSQ_NSZ_BF16 2

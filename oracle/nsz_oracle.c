@@ -8,11 +8,11 @@
  *
  * Reference routines restated (paths relative to nodestor/):
  *
- *   orc_nsz_encode_tile   crates/nodestor-formats/src/nsz_encoder.rs:75-283
+ *   orc_nsz_encode_tile   crates/nodestor-formats/src/nsz_encoder.rs:79-275
  *                         (encode_tile_fp32 / _fp16 / _bf16), find_modal_exp
- *                         :321-335, pack_bits :338-347, serialization
- *                         NszTile::to_bytes nsz_format.rs:301-316
- *   orc_nsz_decode_tile   crates/nodestor-formats/src/nsz_decoder.rs:19-218
+ *                         :300-314, pack_bits :317-326, serialization
+ *                         NszTile::to_bytes nsz_format.rs:291-307
+ *   orc_nsz_decode_tile   crates/nodestor-formats/src/nsz_decoder.rs:19-196
  *                         (decode_tile_fp32 / _fp16 / _bf16), sections laid
  *                         out as NszTile::to_bytes writes them
  *   orc_nsz_matmul        the ZipGEMM operator (VulkanEngine::zipgemm,
@@ -30,11 +30,11 @@
  *
  * Two behaviours of the reference kept as they are:
  *  - the encoder's near test `exp == modal.wrapping_add(1) || (modal > 0 &&
- *    exp == modal - 1)` (nsz_encoder.rs:108) takes exponent 0 as "near" when
+ *    exp == modal - 1)` (nsz_encoder.rs:111, :180, :243) takes exponent 0 as "near" when
  *    the modal exponent is 255, with delta 0, which the decoder reads back as
  *    254: such a tile is not lossless (orc_nsz_encode_tile with
  *    reference_quirks = 1 reproduces it; 0 stores that exponent as a residual);
- *  - the decoder's out-of-range reads return 0 (nsz_decoder.rs:39-45, 48-53).
+ *  - the decoder's out-of-range reads return 0 (nsz_decoder.rs:41-45, 54-58).
  *
  * Pin: the reference's own converter output micro_modelo_ignition.nsz
  * (nsz_convert.rs) decodes and re-encodes to the same bytes
@@ -64,7 +64,7 @@ static int64_t tile_bytes(int n, int num_near, int num_res, int dtype) {
   return (raw + NSZ_ALIGN - 1) / NSZ_ALIGN * NSZ_ALIGN;
 }
 
-/* Exponent, mantissa and sign of element i (nsz_encoder.rs:82-90, 162-166, 218-222). */
+/* Exponent, mantissa and sign of element i (nsz_encoder.rs:86-93, 161-165, 224-228). */
 static void split(const void *w, int64_t i, int dtype, uint8_t *e, uint32_t *m, uint8_t *s) {
   if (dtype == NSZ_FP32) {
     uint32_t b = ((const uint32_t *)w)[i];

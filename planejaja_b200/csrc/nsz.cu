@@ -2,13 +2,13 @@
 // index, the device decoder and ZipGEMM, the fused decompress + GEMV.
 //
 // Tile bytes (crates/nodestor-formats/src/nsz_format.rs:13-44, written by
-// NszTile::to_bytes :301-316): [modal u8][num_res u16][dtype u8][num_near
+// NszTile::to_bytes :291-307): [modal u8][num_res u16][dtype u8][num_near
 // u16][2] | match bitmap B | near bitmap B | near deltas ceil(num_near/8) |
 // residual exponents num_res | mantissas n*MB | signs B | pad to 64, with
 // B = ceil(n/8), MB = 3 / 2 / 1 bytes (FP32 / FP16 / BF16).  Weight i:
 // exponent = modal if match bit i, modal +- 1 (next near delta bit) if near
 // bit i, else the next residual byte; mantissa and sign verbatim
-// (nsz_decoder.rs:19-218).
+// (nsz_decoder.rs:19-196).
 //
 // Device design.  Every warp owns a contiguous run of tiles and keeps
 // kDepth of them in flight: lane 0 moves each whole tile (its size from the

@@ -14,7 +14,7 @@
   zipgemm(w, x, m, k, n)        -> y = x . W^T from an NSZ (TCA-TBE) tensor,
                                    decompressed in registers (lib.rs:124-151)
   nsz_decode(w)                 -> the NSZ tensor's original weights, bit-exact
-                                   (nsz_decoder.rs:19-218)
+                                   (nsz_decoder.rs:19-196)
 
 Device memory, streams and the output buffers come from PyTorch; every
 computation is a call into libnsq.so.  Like the reference, calls are

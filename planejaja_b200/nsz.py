@@ -20,7 +20,7 @@ bitmap | near bitmap | near deltas | residual exponents | mantissas | signs,
 padded to 64 bytes.  `encode` writes exactly the reference encoder's bytes
 (tests compare it with the oracle's restatement), with one deliberate change:
 when a tile's modal exponent is 255 the reference encoder files exponent 0 as
-"near" (nsz_encoder.rs:108, wrapping_add) and its decoder restores 254; here
+"near" (nsz_encoder.rs:111, wrapping_add) and its decoder restores 254; here
 that exponent is a residual, so every stream this module writes is lossless.
 
 The device side (decode and ZipGEMM) takes a tile stream plus the offset

@@ -80,33 +80,33 @@ def test_writer_reproduces_reference_layout(tmp_path, oracle, nszg):
 
 
 # ------------------------------------------------- reference unit tests
-def test_encode_all_same(oracle):  # nsz_encoder.rs:352-366
+def test_encode_all_same(oracle):  # nsz_encoder.rs:333-347
     t = oracle.nsz_encode_tile(np.ones(512, np.float32))
     assert t[0] == 127 and t[1:3] == b"\0\0" and t[4:6] == b"\0\0"
     assert t[8:72] == b"\xff" * 64
 
 
-def test_encode_mixed(oracle):  # nsz_encoder.rs:369-381
+def test_encode_mixed(oracle):  # nsz_encoder.rs:350-361
     w = np.concatenate([np.ones(400), np.full(80, 2.0), np.full(32, 100.0)]).astype(np.float32)
     t = oracle.nsz_encode_tile(w)
     assert t[0] == 127
     assert struct.unpack("<H", t[4:6])[0] == 80 and struct.unpack("<H", t[1:3])[0] == 32
 
 
-def test_pack_bits_order(oracle):  # nsz_encoder.rs:384-390: bit i of byte i/8, LSB first
+def test_pack_bits_order(oracle):  # nsz_encoder.rs:364-370: bit i of byte i/8, LSB first
     w = np.zeros(512, np.float32)
     w[[0, 2, 3, 7, 8]] = 1.0  # exponent 127 on these, 0 elsewhere: modal 0, these residual
     t = oracle.nsz_encode_tile(w)
     assert t[8] == 0b01110010 and t[9] == 0b11111110  # match bitmap = complement of those bits
 
 
-def test_compression_ratio_and_tiles(oracle):  # nsz_encoder.rs:393-405, :408-417
+def test_compression_ratio_and_tiles(oracle):  # nsz_encoder.rs:373-385, :388-396
     assert len(oracle.nsz_encode_tile(np.full(512, 0.02, np.float32))) < 2048
     s = oracle.nsz_encode(np.ones(1024, np.float32))
     assert oracle.nsz_offsets(s, 1024).size == 3  # 2 tiles
 
 
-def test_find_modal_first_maximum(oracle):  # nsz_encoder.rs:420-424 and ties
+def test_find_modal_first_maximum(oracle):  # nsz_encoder.rs:399-402 and ties
     e = [127, 127, 127, 128, 126, 127, 127]
     w = np.array([math.ldexp(1.0, x - 127) for x in e], np.float32)
     assert oracle.nsz_encode_tile(w)[0] == 127
@@ -115,7 +115,7 @@ def test_find_modal_first_maximum(oracle):  # nsz_encoder.rs:420-424 and ties
 
 
 @pytest.mark.parametrize("case", ["ones", "zeros", "negative", "mixed", "subnormals", "multi", "special"])
-def test_reference_round_trips(oracle, case):  # nsz_decoder.rs:243-349
+def test_reference_round_trips(oracle, case):  # nsz_decoder.rs:240-349
     if case == "ones":
         w = np.ones(512, np.float32)
     elif case == "zeros":
@@ -139,7 +139,7 @@ def test_reference_round_trips(oracle, case):  # nsz_decoder.rs:243-349
     assert np.array_equal(Z.encode(w), s)
 
 
-def test_file_header_and_entry_round_trip():  # nsz_format.rs:345-380
+def test_file_header_and_entry_round_trip():  # nsz_format.rs:339-374
     e = Z.Entry("blk.0.attn_q.weight", Z.FP32, 16384, 256, 12000, 32, 4096, (64, 64, 0, 0))
     b = e.to_bytes()
     assert len(b) == 128 and Z.Entry.from_bytes(b) == e
