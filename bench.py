@@ -20,6 +20,10 @@ NVLink (the all-gather a tensor-parallel decode needs, fused into the GEMV;
 nsq_gemv_multi_xchg), strong scaling, total work fixed.  --exchange nccl
 runs the GEMV followed by an NCCL all_gather per projection instead.
 
+--workload l2-7b: Llama-2-7B in Q4_0 (q, k, v, o [4096 x 4096], gate / up
+[11008 x 4096], down [4096 x 11008]; 32 layer copies, 3.64 GB per step), the
+7 projections of a layer in the same 4 fused launches.
+
 --workload l2-70b-ffn --tokens {1,16}: the Llama-2-70B FFN (gate|up [28672 x 8192]
 Q4_K, down [8192 x 28672] Q4_K; 8 layer copies, 3.17 GB), the row-sharded
 configuration measured at 1/2/4/8 GPUs.
@@ -72,6 +76,18 @@ WORKLOADS = {
         "layers": 32,
         "metric": "decode GEMV HBM GB/s (Llama-3-8B Q4_K_M, M={m})",
         "desc": "llama3-8b Q4_K_M decode, M={m}, {layers} layers x 7 projections per step",
+    },
+    # Llama-2-7B, Q4_0 everywhere (q, k, v, o [4096 x 4096], gate / up
+    # [11008 x 4096], down [4096 x 11008]; 113.8 MB per layer)
+    "l2-7b": {
+        "spec": [("q", 4096, 4096, 2), ("k", 4096, 4096, 2), ("v", 4096, 4096, 2), ("o", 4096, 4096, 2),
+                 ("gate", 11008, 4096, 2), ("up", 11008, 4096, 2), ("down", 4096, 11008, 2)],
+        "act_of": {"q": 0, "k": 0, "v": 0, "o": 1, "gate": 2, "up": 2, "down": 3},
+        "act_k": [4096, 4096, 4096, 11008],
+        "groups": [(0, ["q", "k", "v"]), (1, ["o"]), (2, ["gate", "up"]), (3, ["down"])],
+        "layers": 32,
+        "metric": "decode GEMV HBM GB/s (Llama-2-7B Q4_0, M={m})",
+        "desc": "llama2-7b Q4_0 decode, M={m}, {layers} layers x 7 projections per step",
     },
     # Llama-2-70B FFN, Q4_K (gate/up [28672 x 8192], down [8192 x 28672])
     "l2-70b-ffn": {
@@ -465,10 +481,12 @@ def run_gpu(args, rank, world, local_rank):
     # projection, 2 x [14336 x 4096]) over the layer copies
     if not args.skip_roofline:
         rows, _ = layers[0]["gate"]
+        gt = TYPE_OF["gate"]
+        gname = fmt(gt).name
         gi = [i for i, (a, names) in enumerate(GROUPS) if "gate" in names][0]
         ga = GROUPS[gi][0]
         KG = ACT_K[ga]
-        gbytes = 2 * fmt(12).tensor_bytes(rows, KG) + M * KG * 4 + 2 * M * rows * 4
+        gbytes = 2 * fmt(gt).tensor_bytes(rows, KG) + M * KG * 4 + 2 * M * rows * 4
         st = torch.cuda.current_stream(dev).cuda_stream
         gu = [seg_arrays[li][gi][2] for li in range(L)]
         reps = max(4, 256 // L) * L
@@ -490,7 +508,7 @@ def run_gpu(args, rank, world, local_rank):
             key = "gemv_fused_q4k_m1_gate_up" if WORKLOAD == "l3-8b" and M == 1 and world == 1 else None
             traffic = json.load(open(tp)).get(key) if key else None
         result["roofline"] = {"bound": "hbm",
-                              "kernel": f"gemv_fused_kernel<M={M},Q4_K> gate|up 2 x [{rows}x{KG}] (FFN input projection)",
+                              "kernel": f"gemv_fused_kernel<M={M},{gname}> gate|up 2 x [{rows}x{KG}] (FFN input projection)",
                               "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                               "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind,
                               "frac_of_nominal_8tbs": round(achieved / NOMINAL_HBM_GBS, 4),
@@ -504,19 +522,19 @@ def run_gpu(args, rank, world, local_rank):
         xp = T.randn(pm, KG, device=dev).to(T.bfloat16)
         yp = T.empty(pm, rows, dtype=T.bfloat16, device=dev)
         for _ in range(3):
-            lib.nsq_gemm_bf16(wq.data_ptr(), 12, 0, xp.data_ptr(), yp.data_ptr(), pm, rows, KG, st)
+            lib.nsq_gemm_bf16(wq.data_ptr(), gt, 0, xp.data_ptr(), yp.data_ptr(), pm, rows, KG, st)
         torch.cuda.synchronize()
         p0, p1 = T.cuda.Event(enable_timing=True), T.cuda.Event(enable_timing=True)
         preps = 20
         p0.record()
         for i in range(preps):
-            lib.nsq_gemm_bf16(layers[i % L]["gate"][1].data_ptr(), 12, 0, xp.data_ptr(), yp.data_ptr(), pm, rows,
+            lib.nsq_gemm_bf16(layers[i % L]["gate"][1].data_ptr(), gt, 0, xp.data_ptr(), yp.data_ptr(), pm, rows,
                               KG, st)
         p1.record()
         torch.cuda.synchronize()
         pms = p0.elapsed_time(p1) / preps
         tflops = 2.0 * pm * rows * KG / (pms * 1e-3) / 1e12
-        result["prefill"] = {"kernel": "gemm_tc_kernel<Q4_K> (tcgen05, bf16, fp32 TMEM accumulate)",
+        result["prefill"] = {"kernel": f"gemm_tc_kernel<{gname}> (tcgen05, bf16, fp32 TMEM accumulate)",
                              "shape": f"M={pm} N={rows} K={KG}", "tflops": round(tflops, 1),
                              "ms": round(pms, 4), "peak_tflops": bf16_peak, "peak_kind": peak_kind,
                              "frac": round(tflops / bf16_peak, 4)}

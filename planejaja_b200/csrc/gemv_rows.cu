@@ -267,29 +267,55 @@ struct Piece<NSQ_TYPE_Q6_K, NSQ_Q6K_NODESTOR, M> {
 
 // Q4_0: 8 blocks [d][qs 16]: low nibbles = weights 0..15, high = 16..31
 // (dequant_q4.comp:40-61).
+// A piece (144 bytes) starts 16-byte aligned, so it is read as 16-byte words
+// in two halves (words 0..19 and 16..35) and every block field sits at a
+// compile-time position: even blocks start word-aligned (scale in the low
+// half-word, quants shifted by 2 bytes), odd blocks 2 bytes into a word
+// (scale in the high half-word, quants word-aligned).
 template <int LAYOUT, int M>
 struct Piece<NSQ_TYPE_Q4_0, LAYOUT, M> {
   __device__ static void run(const uint8_t* pc, const uint8_t* xp, int xstride, float (&acc)[M]) {
+    const uint4* pv = reinterpret_cast<const uint4*>(pc);
 #pragma unroll
-    for (int g = 0; g < 8; ++g) {
-      const uint8_t* blk = pc + 18 * g;
-      uint32_t w5[5];
-      ld_words_unaligned<5>(blk, w5);  // bytes 0..19 of the block
-      const float d = h2f((uint16_t)(w5[0] & 0xFFFF));
-      uint32_t q[8];
+    for (int h = 0; h < 2; ++h) {
+      uint32_t w[20];  // words 16h .. 16h + 19 of the piece
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint32_t qs = __funnelshift_r(w5[i], w5[i + 1], 16);  // bytes 2+4i .. 5+4i
-        q[i] = qs & 0x0F0F0F0Fu;
-        q[i + 4] = qs & 0xF0F0F0F0u;  // 16 * high nibble
+      for (int i = 0; i < 5; ++i) {
+        const uint4 t = pv[4 * h + i];
+        w[4 * i] = t.x; w[4 * i + 1] = t.y; w[4 * i + 2] = t.z; w[4 * i + 3] = t.w;
       }
 #pragma unroll
-      for (int m = 0; m < M; ++m) {
-        XG x;
-        lds_xg(xp + m * xstride + g * 80, x);
-        int s0, s1;
-        dot8<false>(q, x, s0, s1);
-        acc[m] = fmaf(x.sx * d, (float)(s0 - 8 * x.t0) + 0.0625f * (float)(s1 - 128 * x.t1), acc[m]);
+      for (int b = 0; b < 4; ++b) {
+        const int g = 4 * h + b;
+        const int byte0 = 18 * g - 64 * h;  // block start, relative to word 16h
+        const int wi = byte0 >> 2;
+        float d;
+        uint32_t q[8];
+        if ((byte0 & 3) == 0) {
+          d = h2f((uint16_t)(w[wi] & 0xFFFF));
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint32_t qs = __funnelshift_r(w[wi + i], w[wi + i + 1], 16);  // block bytes 2+4i .. 5+4i
+            q[i] = qs & 0x0F0F0F0Fu;
+            q[i + 4] = qs & 0xF0F0F0F0u;  // 16 * high nibble
+          }
+        } else {
+          d = h2f((uint16_t)(w[wi] >> 16));
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint32_t qs = w[wi + 1 + i];
+            q[i] = qs & 0x0F0F0F0Fu;
+            q[i + 4] = qs & 0xF0F0F0F0u;
+          }
+        }
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+          XG x;
+          lds_xg(xp + m * xstride + g * 80, x);
+          int s0, s1;
+          dot8<false>(q, x, s0, s1);
+          acc[m] = fmaf(x.sx * d, (float)(s0 - 8 * x.t0) + 0.0625f * (float)(s1 - 128 * x.t1), acc[m]);
+        }
       }
     }
   }
@@ -343,6 +369,9 @@ struct FusedParams {
   int R, KS, PPS, npieces, nchunks;
   int xstride;          // bytes per token of per-stage activation records (workspace mode)
   int stage_bytes, nstages, max_pitch;
+  int npre;             // stages whose weights are copied before the dependency wait (<= nstages)
+  int l2hint;           // 1: weight copies evict_first in the L2; 2: also activation reads evict_last
+  int xpipe;            // self-prepared mode: a thread loads its next activation group before quantising
   int Rblk;             // rows per block walked by the cursor: R, or R / 2 with the SwiGLU epilogue
   const float* res[NSQ_MAX_SEGMENTS];  // residual-add epilogue: y = res + x . W^T (may alias y)
   int C;                // self-prepared mode: CTAs per cluster sharing the activation quantisation
@@ -380,16 +409,27 @@ __device__ __forceinline__ void run_piece(int code, const uint8_t* pc, const uin
   }
 }
 
+// Loads one group of 32 activations (8 x 16 bytes); with `hint`, at L2
+// priority evict_last.
+__device__ __forceinline__ void load_group(const float* __restrict__ xs, float4 (&f)[8], bool hint, uint64_t pol) {
+  const float4* q = reinterpret_cast<const float4*>(xs);
+  if (hint) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = ldg_f4_hint(q + i, pol);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = __ldg(q + i);
+  }
+}
+
 // Quantize one group of 32 activations into an 80-byte record (same math as
 // prepare_x_kernel in gemv.cu, one thread per group), returned as 5 words of
 // 16 bytes.
-__device__ __forceinline__ void quantize_group(const float* __restrict__ xs, uint4 (&o)[5]) {
+__device__ __forceinline__ void quantize_group(const float4 (&f)[8], uint4 (&o)[5]) {
   float v[32];
-  const float4* q = reinterpret_cast<const float4*>(xs);
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const float4 f = __ldg(q + i);
-    v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+    v[4 * i] = f[i].x; v[4 * i + 1] = f[i].y; v[4 * i + 2] = f[i].z; v[4 * i + 3] = f[i].w;
   }
   float amax = 0.f;
 #pragma unroll
@@ -507,6 +547,12 @@ __global__ void __launch_bounds__(kRowsThreads, 4) gemv_fused_kernel(const __gri
     // producer warp: lane r issues row r's bulk copy, lane 0 the barrier
     // bookkeeping and the activation copies
     if (r_begin < r_end) {
+      const uint64_t wpol = l2_policy_evict_first(), xpol = l2_policy_evict_last();
+      // weight row runs are read once: evict them first (l2hint)
+      auto copy_w = [&](void* dst, const void* src, int bytes, uint64_t* bar) {
+        if (p.l2hint) bulk_g2s_hint(dst, src, (uint32_t)bytes, bar, wpol);
+        else bulk_g2s(dst, src, (uint32_t)bytes, bar);
+      };
       auto issue = [&](const ItemCursor& it, int s, bool with_w, bool with_x) {
         const FSeg& sg = p.seg[it.seg];
         const int64_t off = (int64_t)it.c * sg.chunk_bytes;
@@ -524,18 +570,21 @@ __global__ void __launch_bounds__(kRowsThreads, 4) gemv_fused_kernel(const __gri
             for (int r = lane; r < 2 * (int)it.rows; r += 32) {
               const bool up = r >= (int)it.rows;
               const int rr = up ? r - (int)it.rows : r;
-              bulk_g2s(slot + (up ? rr + p.Rblk : rr) * sg.pitch, (up ? su.w : sg.w) + (it.row0 + rr) * sg.RB + off,
-                       rbytes, &full[s]);
+              copy_w(slot + (up ? rr + p.Rblk : rr) * sg.pitch, (up ? su.w : sg.w) + (it.row0 + rr) * sg.RB + off,
+                     rbytes, &full[s]);
             }
           } else {
             for (int r = lane; r < (int)it.rows; r += 32)
-              bulk_g2s(slot + r * sg.pitch, sg.w + (it.row0 + r) * sg.RB + off, rbytes, &full[s]);
+              copy_w(slot + r * sg.pitch, sg.w + (it.row0 + r) * sg.RB + off, rbytes, &full[s]);
           }
         }
         if (!XSELF && with_x && lane == 0) {
           uint8_t* xs = slot + p.R * p.max_pitch;
-          for (int m = 0; m < M; ++m)
-            bulk_g2s(xs + m * p.xstride, p.xg + m * p.GX + (int64_t)it.c * p.PPS * 8, ng * 80, &full[s]);
+          for (int m = 0; m < M; ++m) {
+            const void* src = p.xg + m * p.GX + (int64_t)it.c * p.PPS * 8;
+            if (p.l2hint >= 2) bulk_g2s_hint(xs + m * p.xstride, src, (uint32_t)(ng * 80), &full[s], xpol);
+            else bulk_g2s(xs + m * p.xstride, src, (uint32_t)(ng * 80), &full[s]);
+          }
         }
       };
       // weights of the first stages do not depend on the previous kernel
@@ -544,7 +593,7 @@ __global__ void __launch_bounds__(kRowsThreads, 4) gemv_fused_kernel(const __gri
       ItemCursor pre[8];
       int npre = 0;
       bool more = true;
-      while (more && npre < p.nstages) {
+      while (more && npre < p.npre) {
         pre[npre] = it;
         issue(it, npre, true, false);
         ++npre;
@@ -603,10 +652,13 @@ __global__ void __launch_bounds__(kRowsThreads, 4) gemv_fused_kernel(const __gri
       const int64_t ng = (int64_t)M * p.GX;
       const int q = clustered ? (int)cluster_rank() : 0, C = clustered ? p.C : 1;
       if (clustered) cluster_wait_acquire();
-      for (int64_t gi = ng * q / C + ct; gi < ng * (q + 1) / C; gi += kRowsConsumers * 32) {
+      const bool xh = p.l2hint >= 2;
+      const uint64_t xpol = l2_policy_evict_last();
+      const int64_t g_end = ng * (q + 1) / C;
+      auto put = [&](int64_t gi, const float4 (&f)[8]) {
         const int64_t m = gi / p.GX, g = gi - m * p.GX;
         uint4 o[5];
-        quantize_group(p.x + m * p.K + 32 * g, o);
+        quantize_group(f, o);
         uint8_t* rec = xsm + (m * p.GX + g) * 80;
         if (clustered) {
           for (int qq = 0; qq < C; ++qq) {
@@ -619,6 +671,28 @@ __global__ void __launch_bounds__(kRowsThreads, 4) gemv_fused_kernel(const __gri
 #pragma unroll
           for (int i = 0; i < 5; ++i) d[i] = o[i];
         }
+      };
+      auto src = [&](int64_t gi) {
+        const int64_t m = gi / p.GX, g = gi - m * p.GX;
+        return p.x + m * p.K + 32 * g;
+      };
+      constexpr int kStride = kRowsConsumers * 32;
+      int64_t gi = ng * q / C + ct;
+      if (p.xpipe) {
+        // two groups per round: both groups' loads are in flight before the
+        // first is quantised (one memory round trip instead of two)
+        for (; gi + kStride < g_end; gi += 2 * kStride) {
+          float4 fa[8], fb[8];
+          load_group(src(gi), fa, xh, xpol);
+          load_group(src(gi + kStride), fb, xh, xpol);
+          put(gi, fa);
+          put(gi + kStride, fb);
+        }
+      }
+      for (; gi < g_end; gi += kStride) {
+        float4 fa[8];
+        load_group(src(gi), fa, xh, xpol);
+        put(gi, fa);
       }
       if (clustered) {
         // cluster phase 2: all records of the cluster have landed
@@ -815,6 +889,11 @@ static bool plan_fused(const nsq_segment* segs, int nseg, int64_t K, int M, bool
   p.nseg = nseg; p.T = T; p.K = K; p.GX = K / 32;
   p.R = R; p.Rblk = R; p.KS = KS; p.PPS = PPS; p.npieces = (int)npieces; p.nchunks = (int)((npieces + PPS - 1) / PPS);
   p.xstride = xstride; p.stage_bytes = stage_bytes; p.nstages = nstages; p.max_pitch = max_pitch;
+  p.npre = env_int("NSQ_ROWS_PRE", nstages);
+  if (p.npre < 0 || p.npre > nstages) p.npre = nstages;
+  // weights evict_first: 1.70 against 1.78-1.82 ms per Llama-3-8B decode step (B200)
+  p.l2hint = env_int("NSQ_ROWS_L2HINT", 1);
+  p.xpipe = env_int("NSQ_ROWS_XPIPE", 0);
   int per_sm = (int)((220 * 1024) / (smem + 1024));
   if (per_sm > 4) per_sm = 4;
   if (per_sm < 1) per_sm = 1;
@@ -854,6 +933,14 @@ static cudaError_t launch_fused(const FusedParams& p, int blocks, size_t smem, c
   if (dev < 0 || dev >= 64 || smem > configured[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
+    // every instantiation asks for the same (largest) shared-memory carveout,
+    // so the CTAs of consecutive launches with different shared-memory sizes
+    // can share an SM (programmatic dependent launch) without the SM first
+    // draining to switch its L1 / shared split
+    if (env_int("NSQ_ROWS_CARVE", 1)) {
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+      if (e != cudaSuccess) return e;
+    }
     if (dev >= 0 && dev < 64) configured[dev] = smem;
   }
   cudaLaunchConfig_t cfg = {};

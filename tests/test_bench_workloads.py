@@ -1,0 +1,42 @@
+"""The benchmark's workload tables: shapes, activation wiring and byte counts (CPU)."""
+import pytest
+
+import bench
+from planejaja_b200.formats import fmt
+
+MB = 1e6
+
+
+@pytest.mark.parametrize("name", sorted(bench.WORKLOADS))
+def test_workload_wiring(name):
+    w = bench.WORKLOADS[name]
+    names = [n for n, _, _, _ in w["spec"]]
+    grouped = [n for _, g in w["groups"] for n in g]
+    assert sorted(grouped) == sorted(names), "every projection in exactly one fused launch"
+    for a, g in w["groups"]:
+        for nm in g:
+            assert w["act_of"][nm] == a
+    for nm, n, k, t in w["spec"]:
+        assert k == w["act_k"][w["act_of"][nm]], nm
+        assert k % 256 == 0, "the fused decode kernel walks K in 256-weight pieces"
+        assert fmt(t).row_bytes(k) % 16 == 0, "rows are copied with 16-byte-aligned bulk copies"
+
+
+@pytest.mark.parametrize("name,layer_mb", [("l3-8b", 138.90), ("l2-7b", 113.84), ("l2-70b-ffn", 3 * 132.12)])
+def test_layer_weight_bytes(name, layer_mb):
+    # Llama-3-8B Q4_K_M: 138.90 MB per layer; Llama-2-7B Q4_0: 113.84 MB;
+    # Llama-2-70B FFN Q4_K: 3 x 132.12 MB
+    w = bench.WORKLOADS[name]
+    total = sum(fmt(t).tensor_bytes(n, k) for _, n, k, t in w["spec"])
+    assert abs(total / MB - layer_mb) < 0.01
+
+
+def test_select_workload_rebinds():
+    try:
+        bench.select_workload("l2-7b", 1)
+        assert bench.METRIC == "decode GEMV HBM GB/s (Llama-2-7B Q4_0, M=1)"
+        assert {t for _, _, _, t in bench.LAYER_SPEC} == {2}
+        wb, xb, yb = bench.layer_bytes_total()
+        assert xb == 4 * (6 * 4096 + 11008) and yb == 4 * (5 * 4096 + 2 * 11008)
+    finally:
+        bench.select_workload("l3-8b", 1)
