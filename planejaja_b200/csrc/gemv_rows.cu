@@ -36,6 +36,12 @@ namespace nsq {
 
 constexpr int kRowsConsumers = 4;
 constexpr int kRowsThreads = 32 * (1 + kRowsConsumers);
+// Self-prepared activations sit in shared memory as runs of 8 records (80 B
+// each) per 256-weight piece, every run padded by 16 bytes.  The lane groups
+// of a warp read the records of consecutive pieces at once; unpadded (640 B
+// apart) those reads fall in the same banks and the 16-byte loads replay 2-4
+// times, padded they fall in disjoint banks.
+constexpr int kXPieceSelf = 8 * 80 + 16;
 
 
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
@@ -321,26 +327,46 @@ struct Piece<NSQ_TYPE_Q4_0, LAYOUT, M> {
   }
 };
 
-// Q8_0: 8 blocks [d][qs int8 32] (q8_0.rs:14-28).
+// Q8_0: 8 blocks [d][qs int8 32] (q8_0.rs:14-28).  A piece (272 bytes)
+// starts 16-byte aligned; the block pair k (bytes 68k .. 68k+67) is read as
+// the 16-byte words 4k .. 4k+4 (bytes 64k .. 64k+79), where it starts at
+// word k: block 2k word-aligned (scale in the low half-word, quants shifted
+// by 2 bytes), block 2k+1 at word k+8 plus 2 bytes (scale in the high
+// half-word, quants word-aligned from word k+9).
 template <int LAYOUT, int M>
 struct Piece<NSQ_TYPE_Q8_0, LAYOUT, M> {
   __device__ static void run(const uint8_t* pc, const uint8_t* xp, int xstride, float (&acc)[M]) {
+    const uint4* pv = reinterpret_cast<const uint4*>(pc);
 #pragma unroll
-    for (int g = 0; g < 8; ++g) {
-      const uint8_t* blk = pc + 34 * g;
-      uint32_t w9[9];
-      ld_words_unaligned<9>(blk, w9);  // bytes 0..35 of the block
-      const float d = h2f((uint16_t)(w9[0] & 0xFFFF));
-      uint32_t q[8];
+    for (int k = 0; k < 4; ++k) {
+      uint32_t w[20];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) q[i] = __funnelshift_r(w9[i], w9[i + 1], 16);
+      for (int i = 0; i < 5; ++i) {
+        const uint4 t = pv[4 * k + i];
+        w[4 * i] = t.x; w[4 * i + 1] = t.y; w[4 * i + 2] = t.z; w[4 * i + 3] = t.w;
+      }
 #pragma unroll
-      for (int m = 0; m < M; ++m) {
-        XG x;
-        lds_xg(xp + m * xstride + g * 80, x);
-        int s0, s1;
-        dot8<true>(q, x, s0, s1);
-        acc[m] = fmaf(x.sx * d, (float)(s0 + s1), acc[m]);
+      for (int b = 0; b < 2; ++b) {
+        const int g = 2 * k + b;
+        float d;
+        uint32_t q[8];
+        if (b == 0) {
+          d = h2f((uint16_t)(w[k] & 0xFFFF));
+#pragma unroll
+          for (int i = 0; i < 8; ++i) q[i] = __funnelshift_r(w[k + i], w[k + i + 1], 16);
+        } else {
+          d = h2f((uint16_t)(w[k + 8] >> 16));
+#pragma unroll
+          for (int i = 0; i < 8; ++i) q[i] = w[k + 9 + i];
+        }
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+          XG x;
+          lds_xg(xp + m * xstride + g * 80, x);
+          int s0, s1;
+          dot8<true>(q, x, s0, s1);
+          acc[m] = fmaf(x.sx * d, (float)(s0 + s1), acc[m]);
+        }
       }
     }
   }
@@ -371,7 +397,6 @@ struct FusedParams {
   int stage_bytes, nstages, max_pitch;
   int npre;             // stages whose weights are copied before the dependency wait (<= nstages)
   int l2hint;           // 1: weight copies evict_first in the L2; 2: also activation reads evict_last
-  int xpipe;            // self-prepared mode: a thread loads its next activation group before quantising
   int Rblk;             // rows per block walked by the cursor: R, or R / 2 with the SwiGLU epilogue
   const float* res[NSQ_MAX_SEGMENTS];  // residual-add epilogue: y = res + x . W^T (may alias y)
   int C;                // self-prepared mode: CTAs per cluster sharing the activation quantisation
@@ -437,19 +462,50 @@ __device__ __forceinline__ void quantize_group(const float4 (&f)[8], uint4 (&o)[
   const float inv = amax > 0.f ? 32767.0f / amax : 0.f;
   uint32_t hw[8], lw[8];
   int s0 = 0, s1 = 0;
+  if (inv < 3.0e38f) {
+    // |v| <= amax, so X = rn(v * inv) lies in [-32767, 32767] and needs no
+    // clamp.  Adding 1.5 * 2^23 rounds the product into the low mantissa
+    // bits: the sum's bits are 0x4B400000 + X, whose two low bytes are X's
+    // (a NaN product counts as 0, as cvt.rni gives).  One byte permute per
+    // value packs the high and low bytes; the sums are sums of the bits.
+    uint32_t b[32];
 #pragma unroll
-  for (int w = 0; w < 8; ++w) {
-    uint32_t h = 0, l = 0;
-#pragma unroll
-    for (int b = 0; b < 4; ++b) {
-      int X = __float2int_rn(v[4 * w + b] * inv);
-      X = max(-32767, min(32767, X));
-      if (w < 4) s0 += X; else s1 += X;
-      h |= ((uint32_t)(X >> 8) & 0xFF) << (8 * b);
-      l |= ((uint32_t)X & 0xFF) << (8 * b);
+    for (int i = 0; i < 32; ++i) {
+      float y = __fmul_rn(v[i], inv);
+      y = (y == y) ? y : 0.f;
+      b[i] = __float_as_uint(__fadd_rn(y, 12582912.0f));
     }
-    hw[w] = h;
-    lw[w] = l;
+    uint32_t t0 = 0, t1 = 0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      const uint32_t p01 = __byte_perm(b[4 * w], b[4 * w + 1], 0x5140);  // X0.b0 X1.b0 X0.b1 X1.b1
+      const uint32_t p23 = __byte_perm(b[4 * w + 2], b[4 * w + 3], 0x5140);
+      lw[w] = __byte_perm(p01, p23, 0x5410);
+      hw[w] = __byte_perm(p01, p23, 0x7632);
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      t0 += b[i];
+      t1 += b[16 + i];
+    }
+    s0 = (int)(t0 - 16u * 0x4B400000u);
+    s1 = (int)(t1 - 16u * 0x4B400000u);
+  } else {
+    // 32767 / amax overflowed (amax below ~1e-34): convert and clamp
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      uint32_t h = 0, l = 0;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        int X = __float2int_rn(v[4 * w + b] * inv);
+        X = max(-32767, min(32767, X));
+        if (w < 4) s0 += X; else s1 += X;
+        h |= ((uint32_t)(X >> 8) & 0xFF) << (8 * b);
+        l |= ((uint32_t)X & 0xFF) << (8 * b);
+      }
+      hw[w] = h;
+      lw[w] = l;
+    }
   }
   o[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
   o[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
@@ -515,8 +571,8 @@ template <int M, bool XSELF, int CODE, int EPI>
 __global__ void __launch_bounds__(kRowsThreads, 4) gemv_fused_kernel(const __grid_constant__ FusedParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* stages = smem;
-  uint8_t* xsm = smem + (size_t)p.stage_bytes * p.nstages;  // self-prepared activations [M][GX] records
-  const size_t xsm_bytes = XSELF ? (size_t)M * p.GX * 80 : 0;
+  uint8_t* xsm = smem + (size_t)p.stage_bytes * p.nstages;  // self-prepared activations [M][pieces] padded record runs
+  const size_t xsm_bytes = XSELF ? (size_t)M * p.npieces * kXPieceSelf : 0;
   float* red = reinterpret_cast<float*>(xsm + xsm_bytes);  // [2][4][32][M]
   uint64_t* full = reinterpret_cast<uint64_t*>(red + 2 * kRowsConsumers * 32 * M);
   uint64_t* empty = full + p.nstages;
@@ -657,9 +713,9 @@ __global__ void __launch_bounds__(kRowsThreads, 4) gemv_fused_kernel(const __gri
       const int64_t g_end = ng * (q + 1) / C;
       auto put = [&](int64_t gi, const float4 (&f)[8]) {
         const int64_t m = gi / p.GX, g = gi - m * p.GX;
+        uint8_t* rec = xsm + m * ((int64_t)p.npieces * kXPieceSelf) + (g >> 3) * kXPieceSelf + (g & 7) * 80;
         uint4 o[5];
         quantize_group(f, o);
-        uint8_t* rec = xsm + (m * p.GX + g) * 80;
         if (clustered) {
           for (int qq = 0; qq < C; ++qq) {
             const uint32_t ra = cluster_map(rec, (uint32_t)qq);
@@ -677,19 +733,7 @@ __global__ void __launch_bounds__(kRowsThreads, 4) gemv_fused_kernel(const __gri
         return p.x + m * p.K + 32 * g;
       };
       constexpr int kStride = kRowsConsumers * 32;
-      int64_t gi = ng * q / C + ct;
-      if (p.xpipe) {
-        // two groups per round: both groups' loads are in flight before the
-        // first is quantised (one memory round trip instead of two)
-        for (; gi + kStride < g_end; gi += 2 * kStride) {
-          float4 fa[8], fb[8];
-          load_group(src(gi), fa, xh, xpol);
-          load_group(src(gi + kStride), fb, xh, xpol);
-          put(gi, fa);
-          put(gi + kStride, fb);
-        }
-      }
-      for (; gi < g_end; gi += kStride) {
+      for (int64_t gi = ng * q / C + ct; gi < g_end; gi += kStride) {
         float4 fa[8];
         load_group(src(gi), fa, xh, xpol);
         put(gi, fa);
@@ -704,7 +748,8 @@ __global__ void __launch_bounds__(kRowsThreads, 4) gemv_fused_kernel(const __gri
     }
     const int r = lane % p.R, ks = lane / p.R;
     const int lanes_per_piece = kRowsConsumers * p.KS;
-    const int xstride = XSELF ? (int)(p.GX * 80) : p.xstride;
+    const int xstride = XSELF ? p.npieces * kXPieceSelf : p.xstride;
+    const int xpiece = XSELF ? kXPieceSelf : 8 * 80;  // bytes between the record runs of consecutive pieces
     float acc[M];
 #pragma unroll
     for (int m = 0; m < M; ++m) acc[m] = 0.f;
@@ -721,10 +766,10 @@ __global__ void __launch_bounds__(kRowsThreads, 4) gemv_fused_kernel(const __gri
         if (ok) {
           const int np = (int)min((int64_t)p.PPS, (int64_t)p.npieces - (int64_t)it.c * p.PPS);
           const uint8_t* slot = stages + (size_t)s * p.stage_bytes;
-          const uint8_t* xbase = XSELF ? xsm + (int64_t)it.c * p.PPS * 8 * 80 : slot + p.R * p.max_pitch;
+          const uint8_t* xbase = XSELF ? xsm + (int64_t)it.c * p.PPS * kXPieceSelf : slot + p.R * p.max_pitch;
           if ((EPI == 2 ? (r & (p.Rblk - 1)) : r) < it.rows) {
             for (int j = cw * p.KS + ks; j < np; j += lanes_per_piece)
-              run_piece<M, CODE>(sg.code, slot + r * sg.pitch + j * sg.piece_bytes, xbase + j * 8 * 80, xstride, acc);
+              run_piece<M, CODE>(sg.code, slot + r * sg.pitch + j * sg.piece_bytes, xbase + j * xpiece, xstride, acc);
           }
           __syncwarp();
           if (lane == 0) mbar_arrive(&empty[s]);
@@ -822,11 +867,12 @@ static bool plan_fused(const nsq_segment* segs, int nseg, int64_t K, int M, bool
                        int max_clusters, FusedParams& p, int& blocks, size_t& smem, int min_r = 4) {
   if (nseg < 1 || nseg > NSQ_MAX_SEGMENTS || K % 256) return false;
   const int64_t npieces = K / 256;
-  bool any_q6k = false;
+  bool any_q6k = false, any_b32 = false;
   int64_t T = 0;
   for (int i = 0; i < nseg; ++i) {
     const int t = segs[i].ggml_type;
     if (seg_code(t, segs[i].q6k_layout) < 0) return false;
+    if (t == NSQ_TYPE_Q4_0 || t == NSQ_TYPE_Q8_0) any_b32 = true;
     if (t == NSQ_TYPE_Q6_K) {
       any_q6k = true;
       if (npieces % 8) return false;
@@ -835,12 +881,14 @@ static bool plan_fused(const nsq_segment* segs, int nseg, int64_t K, int M, bool
     T += segs[i].N;
   }
   // Defaults from measurement on B200 (M = 1): many rows per SM (an FFN
-  // input projection) stream best in 16-row blocks of whole 4096-wide rows;
-  // long rows (K >= 8192) gain from sharing the activation quantisation in
-  // CTA pairs and from whole row blocks per CTA.
+  // input projection) stream best in 16-row blocks of whole 4096-wide rows
+  // for the K-quants, but in 8-row blocks for the 32-weight-block formats
+  // (Llama-2-7B Q4_0 decode step: 1.33-1.38 against 1.49-1.50 ms); long rows
+  // (K >= 8192) gain from sharing the activation quantisation in CTA pairs
+  // and from whole row blocks per CTA.
   const bool many_rows = T >= (int64_t)128 * num_sms;
   const bool long_k = K >= 8192;
-  int R = env_int("NSQ_ROWS_R", many_rows ? 16 : 8);
+  int R = env_int("NSQ_ROWS_R", many_rows && !any_b32 ? 16 : 8);
   if (R != 4 && R != 8 && R != 16 && R != 32) R = 8;
   if (R < min_r) R = min_r;
   while (R > min_r && (T + R - 1) / R < (int64_t)num_sms) R >>= 1;
@@ -851,7 +899,7 @@ static bool plan_fused(const nsq_segment* segs, int nseg, int64_t K, int M, bool
   if (PPS > npieces) PPS = (int)npieces;
   int nstages = env_int("NSQ_ROWS_STAGES", 2);
   if (nstages < 2 || nstages > 8) nstages = 2;
-  const size_t xsm = xself ? (size_t)M * (K / 32) * 80 : 0;
+  const size_t xsm = xself ? (size_t)M * npieces * kXPieceSelf : 0;
   const int min_pps = any_q6k ? 8 : 1;
   int max_pitch = 0, xstride = 0, stage_bytes = 0;
   for (;;) {
@@ -893,7 +941,7 @@ static bool plan_fused(const nsq_segment* segs, int nseg, int64_t K, int M, bool
   if (p.npre < 0 || p.npre > nstages) p.npre = nstages;
   // weights evict_first: 1.70 against 1.78-1.82 ms per Llama-3-8B decode step (B200)
   p.l2hint = env_int("NSQ_ROWS_L2HINT", 1);
-  p.xpipe = env_int("NSQ_ROWS_XPIPE", 0);
+
   int per_sm = (int)((220 * 1024) / (smem + 1024));
   if (per_sm > 4) per_sm = 4;
   if (per_sm < 1) per_sm = 1;
