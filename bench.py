@@ -505,7 +505,8 @@ def run_gpu(args, rank, world, local_rank):
         traffic = None
         tp = os.path.join(ROOT, "profiles", "traffic.json")
         if os.path.exists(tp):
-            key = "gemv_fused_q4k_m1_gate_up" if WORKLOAD == "l3-8b" and M == 1 and world == 1 else None
+            keys = {"l3-8b": "gemv_fused_q4k_m1_gate_up", "l2-7b": "gemv_fused_q40_m1_gate_up"}
+            key = keys.get(WORKLOAD) if M == 1 and world == 1 else None
             traffic = json.load(open(tp)).get(key) if key else None
         result["roofline"] = {"bound": "hbm",
                               "kernel": f"gemv_fused_kernel<M={M},{gname}> gate|up 2 x [{rows}x{KG}] (FFN input projection)",

@@ -884,8 +884,7 @@ static bool plan_fused(const nsq_segment* segs, int nseg, int64_t K, int M, bool
   // input projection) stream best in 16-row blocks of whole 4096-wide rows
   // for the K-quants, but in 8-row blocks for the 32-weight-block formats
   // (Llama-2-7B Q4_0 decode step: 1.33-1.38 against 1.49-1.50 ms); long rows
-  // (K >= 8192) gain from sharing the activation quantisation in CTA pairs
-  // and from whole row blocks per CTA.
+  // (K >= 8192) gain from sharing the activation quantisation in CTA pairs.
   const bool many_rows = T >= (int64_t)128 * num_sms;
   const bool long_k = K >= 8192;
   int R = env_int("NSQ_ROWS_R", many_rows && !any_b32 ? 16 : 8);
@@ -957,7 +956,9 @@ static bool plan_fused(const nsq_segment* segs, int nseg, int64_t K, int M, bool
   if (C > 1 && max_clusters > 0 && gmax > (int64_t)max_clusters * C) gmax = (int64_t)max_clusters * C;
   gmax = gmax / C * C;
   if (gmax < C) return false;
-  const bool whole_blocks = env_int("NSQ_ROWS_BAL", long_k ? 1 : 0) != 0;
+  // whole row blocks per CTA for every shape: Llama-3-8B decode step 1.596
+  // against 1.638 ms with an even row split for K < 8192
+  const bool whole_blocks = env_int("NSQ_ROWS_BAL", 1) != 0;
   int64_t g = gmax < nrb ? gmax : nrb;
   if (whole_blocks) {
     const int64_t per_cta = (nrb + gmax - 1) / gmax;

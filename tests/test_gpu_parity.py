@@ -194,6 +194,42 @@ def test_gemv_unaligned_activations(eng, oracle):
     assert rel_err(y, oracle.quant_matmul(w, Q4_K, x, n, k)) <= GEMV_TOL
 
 
+def _adversarial_activations(m, k, seed):
+    """Groups of 32 that stress the activation quantisation: Gaussian, a NaN
+    inside a group, exact rounding ties (amax 32767, so x * 32767 / amax lands
+    on .5), amax too small for 32767 / amax (the fallback conversion), an
+    infinite value, all zeros."""
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    g = x.reshape(m, k // 32, 32)
+    g[:, 1, 5] = np.nan
+    g[:, 2, :] = np.arange(-16, 16, dtype=np.float32) + 0.5
+    g[:, 2, 0] = 32767.0
+    g[:, 3, :] = rng.standard_normal(32).astype(np.float32) * np.float32(1e-38)
+    g[:, 4, 7] = np.inf
+    g[:, 5, :] = 0.0
+    g[:, 6, :] = -2.5
+    return x
+
+
+@pytest.mark.parametrize("m", [1, 3])
+def test_gemv_on_chip_quantiser_matches_prepare_kernel(eng, m):
+    """The fused kernel quantises activations on chip (x 16-byte aligned);
+    with x only 4-byte aligned the standalone preparation kernel writes the
+    records and the same fused kernel reads them.  Both plans are identical
+    at this shape, so equal outputs, bit for bit, mean equal records."""
+    n, k = 256, 1024
+    w = eng.upload(Q.synthetic_weights(n, k, Q4_K, seed=12))
+    x = torch.from_numpy(_adversarial_activations(m, k, seed=13)).to(eng.device)
+    buf = torch.empty(m * k + 1, device=eng.device)
+    buf[1:] = x.reshape(-1)
+    y_chip = eng.gemv(w, Q4_K, x, n, k).cpu().numpy()
+    y_prep = eng.gemv(w, Q4_K, buf[1:], n, k).cpu().numpy()
+    assert np.array_equal(np.isnan(y_chip), np.isnan(y_prep))
+    ok = ~np.isnan(y_chip)
+    assert np.array_equal(y_chip[ok].view(np.uint32), y_prep[ok].view(np.uint32))
+
+
 def test_gemv_prepared_shares_activations(eng, oracle):
     k = 1024
     x = Q.synthetic_activations(2, k, seed=9)
