@@ -40,3 +40,25 @@ def test_select_workload_rebinds():
         assert xb == 4 * (6 * 4096 + 11008) and yb == 4 * (5 * 4096 + 2 * 11008)
     finally:
         bench.select_workload("l3-8b", 1)
+
+
+def test_reference_arm_json_line():
+    """`bench.py --impl reference` runs the oracle on the host and prints one
+    JSON line with the GPU arm's metric, a cpu_baseline and an e2e entry."""
+    import json
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    out = subprocess.run([sys.executable, os.path.join(root, "bench.py"), "--impl", "reference", "--steps", "1",
+                          "--warmup", "3", "--ref-frac", "0.005"], capture_output=True, text=True, timeout=600,
+                         cwd=root, env={**os.environ, "WORLD_SIZE": "1", "RANK": "0"})
+    assert out.returncode == 0, out.stderr[-2000:]
+    line = json.loads(out.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference"
+    assert line["metric"] == "decode GEMV HBM GB/s (Llama-3-8B Q4_K_M, M=1)"
+    assert line["unit"] == "GB/s" and line["higher_is_better"] is True and line["value"] > 0
+    assert line["steps"] == 1 and line["warmup"] == 3
+    cb = line["cpu_baseline"]
+    assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == line["value"]
+    assert line["e2e"] == {"value": line["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
