@@ -69,6 +69,13 @@ extern "C" {
 /* Library version (NSQ_VERSION). */
 int nsq_version(void);
 
+/* Re-reads the NSQ_* launch-planning environment variables (kernel choice,
+ * tile and pipeline sizes; all default to measured choices).  The library
+ * reads them once, when it plans its first launch; call this after changing
+ * them in the process environment (tests, tuning runs).  No counterpart in
+ * the reference, which has no such switches. */
+void nsq_reload_tuning(void);
+
 /* Text of a status code; static storage. */
 const char *nsq_strerror(int status);
 
@@ -137,8 +144,12 @@ int nsq_gemv_prepared(const void *w, int ggml_type, int q6k_layout, const void *
  *     NSQ_ERR_WORKSPACE.
  *   - All calls share the array: calls that overlap on the GPU (unordered
  *     streams or threads) race and give wrong results.
- *   - The first call on a device looks up the array's device address; make
- *     it before capturing a stream into a CUDA graph.
+ *   - The first call on a device looks up the array's device address and
+ *     keeps it until the process exits; make that call before capturing a
+ *     stream into a CUDA graph, and do not call this entry point again
+ *     after a cudaDeviceReset of that device.
+ *   - Weight arguments are checked exactly as nsq_gemv checks them (type,
+ *     Q5_K / Q6_K layout, 16-byte alignment, K).
  */
 #define NSQ_NOALLOC_MAX_ELEMS 262144 /* M * K */
 int nsq_gemv_noalloc(const void *w, int ggml_type, int q6k_layout, const float *x, float *y,
@@ -264,7 +275,12 @@ typedef struct nsq_xsegment {
 } nsq_xsegment;
 
 /* y[m, row0 + r] of every rank's buffer = x[m] . W_rank[r].  Same accuracy
- * contract and workspace rule as nsq_gemv_multi; needs K % 256 == 0. */
+ * contract and workspace rule as nsq_gemv_multi; needs K % 256 == 0.
+ * x must not overlap any output range [y_off, y_off + M * n_full * 4) of
+ * this call in this rank's buffer (NSQ_ERR_SHAPE): a peer that runs ahead
+ * stores this call's rows there while this rank may still be reading x.
+ * So an exchange whose input is the previous exchange's output writes a
+ * different range (for a chain of exchanges, alternate two ranges). */
 int nsq_gemv_multi_xchg(const nsq_xsegment *segs, int nseg, const float *x, int64_t M, int64_t K,
                         nsq_comm *comm, void *workspace, size_t workspace_bytes, void *stream);
 

@@ -4,7 +4,9 @@
 // alignment, workspace size, device) and returns an NSQ_* status before
 // launching anything; CUDA launch errors become NSQ_ERR_CUDA.  Nothing here
 // allocates device memory.
+#include <atomic>
 #include <mutex>
+#include <stdlib.h>
 
 #include "nsq_common.cuh"
 
@@ -33,6 +35,29 @@ cudaError_t launch_matmul_f32(const float* a, const float* b, float* c, int64_t 
 bool comm_desc(const nsq_comm* c, XchgDesc& d);
 size_t comm_bytes(const nsq_comm* c);
 cudaError_t comm_launch_wait(const nsq_comm* c, cudaStream_t st);
+
+// ---- launch-planning switches (see TuneId)
+static const char* const kTuneNames[kTuneCount] = {
+    "NSQ_ROWS_R", "NSQ_ROWS_PPSM", "NSQ_ROWS_STAGES", "NSQ_ROWS_PRE", "NSQ_ROWS_L2HINT", "NSQ_ROWS_CPS",
+    "NSQ_ROWS_C", "NSQ_ROWS_BAL", "NSQ_ROWS_CARVE", "NSQ_MMA_MIN_M", "NSQ_MMA_PPS", "NSQ_MMA_STAGES",
+    "NSQ_GEMV_GENERAL", "NSQ_GEMM_SPLIT", "NSQ_GEMM_TOK"};
+static std::atomic<int> g_tune_val[kTuneCount];
+static std::atomic<bool> g_tune_set[kTuneCount];
+static std::once_flag g_tune_once;
+
+static void read_tuning() {
+  for (int i = 0; i < kTuneCount; ++i) {
+    const char* v = getenv(kTuneNames[i]);
+    const bool set = v && v[0];
+    g_tune_val[i].store(set ? atoi(v) : 0, std::memory_order_relaxed);
+    g_tune_set[i].store(set, std::memory_order_release);
+  }
+}
+
+int tune(TuneId id, int dflt) {
+  std::call_once(g_tune_once, read_tuning);
+  return g_tune_set[id].load(std::memory_order_acquire) ? g_tune_val[id].load(std::memory_order_relaxed) : dflt;
+}
 
 struct DevInfo {
   int num_sms = 0;
@@ -74,7 +99,9 @@ int device_check(int* num_sms) {
   return rc;
 }
 
-static int check_weights(const void* w, int type, int layout, int64_t K) {
+// Also used by nsq_gemv_noalloc (noalloc.cu), so that both entry points
+// accept and reject the same weight arguments.
+int check_weights(const void* w, int type, int layout, int64_t K) {
   if (!type_ok(type)) return NSQ_ERR_TYPE;
   if ((type == NSQ_TYPE_Q6_K || type == NSQ_TYPE_Q5_K) && layout != NSQ_Q6K_GGML && layout != NSQ_Q6K_NODESTOR)
     return NSQ_ERR_TYPE;
@@ -92,6 +119,11 @@ using namespace nsq;
 extern "C" {
 
 int nsq_version(void) { return NSQ_VERSION; }
+
+void nsq_reload_tuning(void) {
+  std::call_once(g_tune_once, read_tuning);
+  read_tuning();
+}
 
 const char* nsq_strerror(int status) {
   switch (status) {
@@ -325,6 +357,26 @@ int nsq_gemv_multi_xchg(const nsq_xsegment* segs, int nseg, const float* x, int6
   }
   if (!x) return NSQ_ERR_NULL;
   if (reinterpret_cast<uintptr_t>(x) & 3) return NSQ_ERR_ALIGN;
+  {
+    // x must not lie in an output range this call writes: every rank stores
+    // its rows into that range of every other rank's buffer, possibly while
+    // that rank's own kernel is still reading its activations there.
+    const uintptr_t xb = reinterpret_cast<uintptr_t>(x), xe = xb + (uintptr_t)(M * K * 4);
+    const uintptr_t base = reinterpret_cast<uintptr_t>(nsq_comm_buffer(comm));
+    for (int i = 0; i < nseg; ++i) {
+      const uintptr_t yb = base + (uintptr_t)segs[i].y_off, ye = yb + (uintptr_t)(M * segs[i].n_full * 4);
+      if (xb < ye && yb < xe) return NSQ_ERR_SHAPE;
+    }
+  }
+  if (xd.P == 1) {
+    // a one-rank group: the kernels' exchange epilogue is off (P == 1), so
+    // the outputs go straight to this rank's buffer
+    uint8_t* base = static_cast<uint8_t*>(nsq_comm_buffer(comm));
+    for (int i = 0; i < nseg; ++i) {
+      if (segs[i].row0 != 0 || segs[i].n_full != segs[i].N) return NSQ_ERR_SHAPE;  // one rank holds every row
+      sl[i].y = reinterpret_cast<float*>(base + segs[i].y_off);
+    }
+  }
   const bool mma = M >= gemv_mma_min_m() && gemv_mma_covers(sl, nseg, M, K);
   if (!mma && !fused_covers(sl, nseg, K)) return NSQ_ERR_SHAPE;
   const bool self = !mma && fused_self_prepare_fits(M, K) && !(reinterpret_cast<uintptr_t>(x) & 15);

@@ -689,13 +689,8 @@ static int launch_gemm_t(const void* x, const CUtensorMap& wmap, const GemmParam
   constexpr size_t region = (size_t)gemm_stages<TYPE, TOK>() * (GEMM_BM * 128 + TOK * 128) +
                             (size_t)GEMM_RAW_STAGES * GEMM_BM * RawCol<TYPE>::pitch;
   int S = 1;
-  const char* se = getenv("NSQ_GEMM_SPLIT");
   const int64_t tiles = tiles_n * tiles_m, ncol = p.K / 256;
-  if (se && se[0]) {
-    S = atoi(se);
-  } else if (num_sms > 0 && tiles * 2 <= num_sms) {
-    S = (int)(num_sms / tiles);
-  }
+  S = tune(kTuneGemmSplit, num_sms > 0 && tiles * 2 <= num_sms ? (int)(num_sms / tiles) : 1);
   if (S > 4) S = 4;
   while (S > 1 && (ncol < 2 * S || (size_t)(S - 1) * 16 * 32 * 32 * 4 > region)) --S;
   if (S < 1) S = 1;
@@ -754,9 +749,9 @@ int run_gemm_bf16(const uint8_t* w, int type, int layout, const void* x, void* y
   // tokens per CTA: 128 for short prompts, else 256 or 512 (NSQ_GEMM_TOK
   // overrides); a 512-token tile reuses each dequantized weight tile twice
   // as often, where two 64-wide stages of it fit beside the raw bytes
-  const char* te = getenv("NSQ_GEMM_TOK");
   int tok = M <= 128 ? 128 : (M >= 512 ? 512 : 256);
-  if (te && (atoi(te) == 128 || atoi(te) == 256 || atoi(te) == 512)) tok = atoi(te);
+  const int te = tune(kTuneGemmTok, 0);
+  if (te == 128 || te == 256 || te == 512) tok = te;
   if (M <= 128) tok = 128;
   switch (type) {
     case NSQ_TYPE_Q4_0: return run_gemm_t<NSQ_TYPE_Q4_0, 0>(x, p, tok, st, num_sms);

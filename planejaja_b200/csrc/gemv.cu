@@ -598,8 +598,7 @@ int gemv_mma_min_m();
 bool gemv_force_general() {
   // NSQ_GEMV_GENERAL=1 forces the general kernel below (the parity tests use
   // it to cover both kernels on the same shapes)
-  const char* force = getenv("NSQ_GEMV_GENERAL");
-  return force && force[0] == '1';
+  return tune(kTuneGemvGeneral, 0) == 1;
 }
 
 // GEMV on prepared activations: the tensor-core kernel (gemv_mma.cu) for

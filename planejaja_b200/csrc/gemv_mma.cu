@@ -608,11 +608,6 @@ __global__ void __launch_bounds__(kMmaThreads, 2) gemv_mma_kernel(const __grid_c
 
 // ---------------------------------------------------------------------------
 // Host side
-static int menv(const char* name, int dflt) {
-  const char* v = getenv(name);
-  return (v && v[0]) ? atoi(v) : dflt;
-}
-
 static int mcode(int type, int layout) {
   switch (type) {
     case NSQ_TYPE_Q4_K: return kMQ4K;
@@ -640,7 +635,7 @@ static int mpiece_bytes(int type) {
 // below 8, where the per-scale-group fp32 epilogue and the per-chunk
 // activation loads are not amortised.  Default 9.
 int gemv_mma_min_m() {
-  const int m = menv("NSQ_MMA_MIN_M", 9);
+  const int m = tune(kTuneMmaMinM, 9);
   return m < 1 ? 1 : m;
 }
 
@@ -659,10 +654,10 @@ static bool plan_mma(const nsq_segment* segs, int nseg, int64_t M, int64_t K, in
   int64_t T = 0;
   for (int i = 0; i < nseg; ++i) T += segs[i].N;
   const int noct = M > 8 ? 2 : 1;
-  int PPS = menv("NSQ_MMA_PPS", 2);
+  int PPS = tune(kTuneMmaPPS, 2);
   if (PPS < 1) PPS = 1;
   if (PPS > npieces) PPS = (int)npieces;
-  int nstages = menv("NSQ_MMA_STAGES", 3);
+  int nstages = tune(kTuneMmaStages, 3);
   if (nstages < 2 || nstages > 6) nstages = 3;
   int max_pitch = 0;
   for (int i = 0; i < nseg; ++i) {

@@ -28,8 +28,6 @@
 // and stores the records into the shared memory of every CTA of its cluster
 // (distributed shared memory), so the L2 serves each activation line to 1/C
 // as many CTAs; one cluster barrier publishes the records.
-#include <stdlib.h>
-
 #include "nsq_common.cuh"
 
 namespace nsq {
@@ -835,11 +833,6 @@ __global__ void __launch_bounds__(kRowsThreads, 4) gemv_fused_kernel(const __gri
 // Host side
 constexpr int kXSelfMaxBytes = 40 * 1024;
 
-static int env_int(const char* name, int dflt) {
-  const char* v = getenv(name);
-  return (v && v[0]) ? atoi(v) : dflt;
-}
-
 static int seg_code(int type, int layout) {
   switch (type) {
     case NSQ_TYPE_Q4_K: return kQ4K;
@@ -887,16 +880,16 @@ static bool plan_fused(const nsq_segment* segs, int nseg, int64_t K, int M, bool
   // (K >= 8192) gain from sharing the activation quantisation in CTA pairs.
   const bool many_rows = T >= (int64_t)128 * num_sms;
   const bool long_k = K >= 8192;
-  int R = env_int("NSQ_ROWS_R", many_rows && !any_b32 ? 16 : 8);
+  int R = tune(kTuneRowsR, many_rows && !any_b32 ? 16 : 8);
   if (R != 4 && R != 8 && R != 16 && R != 32) R = 8;
   if (R < min_r) R = min_r;
   while (R > min_r && (T + R - 1) / R < (int64_t)num_sms) R >>= 1;
   const int KS = 32 / R;
-  int PPS = env_int("NSQ_ROWS_PPSM", many_rows ? 2 : 1) * kRowsConsumers * KS;
+  int PPS = tune(kTuneRowsPPSM, many_rows ? 2 : 1) * kRowsConsumers * KS;
   if (PPS < 1) PPS = kRowsConsumers * KS;
   if (any_q6k && PPS % 8) PPS = (PPS + 7) / 8 * 8;
   if (PPS > npieces) PPS = (int)npieces;
-  int nstages = env_int("NSQ_ROWS_STAGES", 2);
+  int nstages = tune(kTuneRowsStages, 2);
   if (nstages < 2 || nstages > 8) nstages = 2;
   const size_t xsm = xself ? (size_t)M * npieces * kXPieceSelf : 0;
   const int min_pps = any_q6k ? 8 : 1;
@@ -936,18 +929,18 @@ static bool plan_fused(const nsq_segment* segs, int nseg, int64_t K, int M, bool
   p.nseg = nseg; p.T = T; p.K = K; p.GX = K / 32;
   p.R = R; p.Rblk = R; p.KS = KS; p.PPS = PPS; p.npieces = (int)npieces; p.nchunks = (int)((npieces + PPS - 1) / PPS);
   p.xstride = xstride; p.stage_bytes = stage_bytes; p.nstages = nstages; p.max_pitch = max_pitch;
-  p.npre = env_int("NSQ_ROWS_PRE", nstages);
+  p.npre = tune(kTuneRowsPre, nstages);
   if (p.npre < 0 || p.npre > nstages) p.npre = nstages;
   // weights evict_first: 1.70 against 1.78-1.82 ms per Llama-3-8B decode step (B200)
-  p.l2hint = env_int("NSQ_ROWS_L2HINT", 1);
+  p.l2hint = tune(kTuneRowsL2Hint, 1);
 
   int per_sm = (int)((220 * 1024) / (smem + 1024));
   if (per_sm > 4) per_sm = 4;
   if (per_sm < 1) per_sm = 1;
-  const int cps = env_int("NSQ_ROWS_CPS", 0);
+  const int cps = tune(kTuneRowsCPS, 0);
   if (cps >= 1 && cps <= per_sm) per_sm = cps;
   // clusters share the activation quantisation (self-prepared mode only)
-  int C = xself ? env_int("NSQ_ROWS_C", long_k ? 2 : 1) : 1;
+  int C = xself ? tune(kTuneRowsC, long_k ? 2 : 1) : 1;
   if (C != 2 && C != 4 && C != 8) C = 1;
   // grid: as many CTAs as fit at once, then the fewest that give every CTA
   // the same number of whole row blocks (give or take one)
@@ -958,7 +951,7 @@ static bool plan_fused(const nsq_segment* segs, int nseg, int64_t K, int M, bool
   if (gmax < C) return false;
   // whole row blocks per CTA for every shape: Llama-3-8B decode step 1.596
   // against 1.638 ms with an even row split for K < 8192
-  const bool whole_blocks = env_int("NSQ_ROWS_BAL", 1) != 0;
+  const bool whole_blocks = tune(kTuneRowsBal, 1) != 0;
   int64_t g = gmax < nrb ? gmax : nrb;
   if (whole_blocks) {
     const int64_t per_cta = (nrb + gmax - 1) / gmax;
@@ -986,7 +979,7 @@ static cudaError_t launch_fused(const FusedParams& p, int blocks, size_t smem, c
     // so the CTAs of consecutive launches with different shared-memory sizes
     // can share an SM (programmatic dependent launch) without the SM first
     // draining to switch its L1 / shared split
-    if (env_int("NSQ_ROWS_CARVE", 1)) {
+    if (tune(kTuneRowsCarve, 1)) {
       e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
       if (e != cudaSuccess) return e;
     }

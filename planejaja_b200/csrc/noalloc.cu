@@ -19,8 +19,11 @@
 //     GPU (different streams, or host threads, without ordering between
 //     them) race on the array and give wrong results; order them.
 //   * The first call on a device looks the array's device address up
-//     (cudaGetSymbolAddress, with that device current).  Make that first call
-//     before capturing a stream into a CUDA graph.
+//     (cudaGetSymbolAddress, with that device current) and keeps it for the
+//     life of the process.  Make that first call before capturing a stream
+//     into a CUDA graph.  Do not use this entry point across a
+//     cudaDeviceReset of the device: the kept address then belongs to the
+//     destroyed context.
 #include <mutex>
 
 #include "nsq_common.cuh"
@@ -30,6 +33,7 @@ namespace nsq {
 cudaError_t launch_prepare_x(const float* x, XGroup* xg, int64_t M, int64_t K, cudaStream_t st, int num_sms);
 int run_gemv(const uint8_t* w, int type, int layout, const XGroup* xg, float* y, int64_t M, int64_t N, int64_t K,
              cudaStream_t st, int num_sms);
+int check_weights(const void* w, int type, int layout, int64_t K);
 
 constexpr size_t kNoAllocBytes = (size_t)(NSQ_NOALLOC_MAX_ELEMS / 32) * sizeof(XGroup);
 
@@ -72,17 +76,15 @@ using namespace nsq;
 
 extern "C" int nsq_gemv_noalloc(const void* w, int ggml_type, int q6k_layout, const float* x, float* y, int64_t M,
                                 int64_t N, int64_t K, void* stream) {
-  const int64_t qk = nsq_block_weights(ggml_type);
-  if (qk == 0) return NSQ_ERR_TYPE;
-  if (ggml_type == NSQ_TYPE_Q6_K && q6k_layout != NSQ_Q6K_GGML && q6k_layout != NSQ_Q6K_NODESTOR)
-    return NSQ_ERR_TYPE;
-  if (!w || !x || !y) return NSQ_ERR_NULL;
-  if (reinterpret_cast<uintptr_t>(w) & 15) return NSQ_ERR_ALIGN;
+  // the weight checks of nsq_gemv (type, K-quant layout, pointer, K)
+  int rc = check_weights(w, ggml_type, q6k_layout, K);
+  if (rc) return rc;
+  if (!x || !y) return NSQ_ERR_NULL;
   if ((reinterpret_cast<uintptr_t>(x) & 3) || (reinterpret_cast<uintptr_t>(y) & 3)) return NSQ_ERR_ALIGN;
-  if (M < 1 || M > NSQ_GEMV_MAX_M || N < 1 || K <= 0 || K % qk) return NSQ_ERR_SHAPE;
+  if (M < 1 || M > NSQ_GEMV_MAX_M || N < 1) return NSQ_ERR_SHAPE;
   if (M * K > NSQ_NOALLOC_MAX_ELEMS) return NSQ_ERR_WORKSPACE;  // beyond the built-in scratch
   NoAllocDev d;
-  int rc = noalloc_setup(d);
+  rc = noalloc_setup(d);
   if (rc) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   XGroup* xg = static_cast<XGroup*>(d.scratch);

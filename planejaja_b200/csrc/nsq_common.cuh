@@ -263,4 +263,16 @@ __device__ __forceinline__ bool wait_geq_bounded(const uint32_t* p, uint32_t wan
   }
 }
 
+// Launch-planning switches: the NSQ_* environment variables below, read
+// once, when the library plans its first launch (nsq_reload_tuning reads
+// them again).  tune(id, dflt) gives the variable's integer value, or dflt
+// when it is unset or empty.  The defaults the planners pass are the
+// measured choices; the switches exist for tests and tuning runs.
+enum TuneId : int {
+  kTuneRowsR, kTuneRowsPPSM, kTuneRowsStages, kTuneRowsPre, kTuneRowsL2Hint, kTuneRowsCPS, kTuneRowsC,
+  kTuneRowsBal, kTuneRowsCarve, kTuneMmaMinM, kTuneMmaPPS, kTuneMmaStages, kTuneGemvGeneral, kTuneGemmSplit,
+  kTuneGemmTok, kTuneCount
+};
+int tune(TuneId id, int dflt);
+
 }  // namespace nsq

@@ -1,6 +1,7 @@
 """Generate tests/golden/nsz_golden.npz from the reference's own NSZ file.
 
-Run from the repository root:  python tests/golden/make_nsz_golden.py
+Run from the repository root, with the path of the reference's file:
+    python tests/golden/make_nsz_golden.py <reference root>/nodestor/micro_modelo_ignition.nsz
 
 Source of truth: nodestor/micro_modelo_ignition.nsz, written by the
 reference's converter (nodestor-cli/src/bin/nsz_convert.rs) from the
@@ -20,16 +21,16 @@ from __future__ import annotations
 
 import os
 import struct
+import sys
 
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-SRC = "/root/reference/nodestor/micro_modelo_ignition.nsz"
 KEEP = ["output_norm.weight", "blk.0.attn_q.weight", "token_embd.weight", "blk.0.ffn_down.weight"]
 
 
-def main() -> None:
-    data = np.fromfile(SRC, np.uint8)
+def main(src: str) -> None:
+    data = np.fromfile(src, np.uint8)
     n = struct.unpack("<I", data[8:12].tobytes())[0]
     out = {"file_header": data[:28].copy(), "entries": data[28:28 + 128 * n].copy()}
     names = []
@@ -47,4 +48,6 @@ def main() -> None:
 
 
 if __name__ == "__main__":
-    main()
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: {sys.argv[0]} <path of micro_modelo_ignition.nsz>")
+    main(sys.argv[1])

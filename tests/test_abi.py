@@ -80,6 +80,15 @@ def test_host_side_argument_errors(lib):
     assert lib.nsq_gemv_multi(ctypes.cast(segs, ctypes.c_void_p), 2, al, 1, 256, None, 0, None) == _lib.ERR_TYPE
     assert lib.nsq_gemv_multi(ctypes.cast(segs, ctypes.c_void_p), 5, al, 1, 256, None, 0, None) == _lib.ERR_SHAPE
     assert lib.nsq_gemv_multi(None, 1, al, 1, 256, None, 0, None) == _lib.ERR_NULL
+    # the allocation-free GEMV checks its weight arguments as nsq_gemv does
+    for t in (13, 14):  # Q5_K, Q6_K: the layout must be GGML or NODESTOR
+        assert lib.nsq_gemv_noalloc(al, t, 5, al, al, 1, 16, 256, None) == _lib.ERR_TYPE
+        assert lib.nsq_gemv(al, t, 5, al, al, 1, 16, 256, al, 1 << 20, None) == _lib.ERR_TYPE
+    assert lib.nsq_gemv_noalloc(al, 3, 0, al, al, 1, 16, 256, None) == _lib.ERR_TYPE
+    assert lib.nsq_gemv_noalloc(ctypes.c_void_p(0x10008), 12, 0, al, al, 1, 16, 256, None) == _lib.ERR_ALIGN
+    assert lib.nsq_gemv_noalloc(al, 12, 0, al, al, 1, 16, 300, None) == _lib.ERR_SHAPE
+    assert lib.nsq_gemv_noalloc(al, 12, 0, None, al, 1, 16, 256, None) == _lib.ERR_NULL
+    assert lib.nsq_gemv_noalloc(al, 12, 0, al, al, 2, 16, 131072 + 256, None) == _lib.ERR_WORKSPACE
     assert lib.nsq_matmul_f32(None, al, al, 2, 2, 2, None) == _lib.ERR_NULL
     assert lib.nsq_matmul_f32(al, al, al, 0, 2, 2, None) == _lib.ERR_SHAPE
 

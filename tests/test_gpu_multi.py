@@ -131,3 +131,39 @@ def test_fused_exchange_wait_times_out_without_peer(tmp_path):
     mp.start_processes(_worker, args=(WORLD, _free_port(), str(tmp_path), True), nprocs=WORLD, start_method="spawn")
     from planejaja_b200 import _lib
     assert int(np.load(tmp_path / "status.npy")[0]) == _lib.ERR_TIMEOUT
+
+
+def test_exchange_rejects_input_inside_its_output():
+    """One GPU, a one-rank exchange group: x inside an output range of the
+    same call is refused before any launch (a peer that ran ahead would
+    store this call's rows there while this rank still reads x); x in the
+    other half of the buffer (the previous exchange's output) is accepted."""
+    import ctypes
+
+    from planejaja_b200 import _lib
+    lib = _lib.load()
+    k, n, m = 256, 256, 1
+    half = m * max(n, k) * 4
+    comm, h = ctypes.c_void_p(), ctypes.create_string_buffer(int(lib.nsq_comm_handle_bytes()))
+    assert lib.nsq_comm_create(1, 0, 2 * half, ctypes.byref(comm), h) == 0
+    try:
+        assert lib.nsq_comm_connect(comm, h) == 0
+        base = int(lib.nsq_comm_buffer(comm))
+        w = torch.from_numpy(Q.synthetic_weights(n, k, Q4_K, seed=3)).cuda()
+        st = torch.cuda.current_stream().cuda_stream
+        ws = torch.empty(1 << 16, dtype=torch.uint8, device="cuda")
+
+        def call(x_ptr, y_off):
+            xs = (_lib.XSegment * 1)(_lib.XSegment(w.data_ptr(), Q4_K, 0, n, 0, n, y_off))
+            return lib.nsq_gemv_multi_xchg(ctypes.cast(xs, ctypes.c_void_p), 1, ctypes.c_void_p(x_ptr), m, k, comm,
+                                           ws.data_ptr(), ws.numel(), st)
+
+        assert call(base, 0) == _lib.ERR_SHAPE              # x is the slot written
+        assert call(base + 512, 0) == _lib.ERR_SHAPE        # x starts inside it
+        assert call(base + half, half) == _lib.ERR_SHAPE    # same, second slot
+        torch.cuda.current_stream().synchronize()
+        assert call(base + half, 0) == 0                    # x in the other slot
+        assert call(base, half) == 0                        # and back
+        torch.cuda.synchronize()
+    finally:
+        assert lib.nsq_comm_destroy(comm) == 0

@@ -89,16 +89,16 @@ def test_dequant_empty(eng):
 
 # ---------------------------------------------------------------- GEMV
 @pytest.fixture(params=["rows", "mma", "general"])
-def gemv_kernel(request, monkeypatch):
+def gemv_kernel(request, tuning):
     """Runs a test with each GEMV kernel: one lane per row (dp4a, every M),
     integer tensor cores (every M), and the general kernel."""
-    monkeypatch.delenv("NSQ_GEMV_GENERAL", raising=False)
+    tuning.unset("NSQ_GEMV_GENERAL")
     if request.param == "general":
-        monkeypatch.setenv("NSQ_GEMV_GENERAL", "1")
+        tuning.set("NSQ_GEMV_GENERAL", "1")
     elif request.param == "mma":
-        monkeypatch.setenv("NSQ_MMA_MIN_M", "1")
+        tuning.set("NSQ_MMA_MIN_M", "1")
     else:
-        monkeypatch.setenv("NSQ_MMA_MIN_M", "17")
+        tuning.set("NSQ_MMA_MIN_M", "17")
     return request.param
 
 
@@ -276,18 +276,18 @@ def test_gemv_errors_on_gpu(eng):
 
 # ---------------------------------------------------------------- GEMM
 @pytest.fixture(params=["tok_auto", "tok128", "tok512", "nosplit"])
-def gemm_tok(request, monkeypatch):
+def gemm_tok(request, tuning):
     """Runs a GEMM test with the default token tile (and the default split-K,
     which small grids get), 128-token tiles, 512-token tiles (two N = 256
     MMAs per K step; Q8_0 falls back to 256), and split-K switched off."""
-    monkeypatch.delenv("NSQ_GEMM_TOK", raising=False)
-    monkeypatch.delenv("NSQ_GEMM_SPLIT", raising=False)
+    tuning.unset("NSQ_GEMM_TOK")
+    tuning.unset("NSQ_GEMM_SPLIT")
     if request.param == "tok128":
-        monkeypatch.setenv("NSQ_GEMM_TOK", "128")
+        tuning.set("NSQ_GEMM_TOK", "128")
     elif request.param == "tok512":
-        monkeypatch.setenv("NSQ_GEMM_TOK", "512")
+        tuning.set("NSQ_GEMM_TOK", "512")
     elif request.param == "nosplit":
-        monkeypatch.setenv("NSQ_GEMM_SPLIT", "1")
+        tuning.set("NSQ_GEMM_SPLIT", "1")
     return request.param
 
 

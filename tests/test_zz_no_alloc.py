@@ -17,7 +17,7 @@ import torch
 
 from planejaja_b200 import _lib
 from planejaja_b200 import quantize as Q
-from planejaja_b200.formats import Q4_K, Q6_K, Q8_0
+from planejaja_b200.formats import Q4_K, Q5_K, Q6_K, Q8_0, Q6K_GGML, Q6K_NODESTOR
 
 pytestmark = pytest.mark.gpu
 
@@ -31,29 +31,31 @@ def rel_err(y, r):
     return float(np.max(np.abs(y - r) / np.maximum(np.abs(r), max(rms, 1e-30))))
 
 
-def _gemv_reference(lib, w, t, x, n, k):
+def _gemv_reference(lib, w, t, lay, x, n, k):
     """Output of the existing entry point nsq_gemv (caller workspace)."""
     m = x.shape[0]
     y = torch.empty((m, n), dtype=torch.float32, device="cuda")
     ws = torch.empty(lib.nsq_gemv_workspace_size(m, k), dtype=torch.uint8, device="cuda")
     st = torch.cuda.current_stream().cuda_stream
-    assert lib.nsq_gemv(w.data_ptr(), t, 0, x.data_ptr(), y.data_ptr(), m, n, k, ws.data_ptr(), ws.numel(), st) == 0
+    assert lib.nsq_gemv(w.data_ptr(), t, lay, x.data_ptr(), y.data_ptr(), m, n, k, ws.data_ptr(), ws.numel(),
+                        st) == 0
     return y
 
 
 def test_noalloc_matches_gemv_two_calls_in_a_row():
     lib = _lib.load()
     st = torch.cuda.current_stream().cuda_stream
-    cases = [(Q4_K, 1, 512, 4096, 11), (Q6_K, 4, 300, 14336, 12), (Q8_0, 16, 200, 1024, 13)]
-    for t, m, n, k, seed in cases:
-        w = torch.from_numpy(Q.synthetic_weights(n, k, t, seed=seed)).cuda()
+    cases = [(Q4_K, 0, 1, 512, 4096, 11), (Q6_K, 0, 4, 300, 14336, 12), (Q8_0, 0, 16, 200, 1024, 13),
+             (Q5_K, Q6K_NODESTOR, 3, 256, 8192, 14), (Q5_K, Q6K_GGML, 2, 96, 2048, 15)]
+    for t, lay, m, n, k, seed in cases:
+        w = torch.from_numpy(Q.synthetic_weights(n, k, t, seed=seed, q6k_layout=lay)).cuda()
         outs = []
         for call in range(2):  # two calls in a row, different activations
             x = torch.from_numpy(Q.synthetic_activations(m, k, seed=100 * seed + call)).cuda()
             y = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
-            rc = lib.nsq_gemv_noalloc(w.data_ptr(), t, 0, x.data_ptr(), y.data_ptr(), m, n, k, st)
+            rc = lib.nsq_gemv_noalloc(w.data_ptr(), t, lay, x.data_ptr(), y.data_ptr(), m, n, k, st)
             assert rc == 0, _lib.strerror(rc)
-            ref = _gemv_reference(lib, w, t, x, n, k)
+            ref = _gemv_reference(lib, w, t, lay, x, n, k)
             torch.cuda.synchronize()
             assert torch.isfinite(y).all()
             assert rel_err(y.cpu().numpy(), ref.cpu().numpy()) <= GEMV_TOL
