@@ -1,57 +1,61 @@
-"""Benchmark: Llama-3-8B-shaped Q4_K_M decode over GGUF blocks on B200.
+"""Benchmark: GGUF block-quantized decode GEMV and prefill GEMM on B200.
 
-Workload (one "step" = one decode token, M = 1, through a stack of L = 32
-Llama-3-8B-shaped layers, each with 7 projections):
+Headline (one "step" = one decode token, M = 1, through L = 32 Llama-3-8B-shaped
+layers, each with 7 projections):
   q, o  [4096 x 4096]  Q4_K     k [1024 x 4096]  Q4_K     v [1024 x 4096]  Q6_K
   gate, up [14336 x 4096] Q4_K  down [4096 x 14336] Q6_K          (138.9 MB / layer)
 Weights are N(0, 0.02) quantized on the host by planejaja_b200.quantize (seed
-1000), activations N(0, 1) (seed 2000); synthetic data, random-init weights.
-The 32 layers are distinct device copies (4.44 GB), so every step streams far
-more than the 126 MB L2 and consecutive steps never hit in L2.
+1000 + projection index), activations N(0, 1) (seed 2000 + activation index);
+synthetic data and random-init weights stand in for the Llama checkpoints.  The
+32 layers are distinct device copies (4.44 GB), so every step streams far more
+than the 126 MB L2 and consecutive steps never hit in L2.
 
 Per layer, one fused GEMV launch per shared activation: q|k|v (attention
 input), o, gate|up (FFN input), down -- 4 kernels, activations quantized on
 chip.  A step is captured once as a CUDA graph and replayed.
 
-With --gpus N > 1 (torchrun, one process per GPU): every projection is
-row-sharded across the ranks (each rank holds N_out / N rows of each matrix)
-and each GEMV stores its output rows into every rank's output buffer over
-NVLink (the all-gather a tensor-parallel decode needs, fused into the GEMV;
-nsq_gemv_multi_xchg), strong scaling, total work fixed.  --exchange nccl
-runs the GEMV followed by an NCCL all_gather per projection instead.
-
---workload l2-7b: Llama-2-7B in Q4_0 (q, k, v, o [4096 x 4096], gate / up
-[11008 x 4096], down [4096 x 11008]; 32 layer copies, 3.64 GB per step), the
-7 projections of a layer in the same 4 fused launches.
-
---workload l2-70b-ffn --tokens {1,16}: the Llama-2-70B FFN (gate|up [28672 x 8192]
-Q4_K, down [8192 x 28672] Q4_K; 8 layer copies, 3.17 GB), the row-sharded
-configuration measured at 1/2/4/8 GPUs.
-
 metric  : decode GEMV HBM GB/s = (weight bytes + fp32 activations + fp32
           outputs) of the whole step / step time (max over ranks), all ranks.
-e2e     : the same step through the C-ABI engine calls with host buffers:
-          pinned-host -> device copy of the step's activation vectors (the
-          inputs every layer copy reads), the GEMVs, one device ->
-          pinned-host copy of all outputs of all layers (one contiguous
-          buffer), stream sync per step.
-roofline: dominant kernel = the fused M = 1 Q4_K gate|up launch (FFN input
-          projection, 2 x [14336 x 4096], 66.06 MB), timed alone with CUDA
-          events rotating over the 32 layer copies; bound = HBM, peak =
-          MEASURED_PEAKS.json hbm_gbs.
-prefill : the tcgen05 GEMM on Q4_K [14336 x 4096] at M = 512 tokens, TFLOP/s.
+e2e     : the same step through the C-ABI calls with host buffers: pinned-host
+          -> device copy of the step's activation vectors, the GEMVs, one
+          device -> pinned-host copy of all outputs of all layers, stream sync.
+roofline: dominant kernel = the fused M = 1 Q4_K gate|up launch (2 x [14336 x
+          4096], 66.19 MB), timed alone with CUDA events over the 32 layer
+          copies; bound = HBM, peak = MEASURED_PEAKS.json hbm_gbs.  "kernels"
+          gives the same for each of the step's four launches.
+workloads (N = 1): the other configurations, one record each -- Llama-3-8B at
+          M = 4 and 16, the same step with v and down in the reference's own
+          Q6_K layout (NODESTOR, dequant_q6k.comp), Llama-2-7B Q4_0, and the
+          Llama-2-70B FFN (gate|up [28672 x 8192], down [8192 x 28672], Q4_K)
+          at M = 1 and 16.
+prefill : the tcgen05 GEMM on Q4_K [14336 x 4096] and Q6_K [4096 x 14336] (both
+          layouts) at M = 128 / 512 / 2048 tokens, TFLOP/s against the measured
+          bf16 peak.
 cpu_baseline: the CPU oracle (C restatement of the reference's dequant +
-          cpu_matmul_f32 composition) on one layer, all host threads.
+          cpu_matmul_f32) on one layer, all host threads, rows walked
+          contiguously; cpu_baseline_single: the reference's own loop order on
+          one pinned core (dequant, transpose to [K x N], cpu_matmul_f32 with
+          stride-N reads of B).
+
+--gpus N > 1 (torchrun, one process per GPU): the headline is N independent
+replicas of the Llama-3-8B step (weak scaling: an 8B model fits one GPU and is
+served by replicas; no collective).  The tensor-parallel forms are
+"tp_workloads" (strong scaling): every projection row-sharded across the ranks,
+each GEMV storing its output rows into every rank's buffer over NVLink (the
+all-gather fused into the GEMV, nsq_gemv_multi_xchg) -- the Llama-3-8B step and
+the Llama-2-70B FFN at M = 1 and 16 -- plus the 70B FFN with an NCCL all_gather
+after each GEMV instead.
 
 --impl reference times that CPU path alone (the reference is Rust/Vulkan;
-neither toolchain nor a Vulkan driver exists on the box) on the same
-workload, a bounded sample per step.
+neither toolchain nor a Vulkan driver exists on the box) on the same workload,
+a bounded sample per step.
 """
 from __future__ import annotations
 
 import argparse
 import ctypes
 import json
+import multiprocessing
 import os
 import statistics
 import sys
@@ -112,6 +116,10 @@ FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
 METRIC = "decode GEMV HBM GB/s (Llama-3-8B Q4_K_M, M=1)"
 UNIT = "GB/s"
+PREFILL_SHAPES = [("Q4_K", 14336, 4096, 12, 0), ("Q6_K", 4096, 14336, 14, 0), ("Q6_K_nodestor", 4096, 14336, 14, 1)]
+PREFILL_M = [128, 512, 2048]
+POOL = None  # spawn-started process pool for host-side quantisation (before any GPU call)
+_HOST_CACHE = {}
 
 
 def select_workload(name: str, m: int) -> None:
@@ -131,24 +139,51 @@ def peaks():
     return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
 
 
-def layer_bytes_total():
+def workload_bytes(name: str, m: int):
+    """(weight, activation, output) bytes of one layer of a workload."""
     from planejaja_b200.formats import fmt
-    w = sum(fmt(t).tensor_bytes(n, k) for _, n, k, t in LAYER_SPEC)
-    x = sum(M_TOK * k * 4 for _, n, k, t in LAYER_SPEC)
-    y = sum(M_TOK * n * 4 for _, n, k, t in LAYER_SPEC)
+    spec = WORKLOADS[name]["spec"]
+    w = sum(fmt(t).tensor_bytes(n, k) for _, n, k, t in spec)
+    x = sum(m * k * 4 for _, n, k, t in spec)
+    y = sum(m * n * 4 for _, n, k, t in spec)
     return w, x, y
 
 
+def layer_bytes_total():
+    return workload_bytes(WORKLOAD, M_TOK)
+
+
+def _quant_job(job):
+    from planejaja_b200 import quantize as Q
+    key, n, k, t, seed, layout, rows = job
+    return key, Q.synthetic_weights(n, k, t, seed=seed, q6k_layout=layout, rows=rows)
+
+
+def host_weights(name: str, q6k_layout: int = 0, world: int = 1, rank: int = 0):
+    """Quantized bytes of one layer, {projection: uint8 array}; with world > 1
+    only this rank's row shard of each matrix (a contiguous byte range)."""
+    key = (name, q6k_layout, world, rank)
+    if key in _HOST_CACHE:
+        return _HOST_CACHE[key]
+    jobs = []
+    for i, (nm, n, k, t) in enumerate(WORKLOADS[name]["spec"]):
+        rows = None if world == 1 else (rank * n // world, (rank + 1) * n // world)
+        jobs.append((nm, n, k, t, SEED_W + i, q6k_layout if t in (13, 14) else 0, rows))
+    out = dict(POOL.map(_quant_job, jobs)) if POOL is not None else dict(map(_quant_job, jobs))
+    _HOST_CACHE[key] = out
+    return out
+
+
 def host_layer():
-    """Quantized bytes of one layer, {name: uint8 array [N * row_bytes]}."""
-    from planejaja_b200 import quantize as Q
-    return {name: Q.synthetic_weights(n, k, t, seed=SEED_W + i)
-            for i, (name, n, k, t) in enumerate(LAYER_SPEC)}
+    """Quantized bytes of one layer of the selected workload."""
+    return host_weights(WORKLOAD)
 
 
-def host_acts():
+def host_acts(name: str = None, m: int = None):
     from planejaja_b200 import quantize as Q
-    return [Q.synthetic_activations(M_TOK, k, seed=SEED_X + i).reshape(-1) for i, k in enumerate(ACT_K)]
+    name, m = name or WORKLOAD, m or M_TOK
+    return [Q.synthetic_activations(m, k, seed=SEED_X + i).reshape(-1)
+            for i, k in enumerate(WORKLOADS[name]["act_k"])]
 
 
 class ClockSampler:
@@ -208,8 +243,8 @@ class ClockSampler:
 # --------------------------------------------------------------------------- CPU (oracle) legs
 def cpu_leg(layer, acts, rows_frac: float = 1.0, reps: int = 1, threads: int = 0, min_seconds: float = 0.0):
     """Time the oracle's dequant + cpu_matmul_f32 composition over (a row
-    sample of) one layer, `reps` times or until `min_seconds` have passed;
-    returns (GB/s, bytes, seconds, threads)."""
+    sample of) one layer, rows walked contiguously, `reps` times or until
+    `min_seconds` have passed; returns (GB/s, bytes, seconds, threads)."""
     from oracle import oracle as O
     from planejaja_b200.formats import fmt
     O.build()
@@ -232,6 +267,44 @@ def cpu_leg(layer, acts, rows_frac: float = 1.0, reps: int = 1, threads: int = 0
     return nbytes * done / dt / 1e9, nbytes * done, dt, th
 
 
+def cpu_leg_reference_loop(layer, acts):
+    """The reference's own CPU path, single-threaded and pinned to one core:
+    each matrix dequantized to f32 (Q4_K through the AVX2 restatement of
+    simd_x86.rs, the other formats through their scalar restatements),
+    transposed to the [K x N] layout cpu_matmul_f32 takes, then
+    cpu_matmul_f32's i-j-l loop with stride-N reads of B
+    (pipeline.rs:1256-1268).  Returns the record for the bench line."""
+    from oracle import oracle as O
+    O.build()
+    old = os.sched_getaffinity(0)
+    core = min(old)
+    os.sched_setaffinity(0, {core})
+    try:
+        t_dq = t_tr = t_mm = 0.0
+        nbytes = 0
+        for name, n, k, t in LAYER_SPEC:
+            w, x = layer[name], acts[ACT_OF[name]]
+            s = time.perf_counter()
+            wf = O.dequant_q4_k_avx2(w) if t == 12 else O.dequant(w, t)
+            t_dq += time.perf_counter() - s
+            s = time.perf_counter()
+            b = np.ascontiguousarray(wf.reshape(n, k).T)
+            t_tr += time.perf_counter() - s
+            s = time.perf_counter()
+            O.matmul_f32(x.reshape(-1, k), b, x.size // k, k, n)
+            t_mm += time.perf_counter() - s
+            nbytes += w.nbytes + x.nbytes + (x.size // k) * n * 4
+            del wf, b
+    finally:
+        os.sched_setaffinity(0, old)
+    total = t_dq + t_tr + t_mm
+    return {"value": round(nbytes / total / 1e9, 4), "unit": UNIT, "cores": 1, "kind": "port",
+            "loop": "reference order: dequant, transpose to [K x N], cpu_matmul_f32 i-j-l with stride-N B reads",
+            "pinned": f"sched_setaffinity to core {core}",
+            "sample": f"one whole layer ({nbytes / 1e6:.1f} MB of weights and activations)",
+            "dequant_s": round(t_dq, 3), "transpose_s": round(t_tr, 3), "matmul_s": round(t_mm, 3)}
+
+
 def run_reference(args, rank, world):
     """--impl reference: the CPU restatement of the reference path, timed on the host."""
     if rank != 0:
@@ -250,12 +323,15 @@ def run_reference(args, rank, world):
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(1e3 * secs / max(1, args.steps), 3), "higher_is_better": True,
-        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": WORKLOADS[WORKLOAD]["desc"].format(m=M_TOK, layers=1),
                    "sample": f"{args.ref_frac:.4f} of the rows of each of the {len(LAYER_SPEC)} matrices of one "
                              f"layer per step",
                    "layers_per_step": 1, "batch": M_TOK},
         "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": th, "kind": "port",
+                         "loop": "rows walked contiguously (each W row dequantized once, its dot product in "
+                                 "cpu_matmul_f32's order), all host threads; the reference's own loop is "
+                                 "single-threaded with stride-N reads and slower",
                          "sample": f"{args.ref_frac:.4f} of one layer's rows per step "
                                    f"({(w * args.ref_frac) / 1e6:.1f} MB of weights)"},
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -263,314 +339,430 @@ def run_reference(args, rank, world):
     print(json.dumps(out), flush=True)
 
 
-# --------------------------------------------------------------------------- GPU leg
-def run_gpu(args, rank, world, local_rank):
-    import torch
-    import torch.distributed as dist
+# --------------------------------------------------------------------------- GPU legs
+class Ctx:
+    """Per-rank GPU context shared by the legs."""
 
-    from planejaja_b200 import _lib
-    from planejaja_b200.engine import CudaEngine
-    from planejaja_b200.formats import fmt
+    def __init__(self, world, rank, local_rank):
+        import torch
+        from planejaja_b200.engine import CudaEngine
+        self.world, self.rank, self.local_rank = world, rank, local_rank
+        self.dev = torch.device("cuda", local_rank)
+        torch.cuda.set_device(self.dev)
+        self.eng = CudaEngine(local_rank)
+        self.lib = self.eng.lib
+        self.launches = 0
 
-    dev = torch.device("cuda", local_rank)
-    torch.cuda.set_device(dev)
-    eng = CudaEngine(local_rank)
-    lib = eng.lib
-    L = args.layers
+    def barrier(self):
+        import torch.distributed as dist
+        if self.world > 1:
+            dist.barrier(device_ids=[self.local_rank])
 
-    layer = host_layer()
-    acts_h = host_acts()
-
-    # shard rows (contiguous byte ranges) and upload; layer copies are device clones
-    shards = {}
-    for name, n, k, t in LAYER_SPEC:
-        rb = fmt(t).row_bytes(k)
-        assert n % world == 0
-        rows = n // world
-        shards[name] = (rows, eng.upload(layer[name][rank * rows * rb:(rank + 1) * rows * rb]))
-    layers = []
-    for li in range(L):
-        layers.append({name: (rows, buf if li == 0 else buf.clone()) for name, (rows, buf) in shards.items()})
-    acts = [torch.from_numpy(a).to(dev) for a in acts_h]
-    M = M_TOK
-    def flat_views(sizes):
-        # one contiguous device buffer per step's outputs (one read-back per step)
-        flat = torch.empty(L * sum(M * n for _, n in sizes), dtype=torch.float32, device=dev)
-        views, off = [], 0
-        for _ in range(L):
-            d = {}
-            for name, n in sizes:
-                d[name] = flat[off:off + M * n]
-                off += M * n
-            views.append(d)
-        return flat, views
-
-    outs_local_flat, outs_local = flat_views([(name, rows) for name, (rows, _) in layers[0].items()])
-    # scratch for prepared activations when they do not fit on chip (M > 4 or long rows)
-    ws = eng.workspace(lib.nsq_gemv_workspace_size(M, max(ACT_K)))
-    ws_ptr, ws_n = ws.data_ptr(), ws.numel()
-    p2p = world > 1 and args.exchange == "p2p"
-    exchange = None
-    if p2p:
-        # full outputs of every projection live in the exchange buffer; each
-        # GEMV stores its rows into every rank's buffer (all-gather fused)
-        from planejaja_b200.sharded import Exchange, OutputLayout, xsegments
-        layout = OutputLayout()
-        for li in range(L):
-            for name, n, k, t in LAYER_SPEC:
-                layout.add((li, name), M, n)
-        exchange = Exchange(layout.nbytes)
-        outs_full = [{name: exchange.view(layout.offsets[(li, name)][0], (M * n,)) for name, n, k, t in LAYER_SPEC}
-                     for li in range(L)]
-    elif world > 1:
-        outs_full_flat, outs_full = flat_views([(name, n) for name, n, k, t in LAYER_SPEC])
-    else:
-        outs_full_flat, outs_full = outs_local_flat, outs_local
-    # one fused launch per shared activation (q|k|v, o, gate|up, down for Llama-3-8B)
-    TYPE_OF = {name: t for name, n, k, t in LAYER_SPEC}
-    N_OF = {name: n for name, n, k, t in LAYER_SPEC}
-    seg_arrays = []
-    xseg_arrays = []
-    for li in range(L):
-        per, xper = [], []
-        for a, names in GROUPS:
-            arr = (_lib.Segment * len(names))()
-            for i, nm in enumerate(names):
-                rows, w = layers[li][nm]
-                arr[i] = _lib.Segment(w.data_ptr(), TYPE_OF[nm], 0, rows, outs_local[li][nm].data_ptr())
-            per.append((a, names, arr))
-            if p2p:
-                xper.append((a, names, xsegments([(layers[li][nm][1].data_ptr(), TYPE_OF[nm], 0, layers[li][nm][0],
-                                                   rank * layers[li][nm][0], N_OF[nm],
-                                                   layout.offsets[(li, nm)][0]) for nm in names])))
-        seg_arrays.append(per)
-        xseg_arrays.append(xper)
-    n_launch = 0
-
-    def step():
-        nonlocal n_launch
-        n_launch = 0
-        st = torch.cuda.current_stream(dev).cuda_stream
-        if p2p:
-            for li in range(L):
-                for a, names, arr in xseg_arrays[li]:
-                    rc = lib.nsq_gemv_multi_xchg(ctypes.cast(arr, ctypes.c_void_p), len(names), acts[a].data_ptr(),
-                                                 M, ACT_K[a], exchange.comm, ws_ptr, ws_n, st)
-                    assert rc == 0, rc
-                    n_launch += 1
-            exchange.wait(st)  # the step ends when every rank's rows have landed here
-            n_launch += 1
-            return
-        for li in range(L):
-            for a, names, arr in seg_arrays[li]:
-                rc = lib.nsq_gemv_multi(ctypes.cast(arr, ctypes.c_void_p), len(names), acts[a].data_ptr(), M,
-                                        ACT_K[a], ws_ptr, ws_n, st)
-                assert rc == 0, rc
-                n_launch += 1
-                if world > 1:
-                    for nm in names:
-                        dist.all_gather_into_tensor(outs_full[li][nm], outs_local[li][nm])
-
-    # warm + capture (single GPU: the whole step as one CUDA graph)
-    step()
-    torch.cuda.synchronize()
-    graph = None
-    if not args.no_graph:
-        # the whole step, NCCL all-gathers included for N > 1, as one graph
-        s = torch.cuda.Stream(dev)
-        s.wait_stream(torch.cuda.current_stream(dev))
-        with torch.cuda.stream(s):
-            step()
-        torch.cuda.current_stream(dev).wait_stream(s)
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=s):
-            step()
-        torch.cuda.synchronize()
-    launches_per_step = n_launch
-
-    def run_step():
-        if graph is not None:
-            graph.replay()
-        else:
-            step()
-
-    def barrier():
-        if world > 1:
-            dist.barrier(device_ids=[local_rank])
-
-    def max_over_ranks(v):
-        if world == 1:
+    def max_over_ranks(self, v):
+        import torch
+        import torch.distributed as dist
+        if self.world == 1:
             return v
-        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        t = torch.tensor([v], dtype=torch.float64, device=self.dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    for _ in range(args.warmup):
-        run_step()
-    torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ else local_rank) as clk:
-        ev0.record()
-        for _ in range(args.steps):
-            run_step()
-        ev1.record()
+
+class DecodeStep:
+    """One decode step of a workload on this rank: L distinct layer copies, one
+    fused GEMV launch per shared activation, captured as one CUDA graph.
+
+    mode "single": every matrix whole on this GPU (N = 1, or one replica per
+    rank); "p2p": rows sharded over the ranks, all-gather fused into the GEMV;
+    "nccl": rows sharded, an NCCL all_gather after each GEMV."""
+
+    def __init__(self, ctx, name, m, L, mode="single", q6k_layout=0, graph=True):
+        import torch
+        import torch.distributed as dist
+        from planejaja_b200 import _lib
+        from planejaja_b200.formats import fmt
+        self.ctx, self.name, self.m, self.L, self.mode = ctx, name, m, L, mode
+        wl = WORKLOADS[name]
+        self.spec, self.groups, self.act_k = wl["spec"], wl["groups"], wl["act_k"]
+        eng, lib, dev = ctx.eng, ctx.lib, ctx.dev
+        world, rank = (ctx.world, ctx.rank) if mode != "single" else (1, 0)
+        self.world = world
+        hw = host_weights(name, q6k_layout, world, rank)
+        self.type_of = {nm: t for nm, n, k, t in self.spec}
+        self.n_of = {nm: n for nm, n, k, t in self.spec}
+        self.layout_of = {nm: (q6k_layout if t in (13, 14) else 0) for nm, n, k, t in self.spec}
+        rows_of = {nm: n // world for nm, n, k, t in self.spec}
+        base = {nm: eng.upload(hw[nm]) for nm in hw}
+        del hw
+        self.layers = [{nm: (rows_of[nm], b if li == 0 else b.clone()) for nm, b in base.items()} for li in range(L)]
+        self.acts_h = host_acts(name, m)
+        self.acts = [torch.from_numpy(a).to(dev) for a in self.acts_h]
+        M = m
+
+        def flat_views(sizes):
+            flat = torch.empty(L * sum(M * n for _, n in sizes), dtype=torch.float32, device=dev)
+            views, off = [], 0
+            for _ in range(L):
+                d = {}
+                for nm, n in sizes:
+                    d[nm] = flat[off:off + M * n]
+                    off += M * n
+                views.append(d)
+            return flat, views
+
+        self.outs_local_flat, self.outs_local = flat_views([(nm, rows_of[nm]) for nm, n, k, t in self.spec])
+        self.ws = eng.workspace(lib.nsq_gemv_workspace_size(M, max(self.act_k)))
+        self.exchange = None
+        if mode == "p2p":
+            from planejaja_b200.sharded import Exchange, OutputLayout, xsegments
+            layout = OutputLayout()
+            for li in range(L):
+                for nm, n, k, t in self.spec:
+                    layout.add((li, nm), M, n)
+            self.exchange = Exchange(layout.nbytes)
+            self.out_dev = torch.as_tensor(self.exchange.view(0, (layout.nbytes // 4,)))
+        elif mode == "nccl":
+            self.outs_full_flat, self.outs_full = flat_views([(nm, n) for nm, n, k, t in self.spec])
+            self.out_dev = self.outs_full_flat
+        else:
+            self.out_dev = self.outs_local_flat
+        self.calls = []  # per layer, per fused launch: (activation index, names, ctypes array)
+        for li in range(L):
+            per = []
+            for a, names in self.groups:
+                if mode == "p2p":
+                    arr = xsegments([(self.layers[li][nm][1].data_ptr(), self.type_of[nm], self.layout_of[nm],
+                                      rows_of[nm], rank * rows_of[nm], self.n_of[nm],
+                                      layout.offsets[(li, nm)][0]) for nm in names])
+                else:
+                    arr = (_lib.Segment * len(names))()
+                    for i, nm in enumerate(names):
+                        arr[i] = _lib.Segment(self.layers[li][nm][1].data_ptr(), self.type_of[nm], self.layout_of[nm],
+                                              rows_of[nm], self.outs_local[li][nm].data_ptr())
+                per.append((a, names, arr))
+            self.calls.append(per)
+        wb = sum(fmt(t).tensor_bytes(n, k) for _, n, k, t in self.spec)
+        xb = sum(M * k * 4 for _, n, k, t in self.spec)
+        yb = sum(M * n * 4 for _, n, k, t in self.spec)
+        self.step_bytes = (wb + xb + yb) * L  # the whole job's bytes (all ranks together when sharded)
+        self.weight_bytes = wb * L
+        self.n_launch = 0
+        self.graph = None
+        self._dist = dist
+        self.step()
         torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
-    ms = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps
-    wb, xb, yb = layer_bytes_total()
-    step_bytes = (wb + xb + yb) * L
-    value = step_bytes / (ms * 1e-3) / 1e9
+        if graph:
+            s = torch.cuda.Stream(dev)
+            s.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(s):
+                self.step()
+            torch.cuda.current_stream(dev).wait_stream(s)
+            torch.cuda.synchronize()
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph, stream=s):
+                self.step()
+            torch.cuda.synchronize()
 
-    # ---- e2e: host buffers through the C-ABI calls, copies inside the timed region
-    # the step's inputs are its activation vectors (every layer copy reads
-    # the same ones); its result is every output of every layer, read back
-    # in one copy from the contiguous output buffer
-    acts_pin = [torch.from_numpy(a).pin_memory() for a in acts_h]
-    if p2p:
-        out_dev = torch.as_tensor(exchange.view(0, (layout.nbytes // 4,)))
-    else:
-        out_dev = outs_full_flat
-    out_pin = torch.empty(out_dev.numel(), dtype=torch.float32).pin_memory()
-    h2d = sum(a.numel() * 4 for a in acts_pin)
-    d2h = out_pin.numel() * 4
+    def launch(self, li, gi, st):
+        """One fused launch (layer li, launch gi) on stream st."""
+        lib, M = self.ctx.lib, self.m
+        a, names, arr = self.calls[li][gi]
+        if self.mode == "p2p":
+            rc = lib.nsq_gemv_multi_xchg(ctypes.cast(arr, ctypes.c_void_p), len(names), self.acts[a].data_ptr(), M,
+                                         self.act_k[a], self.exchange.comm, self.ws.data_ptr(), self.ws.numel(), st)
+        else:
+            rc = lib.nsq_gemv_multi(ctypes.cast(arr, ctypes.c_void_p), len(names), self.acts[a].data_ptr(), M,
+                                    self.act_k[a], self.ws.data_ptr(), self.ws.numel(), st)
+        assert rc == 0, rc
 
-    def e2e_step():
-        for a, src in enumerate(acts_pin):
-            acts[a].copy_(src, non_blocking=True)
-        run_step()
-        out_pin.copy_(out_dev, non_blocking=True)
-        torch.cuda.current_stream(dev).synchronize()
+    def step(self):
+        import torch
+        st = torch.cuda.current_stream(self.ctx.dev).cuda_stream
+        n = 0
+        for li in range(self.L):
+            for gi, (a, names, arr) in enumerate(self.calls[li]):
+                self.launch(li, gi, st)
+                n += 1
+                if self.mode == "nccl":
+                    for nm in names:
+                        self._dist.all_gather_into_tensor(self.outs_full[li][nm], self.outs_local[li][nm])
+        if self.mode == "p2p":
+            self.exchange.wait(st)  # the step ends when every rank's rows have landed here
+            n += 1
+        self.n_launch = n
 
-    for _ in range(args.warmup):
-        e2e_step()
-    barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        e2e_step()
-    e1.record()
-    torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
-    e2e_value = step_bytes / (e2e_ms * 1e-3) / 1e9
+    def run(self):
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self.step()
 
-    hbm_peak, bf16_peak, peak_kind = peaks()
-    result = {
-        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
-        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "int8x2-dp4a/f32",
-        "data": "synthetic (N(0,0.02) weights quantized on host; N(0,1) activations)",
-        "config": {"workload": WORKLOADS[WORKLOAD]["desc"].format(m=M, layers=L),
-                   "layers": L, "batch": 1, "weight_bytes_per_step": wb * L,
-                   "parallelism": (f"tp{world} row-sharded, all-gather fused into the GEMV (NVLink peer stores)"
-                                   if p2p else f"tp{world} row-sharded + NCCL all-gather") if world > 1 else "single GPU",
-                   "l2": f"inputs larger than L2: {L} distinct layer copies, {wb * L / 1e9:.2f} GB per step",
-                   "cuda_graph": graph is not None},
-        "frac_of_nominal_8tbs": round(value / NOMINAL_HBM_GBS, 4),
-        "gpu_launches": launches_per_step * args.steps,
-        "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "ms_per_step": round(e2e_ms, 4)},
-    }
-    clocks = clk.summary()
-
-    # ---- dominant kernel alone: the fused Q4_K gate|up launch (FFN input
-    # projection, 2 x [14336 x 4096]) over the layer copies
-    if not args.skip_roofline:
-        rows, _ = layers[0]["gate"]
-        gt = TYPE_OF["gate"]
-        gname = fmt(gt).name
-        gi = [i for i, (a, names) in enumerate(GROUPS) if "gate" in names][0]
-        ga = GROUPS[gi][0]
-        KG = ACT_K[ga]
-        gbytes = 2 * fmt(gt).tensor_bytes(rows, KG) + M * KG * 4 + 2 * M * rows * 4
-        st = torch.cuda.current_stream(dev).cuda_stream
-        gu = [seg_arrays[li][gi][2] for li in range(L)]
-        reps = max(4, 256 // L) * L
-        for i in range(L):
-            lib.nsq_gemv_multi(ctypes.cast(gu[i], ctypes.c_void_p), 2, acts[ga].data_ptr(), M, KG, ws_ptr, ws_n, st)
+    def time(self, steps, warmup):
+        """ms per step, CUDA events, max over ranks (barrier + sync on both sides)."""
+        import torch
+        ctx = self.ctx
+        for _ in range(warmup):
+            self.run()
         torch.cuda.synchronize()
-        k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        k0.record()
+        ctx.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            self.run()
+        e1.record()
+        torch.cuda.synchronize()
+        ctx.barrier()
+        torch.cuda.synchronize()
+        ctx.launches += self.n_launch * steps
+        return ctx.max_over_ranks(e0.elapsed_time(e1)) / steps
+
+    def time_e2e(self, steps, warmup):
+        """The same step with pinned-host inputs copied in and all outputs read back, per step."""
+        import torch
+        ctx, dev = self.ctx, self.ctx.dev
+        acts_pin = [torch.from_numpy(a).pin_memory() for a in self.acts_h]
+        out_pin = torch.empty(self.out_dev.numel(), dtype=torch.float32).pin_memory()
+
+        def e2e_step():
+            for a, src in enumerate(acts_pin):
+                self.acts[a].copy_(src, non_blocking=True)
+            self.run()
+            out_pin.copy_(self.out_dev, non_blocking=True)
+            torch.cuda.current_stream(dev).synchronize()
+
+        for _ in range(warmup):
+            e2e_step()
+        ctx.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize()
+        ctx.launches += self.n_launch * steps
+        ms = ctx.max_over_ranks(e0.elapsed_time(e1)) / steps
+        return ms, sum(a.numel() * 4 for a in acts_pin), out_pin.numel() * 4
+
+    def kernel_alone(self, gi, reps_min=256):
+        """One of the step's launches (index gi of a layer) alone, rotating over
+        the layer copies: (us per launch, algorithmic bytes per launch)."""
+        import torch
+        from planejaja_b200.formats import fmt
+        st = torch.cuda.current_stream(self.ctx.dev).cuda_stream
+        a, names, _ = self.calls[0][gi]
+        k = self.act_k[a]
+        nbytes = sum(fmt(self.type_of[nm]).tensor_bytes(self.n_of[nm] // self.world, k) +
+                     self.m * (self.n_of[nm] // self.world) * 4 for nm in names) + self.m * k * 4
+        for li in range(self.L):
+            self.launch(li, gi, st)
+        torch.cuda.synchronize()
+        reps = max(4, reps_min // self.L) * self.L
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
         for i in range(reps):
-            lib.nsq_gemv_multi(ctypes.cast(gu[i % L], ctypes.c_void_p), 2, acts[ga].data_ptr(), M, KG, ws_ptr, ws_n,
-                               st)
-        k1.record()
+            self.launch(i % self.L, gi, st)
+        e1.record()
         torch.cuda.synchronize()
-        kms = k0.elapsed_time(k1) / reps
-        achieved = gbytes / (kms * 1e-3) / 1e9
-        traffic = None
-        tp = os.path.join(ROOT, "profiles", "traffic.json")
-        if os.path.exists(tp):
-            keys = {"l3-8b": "gemv_fused_q4k_m1_gate_up", "l2-7b": "gemv_fused_q40_m1_gate_up"}
-            key = keys.get(WORKLOAD) if M == 1 and world == 1 else None
-            traffic = json.load(open(tp)).get(key) if key else None
-        result["roofline"] = {"bound": "hbm",
-                              "kernel": f"gemv_fused_kernel<M={M},{gname}> gate|up 2 x [{rows}x{KG}] (FFN input projection)",
-                              "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
-                              "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind,
-                              "frac_of_nominal_8tbs": round(achieved / NOMINAL_HBM_GBS, 4),
-                              "bytes_per_launch": gbytes, "us_per_launch": round(kms * 1e3, 3),
-                              "traffic": traffic}
+        self.ctx.launches += reps
+        return e0.elapsed_time(e1) / reps * 1e3, nbytes
 
-        # ---- prefill GEMM (tcgen05) on the gate matrix (Q4_K [14336 x 4096] for Llama-3-8B) at M = 512
-        import torch as T
-        pm = args.prefill_m
-        wq = layers[0]["gate"][1]
-        xp = T.randn(pm, KG, device=dev).to(T.bfloat16)
-        yp = T.empty(pm, rows, dtype=T.bfloat16, device=dev)
-        for _ in range(3):
-            lib.nsq_gemm_bf16(wq.data_ptr(), gt, 0, xp.data_ptr(), yp.data_ptr(), pm, rows, KG, st)
+    def close(self):
+        import torch
+        self.graph = None
         torch.cuda.synchronize()
-        p0, p1 = T.cuda.Event(enable_timing=True), T.cuda.Event(enable_timing=True)
-        preps = 20
-        p0.record()
-        for i in range(preps):
-            lib.nsq_gemm_bf16(layers[i % L]["gate"][1].data_ptr(), gt, 0, xp.data_ptr(), yp.data_ptr(), pm, rows,
-                              KG, st)
-        p1.record()
-        torch.cuda.synchronize()
-        pms = p0.elapsed_time(p1) / preps
-        tflops = 2.0 * pm * rows * KG / (pms * 1e-3) / 1e12
-        result["prefill"] = {"kernel": f"gemm_tc_kernel<{gname}> (tcgen05, bf16, fp32 TMEM accumulate)",
-                             "shape": f"M={pm} N={rows} K={KG}", "tflops": round(tflops, 1),
-                             "ms": round(pms, 4), "peak_tflops": bf16_peak, "peak_kind": peak_kind,
-                             "frac": round(tflops / bf16_peak, 4)}
-    result["clocks"] = clocks
-    assert eng.device_status() == 0, "a bounded device wait timed out"
+        if self.exchange is not None:
+            # no rank may unmap its buffer while a peer can still store into it
+            self.ctx.barrier()
+            self.exchange.close()
+            self.exchange = None
+        self.layers = self.calls = None
+        torch.cuda.empty_cache()
 
-    # ---- CPU baseline: oracle on one layer, all host threads (rank 0, N = 1)
+
+def workload_record(ctx, name, m, mode, steps, warmup, q6k_layout=0, hbm_peak=None):
+    st = DecodeStep(ctx, name, m, WORKLOADS[name]["layers"], mode=mode, q6k_layout=q6k_layout)
+    try:
+        ms = st.time(steps, warmup)
+        world = ctx.world
+        # replicas: every rank streams the whole step; sharded: the step's bytes once
+        total = st.step_bytes * (world if mode == "single" else 1)
+        gbs = total / (ms * 1e-3) / 1e9
+        rec = {"metric": WORKLOADS[name]["metric"].format(m=m), "value": round(gbs, 2), "unit": UNIT,
+               "ms_per_step": round(ms, 4), "layers": st.L,
+               "weight_bytes_per_step": st.weight_bytes, "q6k_layout": "nodestor" if q6k_layout else "ggml"}
+        if hbm_peak:
+            rec["frac_of_measured_hbm_per_gpu"] = round(gbs / world / hbm_peak, 4)
+        if mode != "single":
+            rec["scaling"] = "strong"
+            rec["parallelism"] = (f"tp{world} row-sharded, all-gather fused into the GEMV (NVLink peer stores)"
+                                  if mode == "p2p" else f"tp{world} row-sharded + NCCL all_gather per projection")
+        return rec
+    finally:
+        st.close()
+
+
+def prefill_records(ctx, bf16_peak, peak_kind, shapes=PREFILL_SHAPES, ms_list=PREFILL_M, reps=20):
+    """tcgen05 GEMM TFLOP/s per (format, M), rotating over 4 weight copies."""
+    import torch
+    from planejaja_b200.formats import fmt
+    eng, lib, dev = ctx.eng, ctx.lib, ctx.dev
+    st = torch.cuda.current_stream(dev).cuda_stream
+    out = []
+    for label, n, k, t, lay in shapes:
+        from planejaja_b200 import quantize as Q
+        w0 = eng.upload(Q.synthetic_weights(n, k, t, seed=SEED_W + 4, q6k_layout=lay))
+        ws = [w0] + [w0.clone() for _ in range(3)]
+        for pm in ms_list:
+            xp = torch.randn(pm, k, device=dev).to(torch.bfloat16)
+            yp = torch.empty(pm, n, dtype=torch.bfloat16, device=dev)
+            for i in range(3):
+                assert lib.nsq_gemm_bf16(ws[i].data_ptr(), t, lay, xp.data_ptr(), yp.data_ptr(), pm, n, k, st) == 0
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(reps):
+                lib.nsq_gemm_bf16(ws[i % 4].data_ptr(), t, lay, xp.data_ptr(), yp.data_ptr(), pm, n, k, st)
+            e1.record()
+            torch.cuda.synchronize()
+            ctx.launches += reps
+            ms = e0.elapsed_time(e1) / reps
+            tf = 2.0 * pm * n * k / (ms * 1e-3) / 1e12
+            out.append({"weights": f"{label} [{n}x{k}]", "M": pm, "tflops": round(tf, 1), "ms": round(ms, 4),
+                        "frac": round(tf / bf16_peak, 4), "peak_tflops": bf16_peak, "peak_kind": peak_kind})
+        del ws, w0
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_gpu(args, rank, world, local_rank):
+    import torch
+    from planejaja_b200.formats import fmt
+
+    ctx = Ctx(world, rank, local_rank)
+    hbm_peak, bf16_peak, peak_kind = peaks()
+    headline_mode = "single" if (world == 1 or not args.tp) else args.exchange
+    result = {}
+    with ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ else local_rank) as clk:
+        step = DecodeStep(ctx, WORKLOAD, M_TOK, args.layers, mode=headline_mode, graph=not args.no_graph)
+        ms = step.time(args.steps, args.warmup)
+        total = step.step_bytes * (world if headline_mode == "single" else 1)
+        value = total / (ms * 1e-3) / 1e9
+        e2e_ms, h2d, d2h = step.time_e2e(args.steps, args.warmup)
+        e2e_value = total / (e2e_ms * 1e-3) / 1e9
+        wb, xb, yb = workload_bytes(WORKLOAD, M_TOK)
+        result.update({
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "weak" if headline_mode == "single" else "strong", "vs_baseline": None,
+            "dtype": "int8x2-dp4a/f32",
+            "data": "synthetic (N(0,0.02) weights quantized on host; N(0,1) activations)",
+            "config": {"workload": WORKLOADS[WORKLOAD]["desc"].format(m=M_TOK, layers=args.layers),
+                       "layers": args.layers, "batch": M_TOK, "weight_bytes_per_step": wb * args.layers,
+                       "parallelism": ("single GPU" if world == 1 else
+                                       f"{world} independent replicas, one per GPU (no collective)"
+                                       if headline_mode == "single" else
+                                       f"tp{world} row-sharded, all-gather fused into the GEMV"),
+                       "l2": f"inputs larger than L2: {args.layers} distinct layer copies, "
+                             f"{wb * args.layers / 1e9:.2f} GB per step per replica",
+                       "cuda_graph": step.graph is not None},
+            "frac_of_nominal_8tbs": round(value / world / NOMINAL_HBM_GBS, 4),
+            "frac_of_measured_hbm_per_gpu": round(value / world / hbm_peak, 4),
+            "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": round(e2e_ms, 4)},
+        })
+
+        # ---- the step's launches alone; the dominant one (gate|up) is the roofline kernel
+        if not args.skip_roofline and headline_mode == "single":
+            kernels = {}
+            for gi, (a, names) in enumerate(step.groups):
+                us, nb = step.kernel_alone(gi)
+                kernels["|".join(names)] = {"us_per_launch": round(us, 3), "bytes_per_launch": nb,
+                                            "gbs": round(nb / (us * 1e-6) / 1e9, 1),
+                                            "frac": round(nb / (us * 1e-6) / 1e9 / hbm_peak, 4)}
+            result["kernels"] = kernels
+            gk = [g for g in kernels if "gate" in g.split("|")][0]
+            g = kernels[gk]
+            gt = step.type_of["gate"]
+            rows = step.n_of["gate"]
+            KG = step.act_k[step.groups[[i for i, (_, nm) in enumerate(step.groups) if "gate" in nm][0]][0]]
+            traffic = None
+            tp = os.path.join(ROOT, "profiles", "traffic.json")
+            if os.path.exists(tp) and M_TOK == 1 and world == 1:
+                keys = {"l3-8b": "gemv_fused_q4k_m1_gate_up", "l2-7b": "gemv_fused_q40_m1_gate_up"}
+                tr = json.load(open(tp))
+                traffic = tr.get(keys.get(WORKLOAD, ""))
+            result["roofline"] = {
+                "bound": "hbm",
+                "kernel": f"gemv_fused_kernel<M={M_TOK},{fmt(gt).name}> gate|up 2 x [{rows}x{KG}] (FFN input projection)",
+                "achieved": g["gbs"], "peak": hbm_peak, "unit": "GB/s", "frac": g["frac"], "peak_kind": peak_kind,
+                "frac_of_nominal_8tbs": round(g["gbs"] / NOMINAL_HBM_GBS, 4),
+                "bytes_per_launch": g["bytes_per_launch"], "us_per_launch": g["us_per_launch"],
+                "traffic": traffic,
+                "traffic_source": ("dram__bytes_read.sum + dram__bytes_write.sum of one launch, copied from the ncu "
+                                   "capture summarised in profiles/traffic.json (same kernel, not this run)")
+                if traffic else None}
+        n_head_launch = step.n_launch
+        step.close()
+        del step
+
+        # ---- the other configurations
+        if not args.no_sub and world == 1:
+            subs = {}
+            for key, (name, m, lay) in {"l3-8b_q6k_nodestor_m1": ("l3-8b", 1, 1), "l3-8b_m4": ("l3-8b", 4, 0),
+                                        "l3-8b_m16": ("l3-8b", 16, 0), "l2-7b_m1": ("l2-7b", 1, 0),
+                                        "l2-70b-ffn_m1": ("l2-70b-ffn", 1, 0),
+                                        "l2-70b-ffn_m16": ("l2-70b-ffn", 16, 0)}.items():
+                subs[key] = workload_record(ctx, name, m, "single", args.sub_steps, args.warmup, lay, hbm_peak)
+            result["workloads"] = subs
+            if not args.skip_roofline:
+                result["prefill"] = prefill_records(ctx, bf16_peak, peak_kind)
+        if not args.no_sub and world > 1:
+            tps = {}
+            for key, (name, m, mode) in {"tp_l3-8b_m1": ("l3-8b", 1, "p2p"),
+                                         "tp_l2-70b-ffn_m1": ("l2-70b-ffn", 1, "p2p"),
+                                         "tp_l2-70b-ffn_m16": ("l2-70b-ffn", 16, "p2p"),
+                                         "tp_l2-70b-ffn_m1_nccl": ("l2-70b-ffn", 1, "nccl")}.items():
+                tps[key] = workload_record(ctx, name, m, mode, args.sub_steps, args.warmup, 0, hbm_peak)
+            result["tp_workloads"] = tps
+    result["clocks"] = clk.summary()
+    result["gpu_launches"] = n_head_launch * args.steps  # the headline's timed region
+    result["gpu_launches_per_step"] = n_head_launch
+    result["gpu_launches_all_legs"] = ctx.launches
+    assert ctx.eng.device_status() == 0, "a bounded device wait timed out"
+
+    # ---- CPU baselines (rank 0, N = 1)
     if rank == 0 and world == 1 and not args.skip_cpu:
+        layer, acts_h = host_layer(), host_acts()
         v, nb, dt, th = cpu_leg(layer, acts_h, rows_frac=args.cpu_frac, reps=args.cpu_reps,
                                 min_seconds=args.cpu_seconds)
         result["cpu_baseline"] = {"value": round(v, 3), "unit": UNIT, "cores": th, "kind": "port",
+                                  "loop": "rows walked contiguously (each W row dequantized once, its dot product "
+                                          "in cpu_matmul_f32's order), all host threads",
                                   "sample": f"oracle dequant + cpu_matmul_f32 over {args.cpu_frac:.3f} of the rows "
                                             f"of one layer's 7 matrices, repeated for >= {args.cpu_seconds:.0f} s "
                                             f"({nb / 1e6:.1f} MB in {dt:.1f} s)"}
+        result["cpu_baseline_single"] = cpu_leg_reference_loop(layer, acts_h)
     if rank == 0:
         print(json.dumps(result), flush=True)
-    graph = None
-    if exchange is not None:
-        # no rank may unmap its buffer while a peer can still store into it
-        torch.cuda.synchronize()
-        barrier()
-        exchange.close()
 
 
 def main():
+    global POOL
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--sub-steps", type=int, default=20, help="timed steps of each extra workload record")
     ap.add_argument("--impl", default="nsq", choices=["nsq", "reference"])
     ap.add_argument("--layers", type=int, default=None, help="layer copies per step (default: the workload's)")
     ap.add_argument("--workload", default="l3-8b", choices=sorted(WORKLOADS))
     ap.add_argument("--tokens", type=int, default=1, help="tokens per decode step, M (1..16)")
-    ap.add_argument("--prefill-m", type=int, default=512)
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--no-sub", action="store_true", help="headline only (no extra workloads, no prefill)")
+    ap.add_argument("--tp", action="store_true",
+                    help="N > 1: headline tensor parallel (row-sharded) instead of independent replicas")
     ap.add_argument("--skip-roofline", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--cpu-frac", type=float, default=1.0)
@@ -578,7 +770,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-frac", type=float, default=0.25)
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
-                    help="N > 1: all-gather fused into the GEMV (p2p) or NCCL all_gather per projection")
+                    help="tensor-parallel all-gather: fused into the GEMV (p2p) or NCCL all_gather")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -589,23 +781,30 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    if args.impl == "reference":
-        run_reference(args, rank, world)
-        return
-    if world > 1:
-        import datetime
-
-        import torch
-        import torch.distributed as dist
-        torch.cuda.set_device(local_rank)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local_rank))
+    # host-side quantisation in spawned workers, started before any GPU call
+    ncpu = len(os.sched_getaffinity(0))
+    POOL = multiprocessing.get_context("spawn").Pool(max(1, min(8, ncpu // max(1, world))))
     try:
-        run_gpu(args, rank, world, local_rank)
-    finally:
+        if args.impl == "reference":
+            run_reference(args, rank, world)
+            return
         if world > 1:
+            import datetime
+
+            import torch
             import torch.distributed as dist
-            dist.destroy_process_group()
+            torch.cuda.set_device(local_rank)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local_rank))
+        try:
+            run_gpu(args, rank, world, local_rank)
+        finally:
+            if world > 1:
+                import torch.distributed as dist
+                dist.destroy_process_group()
+    finally:
+        POOL.close()
+        POOL.join()
 
 
 if __name__ == "__main__":

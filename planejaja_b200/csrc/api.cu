@@ -28,6 +28,11 @@ int run_gemv_mma(const nsq_segment* segs, int nseg, const XGroup* xg, int64_t M,
                  int num_sms, const XchgDesc* xd);
 int gemv_mma_min_m();
 bool gemv_mma_covers(const nsq_segment* segs, int nseg, int64_t M, int64_t K);
+bool tc_covers(const nsq_segment* segs, int nseg, int64_t M, int64_t K);
+int tc_min_m();
+size_t tc_workspace_bytes(int64_t K);
+int run_gemv_tc(const nsq_segment* segs, int nseg, const float* x, int64_t M, int64_t K, void* workspace,
+                cudaStream_t st, int num_sms);
 int run_gemm_bf16(const uint8_t* w, int type, int layout, const void* x, void* y, int64_t M, int64_t N, int64_t K,
                   cudaStream_t st, int num_sms);
 cudaError_t launch_matmul_f32(const float* a, const float* b, float* c, int64_t M, int64_t K, int64_t N,
@@ -40,7 +45,7 @@ cudaError_t comm_launch_wait(const nsq_comm* c, cudaStream_t st);
 static const char* const kTuneNames[kTuneCount] = {
     "NSQ_ROWS_R", "NSQ_ROWS_PPSM", "NSQ_ROWS_STAGES", "NSQ_ROWS_PRE", "NSQ_ROWS_L2HINT", "NSQ_ROWS_CPS",
     "NSQ_ROWS_C", "NSQ_ROWS_BAL", "NSQ_ROWS_CARVE", "NSQ_MMA_MIN_M", "NSQ_MMA_PPS", "NSQ_MMA_STAGES",
-    "NSQ_GEMV_GENERAL", "NSQ_GEMM_SPLIT", "NSQ_GEMM_TOK"};
+    "NSQ_GEMV_GENERAL", "NSQ_GEMM_SPLIT", "NSQ_GEMM_TOK", "NSQ_TC_MIN_M"};
 static std::atomic<int> g_tune_val[kTuneCount];
 static std::atomic<bool> g_tune_set[kTuneCount];
 static std::once_flag g_tune_once;
@@ -194,7 +199,14 @@ int nsq_dequant(const void* w, int ggml_type, int q6k_layout, int out_dtype, voi
 
 size_t nsq_gemv_workspace_size(int64_t M, int64_t K) {
   if (M <= 0 || K <= 0 || K % 32) return 0;
-  return (size_t)(M * (K / 32)) * sizeof(XGroup);
+  const size_t rec = (size_t)(M * (K / 32)) * sizeof(XGroup);
+  // 2..16 tokens over K-quants run on the tensor cores: fp16 activation
+  // tiles, min-term tiles and split-tile partial sums
+  if (M >= 2 && M <= NSQ_GEMV_MAX_M && K % 256 == 0) {
+    const size_t tc = tc_workspace_bytes(K);
+    return rec > tc ? rec : tc;
+  }
+  return rec;
 }
 
 int nsq_prepare_activations(const float* x, int64_t M, int64_t K, void* workspace, size_t workspace_bytes,
@@ -249,6 +261,16 @@ int nsq_gemv_multi(const nsq_segment* segs, int nseg, const float* x, int64_t M,
     // the on-chip path reads x with 16-byte loads; 4-byte aligned inputs go
     // through the workspace
     if (reinterpret_cast<uintptr_t>(x) & 3) return NSQ_ERR_ALIGN;
+  }
+  if (!gemv_force_general() && M >= tc_min_m() && tc_covers(segs, nseg, M, K)) {
+    // 2..16 tokens over Q4_K / ggml Q6_K: tcgen05 tensor cores (gemv_tc.cu)
+    if (!workspace) return NSQ_ERR_WORKSPACE;
+    if (reinterpret_cast<uintptr_t>(workspace) & 15) return NSQ_ERR_ALIGN;
+    if (workspace_bytes < nsq_gemv_workspace_size(M, K)) return NSQ_ERR_WORKSPACE;
+    DevInfo di;
+    if ((rc = check_device(di))) return rc;
+    rc = run_gemv_tc(segs, nseg, x, M, K, workspace, static_cast<cudaStream_t>(stream), di.num_sms);
+    if (rc != -1) return rc;
   }
   const bool mma = !gemv_force_general() && M >= gemv_mma_min_m() && gemv_mma_covers(segs, nseg, M, K);
   const bool fused = !gemv_force_general() && fused_covers(segs, nseg, K);

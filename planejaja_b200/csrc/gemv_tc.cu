@@ -1,0 +1,759 @@
+// gemv_tc.cu -- batched decode GEMV (M = 2..16 tokens) on 5th-generation
+// tensor cores (tcgen05), for the K-quant formats Q4_K and Q6_K (ggml layout).
+//
+//   y[m, n] = sum_k x[m, k] * W[n, k],   x f32 [M x K], W GGUF blocks [N x K]
+//
+// The per-32 (Q4_K) or per-16 (Q6_K) weight scale is folded into the MMA's A
+// operand, so the fp32 epilogue runs once per 256-weight super-block instead
+// of once per scale group (the cost that bounds an integer-MMA design):
+//
+//   Q4_K  w = d * sc_j * q - dmin * m_j       A = sc_j * q        (<= 945)
+//   Q6_K  w = d * sc_j * (q - 32)             A = sc_j * (q - 32) (|A| <= 4096)
+//
+// A is fp16: Q4_K's products are integers below 2048 and exact; Q6_K's are
+// exact up to 2048 in magnitude (every product the quantizer here writes)
+// and above that rounded to the nearest even integer (relative error at most
+// 2^-12 on those weights).  x enters as two fp16 operands, hi = fp16(x') and
+// lo = fp16(x' - hi), where x' = x * 2^-e_{m,s} with one power of two per
+// token and super-block chosen so that |x'| < 2^15: hi + lo carries 22 bits.
+// The tensor cores accumulate D = sum A (hi + lo) in fp32 (TMEM); the min
+// term sum_j m_j T_j (T_j = the sub-block sums of x') is a second MMA with
+// K = 8 (padded to 16) into D2.  Per super-block the epilogue adds
+//   y += 2^e * (d * D - 32 * dmin * D2)           (T enters as T / 32)
+//
+// Work split (stream-K): units are (128-row tile, super-block) pairs in
+// tile-major order; CTA i of G takes units [U i / G, U (i+1) / G).  A tile
+// that spans CTAs is finished by the last of them to arrive (a counter per
+// split tile), which sums the partials in CTA order -- deterministic, and no
+// CTA ever waits for another.
+//
+// Warp roles (512 threads, one CTA per SM):
+//   warp 0      raw producer: one 2-D TMA box [128 rows x one super-block
+//               column] of the GGUF bytes per unit (evict-first in L2)
+//   warp 1      TMEM owner; one thread issues the MMAs
+//   warp 2      B producer: x tiles (hi, lo) per 64-wide K stage, and per
+//               unit the min-term tile and the token scales, from the
+//               workspace the preparation kernel wrote
+//   warps 4..7  epilogue (TMEM lane quadrant = warp % 4, one row per thread)
+//   warps 8..15 dequant: raw bytes -> fp16 A tiles (128B-swizzled K-major),
+//               the min-term A tile and the row's d / dmin
+// Every wait is bounded (%globaltimer); a wait that gives up records
+// NSQ_ERR_TIMEOUT and the kernel winds down.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "nsq_common.cuh"
+#include "tcgen05.cuh"
+
+namespace nsq {
+
+constexpr int TC_BM = 128;                   // weight rows per tile (UMMA M)
+constexpr int TC_BN = 16;                    // UMMA N: tokens, zero-padded
+constexpr int TC_THREADS = 512;
+constexpr int TC_EPI_WARP0 = 4;
+constexpr int TC_DQ_WARP0 = 8;
+constexpr int TC_DQ_WARPS = 8;
+constexpr int TC_A_BYTES = TC_BM * 128;      // fp16 [128 x 64], 16 KB
+constexpr int TC_B_BYTES = 2 * TC_BN * 128;  // fp16 hi [16 x 64] + lo [16 x 64], 4 KB
+constexpr int TC_COL_BYTES = 5120;           // workspace stride: B2 hi + lo (4 KB), 16 token scales, pad
+constexpr int TC_B2_BYTES = 4096;            // min-term tile (hi + lo) in shared memory
+constexpr int TC_NACC = 8;                   // units in flight between the MMA and the epilogue
+constexpr int TC_SCL_STAGES = 16;            // token scales (64 B per unit)
+constexpr int TC_GMAX = 256;                 // most CTAs a launch uses
+constexpr int TC_TMEM_COLS = 32 * TC_NACC;   // D and D2 (16 columns each) per unit in flight
+constexpr int TC_SMEM_LIMIT = 232448;
+
+enum : int { kTcQ4K = 0, kTcQ6KG = 1, kTcMixed = -1 };
+
+struct TcSeg {
+  const uint8_t* w;
+  float* y;
+  int64_t N, RB;  // rows, bytes per row
+  int code, CB;   // format, bytes per super-block column
+  int tile0;      // first tile of this segment in the concatenated tile list
+};
+
+struct TcParams {
+  CUtensorMap wmap[NSQ_MAX_SEGMENTS];  // W as [N rows x RB/2] u16, box [pitch/2 x 128]
+  TcSeg seg[NSQ_MAX_SEGMENTS];
+  int nseg, T, NSB, M;
+  int64_t U;        // units = T * NSB
+  int pitch;        // raw bytes per row per unit in shared memory
+  int raw_stages, a_stages, col_stages;
+  const uint8_t* ws_b;    // [NSB * 4][hi 2 KB | lo 2 KB]
+  const uint8_t* ws_col;  // [NSB][B2 hi 2 KB | B2 lo 2 KB | 16 f32 scales | pad]
+  float* ws_part;         // [2 * TC_GMAX][128 rows][16 tokens]
+  uint32_t* ws_cnt;       // [TC_GMAX]
+};
+
+// Workspace of the batched path: counters, B tiles, min-term tiles, partials.
+size_t tc_workspace_bytes(int64_t K) {
+  const int64_t nsb = K / 256;
+  return 1024 + (size_t)nsb * 4 * TC_B_BYTES + (size_t)nsb * TC_COL_BYTES + (size_t)2 * TC_GMAX * TC_BM * TC_BN * 4;
+}
+
+__device__ __forceinline__ void tc_grid_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void tc_grid_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------
+// Activation preparation: one warp per (token, super-block), 8 values per lane.
+__global__ void __launch_bounds__(256) tc_prep_kernel(const float* __restrict__ x, int M, int64_t K, int NSB,
+                                                      uint8_t* __restrict__ ws_b, uint8_t* __restrict__ ws_col,
+                                                      uint32_t* __restrict__ ws_cnt) {
+  tc_grid_wait();  // x comes from the previous kernel; the workspace may still be read by it
+  tc_grid_launch();
+  if (blockIdx.x == 0)
+    for (int i = threadIdx.x; i < TC_GMAX; i += blockDim.x) ws_cnt[i] = 0u;
+  const int wg = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+  const int t = wg % TC_BN, c = wg / TC_BN;
+  if (c >= NSB) return;
+  float v[8];
+  if (t < M) {
+    const float* src = x + (int64_t)t * K + 256 * (int64_t)c + 8 * lane;
+    if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+      const float4 a = *reinterpret_cast<const float4*>(src), b = *reinterpret_cast<const float4*>(src + 4);
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = src[i];
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = 0.f;
+  }
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+  for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  // e: amax * 2^-e < 2^15 (amax = f * 2^E, f in [0.5, 1)), at least -126
+  int e = 0;
+  if (amax > 0.f) {
+    const int E = (int)((__float_as_uint(amax) >> 23) & 0xFF) - 126;
+    e = max(E - 15, -126);
+  }
+  const float inv = __uint_as_float((uint32_t)(127 - e) << 23);  // 2^-e
+  const float scl = __uint_as_float((uint32_t)(127 + e) << 23);  // 2^e
+  uint32_t hw[4], lw[4];
+  float ts = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float a = v[2 * i] * inv, b = v[2 * i + 1] * inv;
+    ts += a;
+    ts += b;
+    const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
+    const __half la = __float2half_rn(a - __half2float(ha)), lb = __float2half_rn(b - __half2float(hb));
+    hw[i] = (uint32_t)__half_as_ushort(ha) | ((uint32_t)__half_as_ushort(hb) << 16);
+    lw[i] = (uint32_t)__half_as_ushort(la) | ((uint32_t)__half_as_ushort(lb) << 16);
+  }
+  // B tiles of 64-wide K stage 4c + q: row t, 16-byte chunk k8, 128B swizzle
+  const int q = lane >> 3, k8 = lane & 7;
+  uint8_t* bt = ws_b + (int64_t)(4 * c + q) * TC_B_BYTES + t * 128 + ((k8 ^ (t & 7)) << 4);
+  *reinterpret_cast<uint4*>(bt) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+  *reinterpret_cast<uint4*>(bt + TC_B_BYTES / 2) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+  // sub-block sums T_j (j = lane / 4) as T / 32, split hi / lo, at K = j of the min-term tile
+  ts += __shfl_xor_sync(0xffffffffu, ts, 1);
+  ts += __shfl_xor_sync(0xffffffffu, ts, 2);
+  const float tq = ts * 0.03125f;
+  const __half th = __float2half_rn(tq), tl = __float2half_rn(tq - __half2float(th));
+  uint8_t* col = ws_col + (int64_t)c * TC_COL_BYTES;
+  const int j = lane >> 2;
+  if ((lane & 3) == 0) {
+    const int off = t * 128 + ((0 ^ (t & 7)) << 4) + 2 * j;
+    *reinterpret_cast<__half*>(col + off) = th;
+    *reinterpret_cast<__half*>(col + 2048 + off) = tl;
+  }
+  if (lane == 1) {  // K 8..15 of the min-term tile are zero
+    const int off = t * 128 + ((1 ^ (t & 7)) << 4);
+    *reinterpret_cast<uint4*>(col + off) = make_uint4(0, 0, 0, 0);
+    *reinterpret_cast<uint4*>(col + 2048 + off) = make_uint4(0, 0, 0, 0);
+  }
+  if (lane == 2) reinterpret_cast<float*>(col + 4096)[t] = t < M ? scl : 0.f;
+}
+
+// ---------------------------------------------------------------------------
+// Dequant of one row's share of a 64-wide K stage into fp16 A chunks.
+// Thread (row, pp) writes chunks {pp, pp + 4} (pair pp) and {pp + 2, pp + 6}
+// (pair pp + 2); chunk k8 holds K 8*k8 .. 8*k8 + 7 of the stage in natural
+// order.  `raw` points at the row's super-block bytes.
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+
+// (v0, v1) fp16 with v = base + byte: PRMT of two bytes of `bytes` beside the
+// constant high byte (0x64 -> 1024 + b, 0x54 -> 64 + b / 16).
+__device__ __forceinline__ __half2 magic2(uint32_t bytes, uint32_t hi_bytes, uint32_t sel) {
+  return bits_h2(__byte_perm(bytes, hi_bytes, sel));
+}
+
+// Q4_K stage q: pair p = bytes qs[32q + 8p .. +8): low nibbles are chunk p
+// (sub-block 2q), high nibbles chunk p + 4 (sub-block 2q + 1).
+__device__ __forceinline__ void q4k_pair(const uint8_t* raw, int q, int p, __half2 s0, __half2 b0, __half2 s1,
+                                         __half2 b1, uint4& lo_chunk, uint4& hi_chunk) {
+  const uint2 w = *reinterpret_cast<const uint2*>(raw + 16 + 32 * q + 8 * p);
+  const uint32_t L0 = w.x & 0x0F0F0F0Fu, L1 = w.y & 0x0F0F0F0Fu;
+  const uint32_t H0 = (w.x >> 4) & 0x0F0F0F0Fu, H1 = (w.y >> 4) & 0x0F0F0F0Fu;
+  const uint32_t K64 = 0x64646464u;
+  // (1024 + q) * sc - 1024 * sc = sc * q exactly (one rounding of an integer <= 945)
+  lo_chunk.x = h2_bits(__hfma2(magic2(L0, K64, 0x4140), s0, b0));
+  lo_chunk.y = h2_bits(__hfma2(magic2(L0, K64, 0x4342), s0, b0));
+  lo_chunk.z = h2_bits(__hfma2(magic2(L1, K64, 0x4140), s0, b0));
+  lo_chunk.w = h2_bits(__hfma2(magic2(L1, K64, 0x4342), s0, b0));
+  hi_chunk.x = h2_bits(__hfma2(magic2(H0, K64, 0x4140), s1, b1));
+  hi_chunk.y = h2_bits(__hfma2(magic2(H0, K64, 0x4342), s1, b1));
+  hi_chunk.z = h2_bits(__hfma2(magic2(H1, K64, 0x4140), s1, b1));
+  hi_chunk.w = h2_bits(__hfma2(magic2(H1, K64, 0x4342), s1, b1));
+}
+
+// Q4_K 6-bit scale / min j of the packed 12 bytes (get_scale_min_k4,
+// q4_k.rs:120-131): sc in the low byte, m in the next.
+__device__ __forceinline__ uint32_t q4k_scale_min(uint32_t S0, uint32_t S1, uint32_t S2, int j) {
+  if (j < 4) return ((S0 >> (8 * j)) & 63) | (((S1 >> (8 * j)) & 63) << 8);
+  const int sh = 8 * (j - 4);
+  const uint32_t b2 = (S2 >> sh) & 0xFF, b0 = (S0 >> sh) & 0xFF, b1 = (S1 >> sh) & 0xFF;
+  return ((b2 & 0xF) | ((b0 >> 6) << 4)) | (((b2 >> 4) | ((b1 >> 6) << 4)) << 8);
+}
+
+// Q6_K (ggml) stage q = 64 weights of half n = q / 2: chunk k8 = p + 4h is
+// group j = 2(q & 1) + h, elements l = 8p .. 8p + 7: ql[64n + 32(j & 1) + l]
+// nibble (q & 1), qh[32n + l] bits 2j, scale sc[8n + 2j + p / 2].  The 6-bit
+// value enters as fp16 64 + 4q/16 and (4 sc) * v - 288 sc = sc (q - 32).
+__device__ __forceinline__ void q6k_pair(const uint8_t* raw, int q, int p, uint32_t ql_shift, uint4& c0, uint4& c1,
+                                         int off16) {
+  const int n = q >> 1, j0 = 2 * (q & 1);
+  uint32_t la[2], lb[2], h[2];
+  // raw is 2-byte aligned inside the column's 16-byte span (off16 = its
+  // offset); the qh / ql byte runs are read with unaligned word loads
+  ld_words_unaligned<2>(raw + 64 * n + 8 * p, la);
+  ld_words_unaligned<2>(raw + 64 * n + 32 + 8 * p, lb);
+  ld_words_unaligned<2>(raw + 128 + 32 * n + 8 * p, h);
+  (void)off16;
+  const int8_t sa = (int8_t)raw[192 + 8 * n + 2 * j0 + (p >> 1)];
+  const int8_t sb = (int8_t)raw[192 + 8 * n + 2 * (j0 + 1) + (p >> 1)];
+  const __half2 s4a = __half2half2(__int2half_rn(4 * sa)), s4b = __half2half2(__int2half_rn(4 * sb));
+  const __half2 ca = __half2half2(__int2half_rn(-288 * sa)), cb = __half2half2(__int2half_rn(-288 * sb));
+  const uint32_t K54 = 0x54545454u;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    // 4q as bytes: ((ql >> shift) & 15) << 2 | ((qh >> 2j) & 3) << 6
+    const uint32_t qa = (((la[i] >> ql_shift) & 0x0F0F0F0Fu) << 2) | (((h[i] >> (2 * j0)) & 0x03030303u) << 6);
+    const uint32_t qb = (((lb[i] >> ql_shift) & 0x0F0F0F0Fu) << 2) | (((h[i] >> (2 * j0 + 2)) & 0x03030303u) << 6);
+    const uint32_t a01 = h2_bits(__hfma2(magic2(qa, K54, 0x4140), s4a, ca));
+    const uint32_t a23 = h2_bits(__hfma2(magic2(qa, K54, 0x4342), s4a, ca));
+    const uint32_t b01 = h2_bits(__hfma2(magic2(qb, K54, 0x4140), s4b, cb));
+    const uint32_t b23 = h2_bits(__hfma2(magic2(qb, K54, 0x4342), s4b, cb));
+    if (i == 0) {
+      c0.x = a01; c0.y = a23; c1.x = b01; c1.y = b23;
+    } else {
+      c0.z = a01; c0.w = a23; c1.z = b01; c1.w = b23;
+    }
+  }
+}
+
+// CTA index owning unit u (unit ranges [U i / G, U (i+1) / G)).
+__device__ __forceinline__ int tc_owner(int64_t u, int64_t U, int G) { return (int)(((u + 1) * G - 1) / U); }
+
+template <int CODE>
+__global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_constant__ TcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int AS = p.a_stages, CS = p.col_stages, RS = p.raw_stages, PITCH = p.pitch;
+  // 1024-aligned swizzled tiles first: A and B stages, the two min-term A
+  // tiles (4 unit slots each, 16 K columns per slot), the min-term B tiles
+  uint8_t* a_sm = smem;
+  uint8_t* b_sm = a_sm + AS * TC_A_BYTES;
+  uint8_t* a2_sm = b_sm + AS * TC_B_BYTES;
+  uint8_t* col_sm = a2_sm + 2 * TC_A_BYTES;
+  float* scl_sm = reinterpret_cast<float*>(col_sm + CS * TC_B2_BYTES);     // [16][16]
+  float2* dsc = reinterpret_cast<float2*>(scl_sm + TC_SCL_STAGES * TC_BN);  // [8][128] (d, 32 dmin)
+  uint8_t* raw_sm = reinterpret_cast<uint8_t*>(dsc + TC_NACC * TC_BM);
+  const uint32_t RAW_BYTES = (uint32_t)(TC_BM * PITCH);
+  uint64_t* full = reinterpret_cast<uint64_t*>(raw_sm + RS * RAW_BYTES);
+  uint64_t* empty = full + AS;
+  uint64_t* col_full = empty + AS;
+  uint64_t* col_empty = col_full + CS;
+  uint64_t* scl_full = col_empty + CS;
+  uint64_t* scl_empty = scl_full + TC_SCL_STAGES;
+  uint64_t* a2_full = scl_empty + TC_SCL_STAGES;
+  uint64_t* a2_empty = a2_full + TC_NACC;
+  uint64_t* acc_full = a2_empty + TC_NACC;
+  uint64_t* acc_empty = acc_full + TC_NACC;
+  uint64_t* raw_full = acc_empty + TC_NACC;
+  uint64_t* raw_empty = raw_full + RS;
+  uint64_t* done = raw_empty + RS;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  int* s_last = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = (int)gridDim.x;
+  const int64_t u0 = p.U * blockIdx.x / G, u1 = p.U * (blockIdx.x + 1) / G;
+  const int nunits = (int)(u1 - u0);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < AS; ++s) {
+      mbar_init(&full[s], 1 + TC_DQ_WARPS);
+      mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < CS; ++s) {
+      mbar_init(&col_full[s], 1);
+      mbar_init(&col_empty[s], 1);
+    }
+    for (int s = 0; s < TC_SCL_STAGES; ++s) {
+      mbar_init(&scl_full[s], 1);
+      mbar_init(&scl_empty[s], 4);
+    }
+    for (int s = 0; s < TC_NACC; ++s) {
+      mbar_init(&a2_full[s], TC_DQ_WARPS);
+      mbar_init(&a2_empty[s], 4);
+      mbar_init(&acc_full[s], 1);
+      mbar_init(&acc_empty[s], 4);
+    }
+    for (int s = 0; s < RS; ++s) {
+      mbar_init(&raw_full[s], 1);
+      mbar_init(&raw_empty[s], TC_DQ_WARPS);
+    }
+    mbar_init(done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TC_TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  // unit n of this CTA -> segment, tile within it, super-block column
+  auto locate = [&](int n, int& sg, int& tl, int& c) {
+    const int64_t u = u0 + n;
+    const int t = (int)(u / p.NSB);
+    c = (int)(u - (int64_t)t * p.NSB);
+    sg = 0;
+    while (sg + 1 < p.nseg && t >= p.seg[sg + 1].tile0) ++sg;
+    tl = t - p.seg[sg].tile0;
+  };
+  // parity of the k-th use of a ring slot: full waits (k / R) & 1, empty waits its complement
+  auto ph = [](int k, int R) { return (uint32_t)((k / R) & 1); };
+
+  if (warp == 0) {
+    // ---- raw producer: the unit's GGUF column for the tile's 128 rows
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_first();
+      for (int n = 0; n < nunits; ++n) {
+        int sg, tl, c;
+        locate(n, sg, tl, c);
+        const int rs = n % RS;
+        if (!mbar_wait_bounded(&raw_empty[rs], ph(n, RS) ^ 1)) break;
+        const int x0 = (int)(((int64_t)c * p.seg[sg].CB) & ~int64_t(15)) / 2;
+        mbar_arrive_expect_tx(&raw_full[rs], RAW_BYTES);
+        asm volatile(
+            "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+            " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(raw_sm + rs * RAW_BYTES)),
+            "l"(reinterpret_cast<uint64_t>(&p.wmap[sg])), "r"(x0), "r"(tl * TC_BM), "r"(smem_u32(&raw_full[rs])),
+            "l"(pol)
+            : "memory");
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issue
+    if (lane == 0) {
+      constexpr uint32_t IDESC = umma_idesc_f16(TC_BM, TC_BN);
+      const uint32_t a_base = smem_u32(a_sm), b_base = smem_u32(b_sm), a2_base = smem_u32(a2_sm);
+      const uint32_t col_base = smem_u32(col_sm);
+      bool ok = true;
+      for (int n = 0; n < nunits && ok; ++n) {
+        const int a = n % TC_NACC;
+        const uint32_t dD = tmem + (uint32_t)(32 * a), dD2 = dD + 16;
+        if (!mbar_wait_bounded(&acc_empty[a], ph(n, TC_NACC) ^ 1)) break;
+        tc_fence_after();
+        for (int q = 0; q < 4; ++q) {
+          const int k = 4 * n + q, s = k % AS;
+          if (!mbar_wait_bounded(&full[s], ph(k, AS))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t ad = umma_desc_sw128(a_base + s * TC_A_BYTES + kk * 32);
+            const uint64_t bh = umma_desc_sw128(b_base + s * TC_B_BYTES + kk * 32);
+            const uint64_t bl = umma_desc_sw128(b_base + s * TC_B_BYTES + TC_B_BYTES / 2 + kk * 32);
+            tc_mma_bf16(dD, ad, bh, IDESC, (q | kk) ? 1u : 0u);
+            tc_mma_bf16(dD, ad, bl, IDESC, 1u);
+          }
+          tc_commit(&empty[s]);
+        }
+        if (!ok) break;
+        const int cs = n % CS;
+        if (!mbar_wait_bounded(&col_full[cs], ph(n, CS)) || !mbar_wait_bounded(&a2_full[a], ph(n, TC_NACC))) break;
+        tc_fence_after();
+        // min-term A slot a: tile a / 4, K columns 16 (a % 4) .. +16
+        const uint64_t a2d = umma_desc_sw128(a2_base + (a >> 2) * TC_A_BYTES + (a & 3) * 32);
+        tc_mma_bf16(dD2, a2d, umma_desc_sw128(col_base + cs * TC_B2_BYTES), IDESC, 0u);
+        tc_mma_bf16(dD2, a2d, umma_desc_sw128(col_base + cs * TC_B2_BYTES + TC_B2_BYTES / 2), IDESC, 1u);
+        tc_commit(&col_empty[cs]);
+        tc_commit(&acc_full[a]);
+      }
+      tc_commit(done);  // every MMA issued above has completed when this arrives
+    }
+  } else if (warp == 2) {
+    // ---- B producer: x tiles per K stage; per unit the min-term tile and the token scales
+    if (lane == 0) {
+      tc_grid_wait();  // the workspace is written by the preparation kernel
+      const uint64_t pol = l2_policy_evict_last();
+      for (int n = 0; n < nunits; ++n) {
+        int sg, tl, c;
+        locate(n, sg, tl, c);
+        bool ok = true;
+        for (int q = 0; q < 4; ++q) {
+          const int k = 4 * n + q, s = k % AS;
+          if (!mbar_wait_bounded(&empty[s], ph(k, AS) ^ 1)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], TC_B_BYTES);
+          bulk_g2s_hint(b_sm + s * TC_B_BYTES, p.ws_b + (int64_t)(4 * c + q) * TC_B_BYTES, TC_B_BYTES, &full[s], pol);
+        }
+        if (!ok) break;
+        const int cs = n % CS, ss = n % TC_SCL_STAGES;
+        const uint8_t* col = p.ws_col + (int64_t)c * TC_COL_BYTES;
+        if (!mbar_wait_bounded(&col_empty[cs], ph(n, CS) ^ 1)) break;
+        mbar_arrive_expect_tx(&col_full[cs], TC_B2_BYTES);
+        bulk_g2s_hint(col_sm + cs * TC_B2_BYTES, col, TC_B2_BYTES, &col_full[cs], pol);
+        if (!mbar_wait_bounded(&scl_empty[ss], ph(n, TC_SCL_STAGES) ^ 1)) break;
+        mbar_arrive_expect_tx(&scl_full[ss], TC_BN * 4);
+        bulk_g2s_hint(scl_sm + ss * TC_BN, col + TC_B2_BYTES, TC_BN * 4, &scl_full[ss], pol);
+      }
+    }
+  } else if (warp >= TC_DQ_WARP0) {
+    // ---- dequant: thread (row, pp) produces pairs pp and pp + 2 of every
+    // stage; a quarter-warp is 8 consecutive rows of one pair, so its
+    // 16-byte swizzled stores fall in 8 distinct bank groups
+    const int td = threadIdx.x - TC_DQ_WARP0 * 32;  // 0..255
+    const int row = (td & 7) | ((td >> 4) << 3);    // 0..127
+    const int pp = (td >> 3) & 1;
+    const int sw = row & 7;
+    for (int n = 0; n < nunits; ++n) {
+      int sg, tl, c;
+      locate(n, sg, tl, c);
+      const int code = CODE == kTcMixed ? p.seg[sg].code : CODE;
+      const int rs = n % RS, a = n % TC_NACC;
+      if (!mbar_wait_bounded(&raw_full[rs], ph(n, RS))) break;
+      const int off16 = (int)(((int64_t)c * p.seg[sg].CB) & 15);
+      const uint8_t* raw = raw_sm + rs * RAW_BYTES + row * PITCH + off16;
+      // per-unit row data: d / dmin for the epilogue, mins for the min-term MMA
+      if (!mbar_wait_bounded(&a2_empty[a], ph(n, TC_NACC) ^ 1)) break;
+      uint8_t* a2row = a2_sm + (a >> 2) * TC_A_BYTES + row * 128;
+      const int a2c = 2 * (a & 3);  // 16-byte chunks of this slot's 16 K columns
+      uint32_t S0 = 0, S1 = 0, S2 = 0;
+      if (code == kTcQ4K) {
+        const uint4 hdr = *reinterpret_cast<const uint4*>(raw);
+        S0 = hdr.y; S1 = hdr.z; S2 = hdr.w;
+        if (pp == 0) {
+          const float d = h2f((uint16_t)(hdr.x & 0xFFFF)), dmin = h2f((uint16_t)(hdr.x >> 16));
+          dsc[a * TC_BM + row] = make_float2(d, 32.0f * dmin);
+          uint32_t mw[4];
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            const uint32_t m0 = q4k_scale_min(S0, S1, S2, 2 * jj) >> 8, m1 = q4k_scale_min(S0, S1, S2, 2 * jj + 1) >> 8;
+            mw[jj] = h2_bits(__halves2half2(__uint2half_rn(m0), __uint2half_rn(m1)));
+          }
+          *reinterpret_cast<uint4*>(a2row + ((a2c ^ sw) << 4)) = make_uint4(mw[0], mw[1], mw[2], mw[3]);
+          *reinterpret_cast<uint4*>(a2row + (((a2c + 1) ^ sw) << 4)) = make_uint4(0, 0, 0, 0);
+        }
+      } else {
+        if (pp == 0) {
+          dsc[a * TC_BM + row] = make_float2(h2f((uint16_t)ld_u16(raw + 208)), 0.f);
+          *reinterpret_cast<uint4*>(a2row + ((a2c ^ sw) << 4)) = make_uint4(0, 0, 0, 0);
+          *reinterpret_cast<uint4*>(a2row + (((a2c + 1) ^ sw) << 4)) = make_uint4(0, 0, 0, 0);
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&a2_full[a]);
+      bool ok = true;
+      for (int q = 0; q < 4; ++q) {
+        const int k = 4 * n + q, s = k % AS;
+        uint4 ch[4];
+        if (code == kTcQ4K) {
+          const uint32_t sm0 = q4k_scale_min(S0, S1, S2, 2 * q), sm1 = q4k_scale_min(S0, S1, S2, 2 * q + 1);
+          const __half h0 = __uint2half_rn(sm0 & 0xFF), h1 = __uint2half_rn(sm1 & 0xFF);
+          const __half2 s0 = __half2half2(h0), s1 = __half2half2(h1);
+          const __half2 b0 = __half2half2(__hmul(h0, __float2half_rn(-1024.f)));
+          const __half2 b1 = __half2half2(__hmul(h1, __float2half_rn(-1024.f)));
+          q4k_pair(raw, q, pp, s0, b0, s1, b1, ch[0], ch[1]);
+          q4k_pair(raw, q, pp + 2, s0, b0, s1, b1, ch[2], ch[3]);
+        } else {
+          q6k_pair(raw, q, pp, 4 * (q & 1), ch[0], ch[1], off16);
+          q6k_pair(raw, q, pp + 2, 4 * (q & 1), ch[2], ch[3], off16);
+        }
+        if (!mbar_wait_bounded(&empty[s], ph(k, AS) ^ 1)) {
+          ok = false;
+          break;
+        }
+        uint8_t* dst = a_sm + s * TC_A_BYTES + row * 128;
+        *reinterpret_cast<uint4*>(dst + ((pp ^ sw) << 4)) = ch[0];
+        *reinterpret_cast<uint4*>(dst + (((pp + 4) ^ sw) << 4)) = ch[1];
+        *reinterpret_cast<uint4*>(dst + (((pp + 2) ^ sw) << 4)) = ch[2];
+        *reinterpret_cast<uint4*>(dst + (((pp + 6) ^ sw) << 4)) = ch[3];
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full[s]);
+      }
+      if (!ok) break;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&raw_empty[rs]);
+    }
+  } else if (warp >= TC_EPI_WARP0) {
+    // ---- epilogue: one weight row per thread
+    const int qd = warp & 3, row = 32 * qd + lane;
+    tc_grid_wait();  // y and the partials may still be in use by the previous kernel
+    float acc[TC_BN];
+#pragma unroll
+    for (int t = 0; t < TC_BN; ++t) acc[t] = 0.f;
+    int seg_first_c = -1;
+    // A wait that gives up stops the work but not the walk: the four warps
+    // pass the same named barriers whatever happens.
+    bool ok = true;
+    for (int n = 0; n < nunits; ++n) {
+      int sg, tl, c;
+      locate(n, sg, tl, c);
+      if (seg_first_c < 0) seg_first_c = c;
+      const int a = n % TC_NACC, ss = n % TC_SCL_STAGES;
+      if (ok)
+        ok = mbar_wait_bounded(&acc_full[a], ph(n, TC_NACC)) && mbar_wait_bounded(&a2_full[a], ph(n, TC_NACC)) &&
+             mbar_wait_bounded(&scl_full[ss], ph(n, TC_SCL_STAGES));
+      if (ok) {
+        tc_fence_after();
+        uint32_t D[16], D2[16];
+        const uint32_t taddr = tmem + ((uint32_t)(32 * qd) << 16) + (uint32_t)(32 * a);
+        tc_ld_32x32b_x16(taddr, D);
+        tc_ld_32x32b_x16(taddr + 16, D2);
+        tc_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[a]);
+        const float2 dd = dsc[a * TC_BM + row];
+        const float* sct = scl_sm + ss * TC_BN;
+#pragma unroll
+        for (int t = 0; t < TC_BN; ++t)
+          acc[t] = fmaf(sct[t], fmaf(dd.x, __uint_as_float(D[t]), -dd.y * __uint_as_float(D2[t])), acc[t]);
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&a2_empty[a]);
+          mbar_arrive(&scl_empty[ss]);
+        }
+      }
+      // end of this CTA's segment of the tile?
+      const bool last_of_tile = (c == p.NSB - 1) || (n == nunits - 1);
+      if (!last_of_tile) continue;
+      const TcSeg& S = p.seg[sg];
+      const int t_glob = S.tile0 + tl;
+      const int64_t nrow = (int64_t)tl * TC_BM + row;
+      const bool row_ok = nrow < S.N;
+      if (seg_first_c == 0 && c == p.NSB - 1) {
+        if (row_ok && ok) {
+#pragma unroll
+          for (int m = 0; m < TC_BN; ++m)
+            if (m < p.M) S.y[(int64_t)m * S.N + nrow] = acc[m];
+        }
+      } else {
+        // partial: slot 2i for the first segment of CTA i, 2i + 1 for its last
+        const bool first_seg = (int64_t)t_glob * p.NSB <= u0;
+        const int slot = 2 * (int)blockIdx.x + (first_seg ? 0 : 1);
+        float4* dst = reinterpret_cast<float4*>(p.ws_part + ((int64_t)slot * TC_BM + row) * TC_BN);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) __stcg(dst + i, make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]));
+        __threadfence();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        const int64_t ut0 = (int64_t)t_glob * p.NSB;
+        const int i_first = tc_owner(ut0, p.U, G), i_last = tc_owner(ut0 + p.NSB - 1, p.U, G);
+        if (threadIdx.x == TC_EPI_WARP0 * 32) {
+          const uint32_t old = atomicAdd(p.ws_cnt + i_first, 1u);
+          *s_last = (old == (uint32_t)(i_last - i_first)) ? 1 : 0;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (*s_last) {
+          __threadfence();
+          float sum[TC_BN];
+#pragma unroll
+          for (int t = 0; t < TC_BN; ++t) sum[t] = 0.f;
+          for (int i = i_first; i <= i_last; ++i) {
+            const int64_t ui0 = p.U * i / G;
+            const int sl = 2 * i + ((i == i_first && ui0 < ut0) ? 1 : 0);
+            const float4* src = reinterpret_cast<const float4*>(p.ws_part + ((int64_t)sl * TC_BM + row) * TC_BN);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const float4 f = __ldcg(src + q);
+              sum[4 * q] += f.x; sum[4 * q + 1] += f.y; sum[4 * q + 2] += f.z; sum[4 * q + 3] += f.w;
+            }
+          }
+          if (row_ok) {
+#pragma unroll
+            for (int m = 0; m < TC_BN; ++m)
+              if (m < p.M) S.y[(int64_t)m * S.N + nrow] = sum[m];
+          }
+          if (threadIdx.x == TC_EPI_WARP0 * 32) p.ws_cnt[i_first] = 0u;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+      }
+#pragma unroll
+      for (int t = 0; t < TC_BN; ++t) acc[t] = 0.f;
+      seg_first_c = -1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    // the final commit arrives once every MMA has completed
+    mbar_wait_bounded(done, 0);
+    tc_fence_after();
+    tmem_dealloc(tmem, TC_TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+static PFN_cuTensorMapEncodeTiled_v12000 tc_encode_fn() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+static int tc_code(int type, int layout) {
+  if (type == NSQ_TYPE_Q4_K) return kTcQ4K;
+  if (type == NSQ_TYPE_Q6_K && layout == NSQ_Q6K_GGML) return kTcQ6KG;
+  return -2;
+}
+
+// True if the batched tensor-core path covers these segments: Q4_K or ggml
+// Q6_K, K % 256 == 0, whole 16-byte rows, M in [2, 16].
+bool tc_covers(const nsq_segment* segs, int nseg, int64_t M, int64_t K) {
+  if (M < 2 || M > TC_BN || K % 256 || K <= 0 || nseg < 1 || nseg > NSQ_MAX_SEGMENTS) return false;
+  for (int i = 0; i < nseg; ++i) {
+    if (tc_code(segs[i].ggml_type, segs[i].q6k_layout) < -1) return false;
+    const int64_t rb = (K / 256) * nsq_block_bytes(segs[i].ggml_type);
+    if (rb % 16 || segs[i].N > 0x7FFFFFFF) return false;
+  }
+  return true;
+}
+
+int tc_min_m() { return tune(kTuneTcMinM, 9); }
+
+template <int CODE>
+static cudaError_t launch_tc(const TcParams& p, int blocks, size_t smem, cudaStream_t st) {
+  auto kern = gemv_tc_kernel<CODE>;
+  static size_t configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || smem > configured[dev]) {
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) configured[dev] = smem;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)blocks);
+  cfg.blockDim = dim3(TC_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+// Batched decode GEMV; -1 if not covered.  workspace: tc_workspace_bytes(K)
+// bytes, 16-byte aligned.
+int run_gemv_tc(const nsq_segment* segs, int nseg, const float* x, int64_t M, int64_t K, void* workspace,
+                cudaStream_t st, int num_sms) {
+  if (!tc_covers(segs, nseg, M, K)) return -1;
+  auto enc = tc_encode_fn();
+  if (!enc) return -1;
+  TcParams p{};
+  const int NSB = (int)(K / 256);
+  int pitch = 144, code = -2, tiles = 0;
+  for (int i = 0; i < nseg; ++i) {
+    TcSeg& s = p.seg[i];
+    s.code = tc_code(segs[i].ggml_type, segs[i].q6k_layout);
+    s.CB = (int)nsq_block_bytes(segs[i].ggml_type);
+    s.w = static_cast<const uint8_t*>(segs[i].w);
+    s.y = segs[i].y;
+    s.N = segs[i].N;
+    s.RB = (int64_t)NSB * s.CB;
+    s.tile0 = tiles;
+    tiles += (int)((s.N + TC_BM - 1) / TC_BM);
+    code = (i == 0 || code == s.code) ? s.code : kTcMixed;
+    if (s.code == kTcQ6KG) pitch = 240;  // 210-byte columns start on any even offset
+  }
+  for (int i = 0; i < nseg; ++i) {
+    cuuint64_t dims[2] = {(cuuint64_t)(p.seg[i].RB / 2), (cuuint64_t)p.seg[i].N};
+    cuuint64_t strides[1] = {(cuuint64_t)p.seg[i].RB};
+    cuuint32_t box[2] = {(cuuint32_t)(pitch / 2), (cuuint32_t)TC_BM};
+    cuuint32_t estr[2] = {1, 1};
+    if (enc(&p.wmap[i], CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint8_t*>(p.seg[i].w), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return -1;
+  }
+  p.nseg = nseg;
+  p.T = tiles;
+  p.NSB = NSB;
+  p.M = (int)M;
+  p.U = (int64_t)tiles * NSB;
+  p.pitch = pitch;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  p.ws_cnt = reinterpret_cast<uint32_t*>(ws);
+  p.ws_b = ws + 1024;
+  p.ws_col = p.ws_b + (size_t)NSB * 4 * TC_B_BYTES;
+  p.ws_part = reinterpret_cast<float*>(const_cast<uint8_t*>(p.ws_col) + (size_t)NSB * TC_COL_BYTES);
+  // shared memory: 4 A/B stages and 3 min-term stages, the raw ring takes
+  // what is left (up to 4 units)
+  const int as = 4, cs = 3;
+  const size_t fixed = 1024 + (size_t)as * (TC_A_BYTES + TC_B_BYTES) + 2 * TC_A_BYTES + (size_t)cs * TC_B2_BYTES +
+                       (size_t)TC_SCL_STAGES * TC_BN * 4 + (size_t)TC_NACC * TC_BM * 8 + 1024;
+  int rs = 4;
+  while (rs > 2 && fixed + (size_t)rs * TC_BM * pitch > (size_t)TC_SMEM_LIMIT) --rs;
+  const size_t smem = fixed + (size_t)rs * TC_BM * pitch;
+  if (smem > (size_t)TC_SMEM_LIMIT) return -1;
+  p.raw_stages = rs;
+  p.a_stages = as;
+  p.col_stages = cs;
+  int G = num_sms > 0 ? num_sms : 148;
+  if (G > TC_GMAX) G = TC_GMAX;
+  if ((int64_t)G > p.U) G = (int)p.U;
+  // activations -> fp16 B tiles, min-term tiles, scales; counters zeroed
+  {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((TC_BN * NSB + 7) / 8));
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, tc_prep_kernel, x, (int)M, K, NSB, ws + 1024,
+                           const_cast<uint8_t*>(p.ws_col), p.ws_cnt) != cudaSuccess)
+      return NSQ_ERR_CUDA;
+  }
+  cudaError_t e;
+  switch (code) {
+    case kTcQ4K: e = launch_tc<kTcQ4K>(p, G, smem, st); break;
+    case kTcQ6KG: e = launch_tc<kTcQ6KG>(p, G, smem, st); break;
+    default: e = launch_tc<kTcMixed>(p, G, smem, st); break;
+  }
+  return e == cudaSuccess ? NSQ_OK : NSQ_ERR_CUDA;
+}
+
+}  // namespace nsq

@@ -271,7 +271,7 @@ __device__ __forceinline__ bool wait_geq_bounded(const uint32_t* p, uint32_t wan
 enum TuneId : int {
   kTuneRowsR, kTuneRowsPPSM, kTuneRowsStages, kTuneRowsPre, kTuneRowsL2Hint, kTuneRowsCPS, kTuneRowsC,
   kTuneRowsBal, kTuneRowsCarve, kTuneMmaMinM, kTuneMmaPPS, kTuneMmaStages, kTuneGemvGeneral, kTuneGemmSplit,
-  kTuneGemmTok, kTuneCount
+  kTuneGemmTok, kTuneTcMinM, kTuneCount
 };
 int tune(TuneId id, int dflt);
 

@@ -215,20 +215,28 @@ def quantize(w: np.ndarray, type_id: int, q6k_layout: int = Q6K_GGML) -> np.ndar
 
 
 def synthetic_weights(n: int, k: int, type_id: int, seed: int, std: float = 0.02,
-                      q6k_layout: int = Q6K_GGML, chunk_rows: int = 2048) -> np.ndarray:
+                      q6k_layout: int = Q6K_GGML, chunk_rows: int = 2048, rows=None) -> np.ndarray:
     """W[n, k] ~ N(0, std) drawn with `seed`, quantized; returns GGUF bytes.
 
     Rows are drawn and quantized in chunks so that large matrices (e.g. the
     28672 x 8192 FFN weights) never hold the full fp32 matrix at once.
+    rows=(r0, r1) returns only the bytes of rows [r0, r1) (a row shard): the
+    rows before r0 are drawn but not quantized, so the bytes equal that slice
+    of the whole matrix's bytes.
     """
     f = fmt(type_id)
+    r_lo, r_hi = (0, n) if rows is None else (int(rows[0]), int(rows[1]))
+    if not 0 <= r_lo <= r_hi <= n:
+        raise ValueError(f"rows {rows} outside [0, {n}]")
     rng = np.random.default_rng(seed)
-    out = np.empty(f.tensor_bytes(n, k), np.uint8)
     rb = f.row_bytes(k)
-    for r0 in range(0, n, chunk_rows):
-        r1 = min(n, r0 + chunk_rows)
-        w = rng.standard_normal((r1 - r0, k), dtype=np.float32) * np.float32(std)
-        out[r0 * rb:r1 * rb] = quantize(w, type_id, q6k_layout)
+    out = np.empty((r_hi - r_lo) * rb, np.uint8)
+    for c0 in range(0, r_hi, chunk_rows):
+        c1 = min(n, c0 + chunk_rows)
+        w = rng.standard_normal((c1 - c0, k), dtype=np.float32) * np.float32(std)
+        a, b = max(c0, r_lo), min(c1, r_hi)
+        if a < b:
+            out[(a - r_lo) * rb:(b - r_lo) * rb] = quantize(w[a - c0:b - c0], type_id, q6k_layout)
     return out
 
 

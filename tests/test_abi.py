@@ -54,7 +54,13 @@ def test_block_table_matches_formats(lib):
 
 def test_workspace_size(lib):
     assert lib.nsq_gemv_workspace_size(1, 4096) == 128 * 80
-    assert lib.nsq_gemv_workspace_size(16, 14336) == 16 * 448 * 80
+    # 2..16 tokens with K % 256 == 0 may run on the tensor cores: fp16
+    # activation tiles (16 KB per 256 of K), min-term tiles (5 KB per 256),
+    # 1 KB of counters and 512 partial-sum slots of 8 KB
+    tc = 1024 + 56 * 16384 + 56 * 5120 + 512 * 8192
+    assert lib.nsq_gemv_workspace_size(16, 14336) == max(16 * 448 * 80, tc)
+    assert lib.nsq_gemv_workspace_size(2, 4096) == 1024 + 16 * 16384 + 16 * 5120 + 512 * 8192
+    assert lib.nsq_gemv_workspace_size(2, 4096 + 32) == 2 * 129 * 80
     assert lib.nsq_gemv_workspace_size(1, 33) == 0
 
 

@@ -62,3 +62,35 @@ def test_reference_arm_json_line():
     cb = line["cpu_baseline"]
     assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == line["value"]
     assert line["e2e"] == {"value": line["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+
+
+def test_row_shards_are_slices_of_the_whole_matrix():
+    """Each rank quantizes only its rows; the bytes equal that slice of the whole matrix."""
+    import numpy as np
+    from planejaja_b200 import quantize as Q
+    n, k = 6000, 512
+    whole = Q.synthetic_weights(n, k, 12, seed=5)
+    rb = fmt(12).row_bytes(k)
+    for world in (2, 4, 8):
+        parts = [Q.synthetic_weights(n, k, 12, seed=5, rows=(r * n // world, (r + 1) * n // world))
+                 for r in range(world)]
+        assert np.array_equal(np.concatenate(parts), whole)
+        assert parts[1].size == (n // world) * rb
+
+
+def test_single_thread_reference_loop_on_a_small_layer():
+    """The reference-order CPU leg (dequant, transpose, stride-N cpu_matmul_f32) on a tiny layer."""
+    try:
+        bench.select_workload("l3-8b", 1)
+        spec = [("q", 64, 512, 12), ("v", 32, 512, 14)]
+        saved = bench.LAYER_SPEC, bench.ACT_OF
+        bench.LAYER_SPEC, bench.ACT_OF = spec, {"q": 0, "v": 0}
+        from planejaja_b200 import quantize as Q
+        layer = {nm: Q.synthetic_weights(n, k, t, seed=1) for nm, n, k, t in spec}
+        acts = [Q.synthetic_activations(1, 512, seed=2).reshape(-1)]
+        rec = bench.cpu_leg_reference_loop(layer, acts)
+        assert rec["cores"] == 1 and rec["value"] > 0 and rec["matmul_s"] >= 0
+        assert "stride-N" in rec["loop"]
+    finally:
+        bench.LAYER_SPEC, bench.ACT_OF = saved
+        bench.select_workload("l3-8b", 1)

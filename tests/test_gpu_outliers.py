@@ -35,13 +35,19 @@ def eng():
     assert e.device_status() == 0
 
 
-@pytest.fixture(params=["rows", "mma", "general"])
+@pytest.fixture(params=["rows", "mma", "general", "tc"])
 def gemv_kernel(request, tuning):
     tuning.unset("NSQ_GEMV_GENERAL")
+    tuning.set("NSQ_TC_MIN_M", "17")
     if request.param == "general":
         tuning.set("NSQ_GEMV_GENERAL", "1")
     elif request.param == "mma":
         tuning.set("NSQ_MMA_MIN_M", "1")
+    elif request.param == "tc":
+        # tcgen05 path for M >= 2 over Q4_K / ggml Q6_K; the other formats
+        # (and M = 1) take the one-lane-per-row kernel
+        tuning.set("NSQ_TC_MIN_M", "2")
+        tuning.set("NSQ_MMA_MIN_M", "17")
     else:
         tuning.set("NSQ_MMA_MIN_M", "17")
     return request.param

@@ -88,15 +88,22 @@ def test_dequant_empty(eng):
 
 
 # ---------------------------------------------------------------- GEMV
-@pytest.fixture(params=["rows", "mma", "general"])
+@pytest.fixture(params=["rows", "mma", "general", "tc"])
 def gemv_kernel(request, tuning):
     """Runs a test with each GEMV kernel: one lane per row (dp4a, every M),
-    integer tensor cores (every M), and the general kernel."""
+    integer tensor cores (mma.sync, every M), the general kernel, and the
+    tcgen05 kernel (M >= 2, Q4_K and ggml Q6_K)."""
     tuning.unset("NSQ_GEMV_GENERAL")
+    tuning.set("NSQ_TC_MIN_M", "17")
     if request.param == "general":
         tuning.set("NSQ_GEMV_GENERAL", "1")
     elif request.param == "mma":
         tuning.set("NSQ_MMA_MIN_M", "1")
+    elif request.param == "tc":
+        # tcgen05 path for M >= 2 over Q4_K / ggml Q6_K; the other formats
+        # (and M = 1) take the one-lane-per-row kernel
+        tuning.set("NSQ_TC_MIN_M", "2")
+        tuning.set("NSQ_MMA_MIN_M", "17")
     else:
         tuning.set("NSQ_MMA_MIN_M", "17")
     return request.param
@@ -213,11 +220,12 @@ def _adversarial_activations(m, k, seed):
 
 
 @pytest.mark.parametrize("m", [1, 3])
-def test_gemv_on_chip_quantiser_matches_prepare_kernel(eng, m):
+def test_gemv_on_chip_quantiser_matches_prepare_kernel(eng, tuning, m):
     """The fused kernel quantises activations on chip (x 16-byte aligned);
     with x only 4-byte aligned the standalone preparation kernel writes the
     records and the same fused kernel reads them.  Both plans are identical
     at this shape, so equal outputs, bit for bit, mean equal records."""
+    tuning.set("NSQ_TC_MIN_M", "17")  # the fused kernel for M = 3 too
     n, k = 256, 1024
     w = eng.upload(Q.synthetic_weights(n, k, Q4_K, seed=12))
     x = torch.from_numpy(_adversarial_activations(m, k, seed=13)).to(eng.device)
