@@ -119,6 +119,15 @@ int nsq_dequant(const void *w, int ggml_type, int q6k_layout, int out_dtype, voi
  * nsq_gemv_workspace_size bytes, 16-byte aligned, which may be NULL when
  * not needed); the GEMV accumulates exact integer dot products per 16 or 32
  * weights and combines them in fp32.
+ *
+ * For 9..16 tokens over Q4_K and ggml-layout Q6_K (K % 256 == 0) the GEMV
+ * runs on the tcgen05 tensor cores: the 6-bit sub-scales folded into fp16
+ * weight operands (exact products), x as fp16 hi + lo parts (22 bits), fp32
+ * accumulation, one fp32 epilogue per 256 weights.  Its workspace (fp16
+ * activation tiles and split-tile partial sums, about 21 KB per 256 of K
+ * plus 4 MiB) is what nsq_gemv_workspace_size returns for M >= 2; with a
+ * workspace of only the M * K / 32 * 80 bytes of prepared activations the
+ * other kernels run instead.
  */
 size_t nsq_gemv_workspace_size(int64_t M, int64_t K);
 int nsq_gemv(const void *w, int ggml_type, int q6k_layout, const float *x, float *y, int64_t M,

@@ -197,9 +197,16 @@ int nsq_dequant(const void* w, int ggml_type, int q6k_layout, int out_dtype, voi
   return e == cudaSuccess ? NSQ_OK : NSQ_ERR_CUDA;
 }
 
+// Bytes of the prepared activation records alone (every path but the
+// tensor-core one needs only these).
+static size_t records_bytes(int64_t M, int64_t K) {
+  if (M <= 0 || K <= 0 || K % 32) return 0;
+  return (size_t)(M * (K / 32)) * sizeof(XGroup);
+}
+
 size_t nsq_gemv_workspace_size(int64_t M, int64_t K) {
   if (M <= 0 || K <= 0 || K % 32) return 0;
-  const size_t rec = (size_t)(M * (K / 32)) * sizeof(XGroup);
+  const size_t rec = records_bytes(M, K);
   // 2..16 tokens over K-quants run on the tensor cores: fp16 activation
   // tiles, min-term tiles and split-tile partial sums
   if (M >= 2 && M <= NSQ_GEMV_MAX_M && K % 256 == 0) {
@@ -215,7 +222,7 @@ int nsq_prepare_activations(const float* x, int64_t M, int64_t K, void* workspac
   if (!x || !workspace) return x ? NSQ_ERR_WORKSPACE : NSQ_ERR_NULL;
   if (reinterpret_cast<uintptr_t>(x) & 3) return NSQ_ERR_ALIGN;
   if (reinterpret_cast<uintptr_t>(workspace) & 15) return NSQ_ERR_ALIGN;
-  if (workspace_bytes < nsq_gemv_workspace_size(M, K)) return NSQ_ERR_WORKSPACE;
+  if (workspace_bytes < records_bytes(M, K)) return NSQ_ERR_WORKSPACE;
   DevInfo di;
   int rc = check_device(di);
   if (rc) return rc;
@@ -262,11 +269,10 @@ int nsq_gemv_multi(const nsq_segment* segs, int nseg, const float* x, int64_t M,
     // through the workspace
     if (reinterpret_cast<uintptr_t>(x) & 3) return NSQ_ERR_ALIGN;
   }
-  if (!gemv_force_general() && M >= tc_min_m() && tc_covers(segs, nseg, M, K)) {
-    // 2..16 tokens over Q4_K / ggml Q6_K: tcgen05 tensor cores (gemv_tc.cu)
-    if (!workspace) return NSQ_ERR_WORKSPACE;
-    if (reinterpret_cast<uintptr_t>(workspace) & 15) return NSQ_ERR_ALIGN;
-    if (workspace_bytes < nsq_gemv_workspace_size(M, K)) return NSQ_ERR_WORKSPACE;
+  if (!gemv_force_general() && M >= tc_min_m() && tc_covers(segs, nseg, M, K) && workspace &&
+      !(reinterpret_cast<uintptr_t>(workspace) & 15) && workspace_bytes >= tc_workspace_bytes(K)) {
+    // 2..16 tokens over Q4_K / ggml Q6_K: tcgen05 tensor cores (gemv_tc.cu),
+    // when the workspace holds its tiles (nsq_gemv_workspace_size sizes it so)
     DevInfo di;
     if ((rc = check_device(di))) return rc;
     rc = run_gemv_tc(segs, nseg, x, M, K, workspace, static_cast<cudaStream_t>(stream), di.num_sms);
@@ -278,7 +284,7 @@ int nsq_gemv_multi(const nsq_segment* segs, int nseg, const float* x, int64_t M,
   if (!self) {
     if (!workspace) return NSQ_ERR_WORKSPACE;
     if (reinterpret_cast<uintptr_t>(workspace) & 15) return NSQ_ERR_ALIGN;
-    if (workspace_bytes < nsq_gemv_workspace_size(M, K)) return NSQ_ERR_WORKSPACE;
+    if (workspace_bytes < records_bytes(M, K)) return NSQ_ERR_WORKSPACE;
   }
   DevInfo di;
   if ((rc = check_device(di))) return rc;
@@ -288,7 +294,7 @@ int nsq_gemv_multi(const nsq_segment* segs, int nseg, const float* x, int64_t M,
     if (rc != -1) return rc;
     // not covered on chip after all: go through the workspace
     if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 15) ||
-        workspace_bytes < nsq_gemv_workspace_size(M, K))
+        workspace_bytes < records_bytes(M, K))
       return NSQ_ERR_WORKSPACE;
   }
   if (launch_prepare_x(x, static_cast<XGroup*>(workspace), M, K, st, di.num_sms) != cudaSuccess) return NSQ_ERR_CUDA;
@@ -319,7 +325,7 @@ static int gemv_epilogue(const nsq_segment* segs, int nseg, const float* x, int6
   if (!self) {
     if (!workspace) return NSQ_ERR_WORKSPACE;
     if (reinterpret_cast<uintptr_t>(workspace) & 15) return NSQ_ERR_ALIGN;
-    if (workspace_bytes < nsq_gemv_workspace_size(M, K)) return NSQ_ERR_WORKSPACE;
+    if (workspace_bytes < records_bytes(M, K)) return NSQ_ERR_WORKSPACE;
   }
   DevInfo di;
   int rc;
@@ -405,7 +411,7 @@ int nsq_gemv_multi_xchg(const nsq_xsegment* segs, int nseg, const float* x, int6
   if (!self) {
     if (!workspace) return NSQ_ERR_WORKSPACE;
     if (reinterpret_cast<uintptr_t>(workspace) & 15) return NSQ_ERR_ALIGN;
-    if (workspace_bytes < nsq_gemv_workspace_size(M, K)) return NSQ_ERR_WORKSPACE;
+    if (workspace_bytes < records_bytes(M, K)) return NSQ_ERR_WORKSPACE;
   }
   DevInfo di;
   if ((rc = check_device(di))) return rc;

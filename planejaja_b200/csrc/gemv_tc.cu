@@ -16,7 +16,9 @@
 // 2^-12 on those weights).  x enters as two fp16 operands, hi = fp16(x') and
 // lo = fp16(x' - hi), where x' = x * 2^-e_{m,s} with one power of two per
 // token and super-block chosen so that |x'| < 2^15: hi + lo carries 22 bits.
-// The tensor cores accumulate D = sum A (hi + lo) in fp32 (TMEM); the min
+// One MMA with N = 32 takes both (the hi and lo tiles are adjacent rows of
+// one operand); the epilogue adds the two halves of D.  The tensor cores
+// accumulate in fp32 (TMEM); the min
 // term sum_j m_j T_j (T_j = the sub-block sums of x') is a second MMA with
 // K = 8 (padded to 16) into D2.  Per super-block the epilogue adds
 //   y += 2^e * (d * D - 32 * dmin * D2)           (T enters as T / 32)
@@ -59,10 +61,11 @@ constexpr int TC_A_BYTES = TC_BM * 128;      // fp16 [128 x 64], 16 KB
 constexpr int TC_B_BYTES = 2 * TC_BN * 128;  // fp16 hi [16 x 64] + lo [16 x 64], 4 KB
 constexpr int TC_COL_BYTES = 5120;           // workspace stride: B2 hi + lo (4 KB), 16 token scales, pad
 constexpr int TC_B2_BYTES = 4096;            // min-term tile (hi + lo) in shared memory
-constexpr int TC_NACC = 8;                   // units in flight between the MMA and the epilogue
+constexpr int TC_NACC = 4;                   // units in flight between the MMA and the epilogue
+constexpr int TC_ACC_COLS = 64;              // per unit: D (hi | lo, 32 columns) and the min-term D2
 constexpr int TC_SCL_STAGES = 16;            // token scales (64 B per unit)
 constexpr int TC_GMAX = 256;                 // most CTAs a launch uses
-constexpr int TC_TMEM_COLS = 32 * TC_NACC;   // D and D2 (16 columns each) per unit in flight
+constexpr int TC_TMEM_COLS = TC_NACC * TC_ACC_COLS;
 constexpr int TC_SMEM_LIMIT = 232448;
 
 enum : int { kTcQ4K = 0, kTcQ6KG = 1, kTcMixed = -1 };
@@ -81,7 +84,7 @@ struct TcParams {
   int nseg, T, NSB, M;
   int64_t U;        // units = T * NSB
   int pitch;        // raw bytes per row per unit in shared memory
-  int raw_stages, a_stages, col_stages;
+  int raw_stages, a_stages, b_stages, col_stages;
   const uint8_t* ws_b;    // [NSB * 4][hi 2 KB | lo 2 KB]
   const uint8_t* ws_col;  // [NSB][B2 hi 2 KB | B2 lo 2 KB | 16 f32 scales | pad]
   float* ws_part;         // [2 * TC_GMAX][128 rows][16 tokens]
@@ -258,20 +261,23 @@ template <int CODE>
 __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_constant__ TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int AS = p.a_stages, CS = p.col_stages, RS = p.raw_stages, PITCH = p.pitch;
-  // 1024-aligned swizzled tiles first: A and B stages, the two min-term A
-  // tiles (4 unit slots each, 16 K columns per slot), the min-term B tiles
+  const int AS = p.a_stages, BS = p.b_stages, CS = p.col_stages, RS = p.raw_stages, PITCH = p.pitch;
+  // 1024-aligned swizzled tiles first: A stages, B stages (their own, deeper
+  // ring: x tiles come from the L2 and are prefetched several units ahead),
+  // the min-term A tile (4 unit slots, 16 K columns each), min-term B tiles
   uint8_t* a_sm = smem;
   uint8_t* b_sm = a_sm + AS * TC_A_BYTES;
-  uint8_t* a2_sm = b_sm + AS * TC_B_BYTES;
-  uint8_t* col_sm = a2_sm + 2 * TC_A_BYTES;
+  uint8_t* a2_sm = b_sm + BS * TC_B_BYTES;
+  uint8_t* col_sm = a2_sm + TC_A_BYTES;
   float* scl_sm = reinterpret_cast<float*>(col_sm + CS * TC_B2_BYTES);     // [16][16]
   float2* dsc = reinterpret_cast<float2*>(scl_sm + TC_SCL_STAGES * TC_BN);  // [8][128] (d, 32 dmin)
   uint8_t* raw_sm = reinterpret_cast<uint8_t*>(dsc + TC_NACC * TC_BM);
   const uint32_t RAW_BYTES = (uint32_t)(TC_BM * PITCH);
   uint64_t* full = reinterpret_cast<uint64_t*>(raw_sm + RS * RAW_BYTES);
   uint64_t* empty = full + AS;
-  uint64_t* col_full = empty + AS;
+  uint64_t* bfull = empty + AS;
+  uint64_t* bempty = bfull + BS;
+  uint64_t* col_full = bempty + BS;
   uint64_t* col_empty = col_full + CS;
   uint64_t* scl_full = col_empty + CS;
   uint64_t* scl_empty = scl_full + TC_SCL_STAGES;
@@ -292,8 +298,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < AS; ++s) {
-      mbar_init(&full[s], 1 + TC_DQ_WARPS);
+      mbar_init(&full[s], TC_DQ_WARPS);
       mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < BS; ++s) {
+      mbar_init(&bfull[s], 1);
+      mbar_init(&bempty[s], 1);
     }
     for (int s = 0; s < CS; ++s) {
       mbar_init(&col_full[s], 1);
@@ -359,18 +369,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
   } else if (warp == 1) {
     // ---- MMA issue
     if (lane == 0) {
-      constexpr uint32_t IDESC = umma_idesc_f16(TC_BM, TC_BN);
+      // N = 32: the hi and lo x tiles are adjacent 16-row tiles, one operand
+      constexpr uint32_t IDESC = umma_idesc_f16(TC_BM, 2 * TC_BN);
       const uint32_t a_base = smem_u32(a_sm), b_base = smem_u32(b_sm), a2_base = smem_u32(a2_sm);
       const uint32_t col_base = smem_u32(col_sm);
       bool ok = true;
       for (int n = 0; n < nunits && ok; ++n) {
         const int a = n % TC_NACC;
-        const uint32_t dD = tmem + (uint32_t)(32 * a), dD2 = dD + 16;
+        const uint32_t dD = tmem + (uint32_t)(TC_ACC_COLS * a), dD2 = dD + 32;
         if (!mbar_wait_bounded(&acc_empty[a], ph(n, TC_NACC) ^ 1)) break;
         tc_fence_after();
         for (int q = 0; q < 4; ++q) {
-          const int k = 4 * n + q, s = k % AS;
-          if (!mbar_wait_bounded(&full[s], ph(k, AS))) {
+          const int k = 4 * n + q, s = k % AS, sb = k % BS;
+          if (!mbar_wait_bounded(&full[s], ph(k, AS)) || !mbar_wait_bounded(&bfull[sb], ph(k, BS))) {
             ok = false;
             break;
           }
@@ -378,21 +389,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             const uint64_t ad = umma_desc_sw128(a_base + s * TC_A_BYTES + kk * 32);
-            const uint64_t bh = umma_desc_sw128(b_base + s * TC_B_BYTES + kk * 32);
-            const uint64_t bl = umma_desc_sw128(b_base + s * TC_B_BYTES + TC_B_BYTES / 2 + kk * 32);
-            tc_mma_bf16(dD, ad, bh, IDESC, (q | kk) ? 1u : 0u);
-            tc_mma_bf16(dD, ad, bl, IDESC, 1u);
+            const uint64_t bd = umma_desc_sw128(b_base + sb * TC_B_BYTES + kk * 32);
+            tc_mma_bf16(dD, ad, bd, IDESC, (q | kk) ? 1u : 0u);
           }
           tc_commit(&empty[s]);
+          tc_commit(&bempty[sb]);
         }
         if (!ok) break;
         const int cs = n % CS;
         if (!mbar_wait_bounded(&col_full[cs], ph(n, CS)) || !mbar_wait_bounded(&a2_full[a], ph(n, TC_NACC))) break;
         tc_fence_after();
         // min-term A slot a: tile a / 4, K columns 16 (a % 4) .. +16
-        const uint64_t a2d = umma_desc_sw128(a2_base + (a >> 2) * TC_A_BYTES + (a & 3) * 32);
+        const uint64_t a2d = umma_desc_sw128(a2_base + a * 32);
         tc_mma_bf16(dD2, a2d, umma_desc_sw128(col_base + cs * TC_B2_BYTES), IDESC, 0u);
-        tc_mma_bf16(dD2, a2d, umma_desc_sw128(col_base + cs * TC_B2_BYTES + TC_B2_BYTES / 2), IDESC, 1u);
         tc_commit(&col_empty[cs]);
         tc_commit(&acc_full[a]);
       }
@@ -408,13 +417,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
         locate(n, sg, tl, c);
         bool ok = true;
         for (int q = 0; q < 4; ++q) {
-          const int k = 4 * n + q, s = k % AS;
-          if (!mbar_wait_bounded(&empty[s], ph(k, AS) ^ 1)) {
+          const int k = 4 * n + q, sb = k % BS;
+          if (!mbar_wait_bounded(&bempty[sb], ph(k, BS) ^ 1)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[s], TC_B_BYTES);
-          bulk_g2s_hint(b_sm + s * TC_B_BYTES, p.ws_b + (int64_t)(4 * c + q) * TC_B_BYTES, TC_B_BYTES, &full[s], pol);
+          mbar_arrive_expect_tx(&bfull[sb], TC_B_BYTES);
+          bulk_g2s_hint(b_sm + sb * TC_B_BYTES, p.ws_b + (int64_t)(4 * c + q) * TC_B_BYTES, TC_B_BYTES, &bfull[sb],
+                        pol);
         }
         if (!ok) break;
         const int cs = n % CS, ss = n % TC_SCL_STAGES;
@@ -445,8 +455,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
       const uint8_t* raw = raw_sm + rs * RAW_BYTES + row * PITCH + off16;
       // per-unit row data: d / dmin for the epilogue, mins for the min-term MMA
       if (!mbar_wait_bounded(&a2_empty[a], ph(n, TC_NACC) ^ 1)) break;
-      uint8_t* a2row = a2_sm + (a >> 2) * TC_A_BYTES + row * 128;
-      const int a2c = 2 * (a & 3);  // 16-byte chunks of this slot's 16 K columns
+      uint8_t* a2row = a2_sm + row * 128;
+      const int a2c = 2 * a;  // 16-byte chunks of this slot's 16 K columns
       uint32_t S0 = 0, S1 = 0, S2 = 0;
       if (code == kTcQ4K) {
         const uint4 hdr = *reinterpret_cast<const uint4*>(raw);
@@ -527,19 +537,27 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
              mbar_wait_bounded(&scl_full[ss], ph(n, TC_SCL_STAGES));
       if (ok) {
         tc_fence_after();
-        uint32_t D[16], D2[16];
-        const uint32_t taddr = tmem + ((uint32_t)(32 * qd) << 16) + (uint32_t)(32 * a);
-        tc_ld_32x32b_x16(taddr, D);
-        tc_ld_32x32b_x16(taddr + 16, D2);
-        tc_wait_ld();
+        // D and D2, each as hi | lo halves of 16 columns
+        float dsum[TC_BN], d2sum[TC_BN];
+        const uint32_t taddr = tmem + ((uint32_t)(32 * qd) << 16) + (uint32_t)(TC_ACC_COLS * a);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t v[32];
+          tc_ld_32x32b_x32(taddr + 32 * h, v);
+#pragma unroll
+          for (int t = 0; t < TC_BN; ++t) {
+            const float x = __uint_as_float(v[t]) + __uint_as_float(v[t + 16]);
+            if (h == 0) dsum[t] = x;
+            else d2sum[t] = x;
+          }
+        }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[a]);
         const float2 dd = dsc[a * TC_BM + row];
         const float* sct = scl_sm + ss * TC_BN;
 #pragma unroll
-        for (int t = 0; t < TC_BN; ++t)
-          acc[t] = fmaf(sct[t], fmaf(dd.x, __uint_as_float(D[t]), -dd.y * __uint_as_float(D2[t])), acc[t]);
+        for (int t = 0; t < TC_BN; ++t) acc[t] = fmaf(sct[t], fmaf(dd.x, dsum[t], -dd.y * d2sum[t]), acc[t]);
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&a2_empty[a]);
@@ -717,17 +735,21 @@ int run_gemv_tc(const nsq_segment* segs, int nseg, const float* x, int64_t M, in
   p.ws_b = ws + 1024;
   p.ws_col = p.ws_b + (size_t)NSB * 4 * TC_B_BYTES;
   p.ws_part = reinterpret_cast<float*>(const_cast<uint8_t*>(p.ws_col) + (size_t)NSB * TC_COL_BYTES);
-  // shared memory: 4 A/B stages and 3 min-term stages, the raw ring takes
-  // what is left (up to 4 units)
+  // shared memory: 4 A stages, up to 12 B stages (3 units of x ahead), 3
+  // min-term stages; the raw ring takes what is left (3 or 4 units)
   const int as = 4, cs = 3;
-  const size_t fixed = 1024 + (size_t)as * (TC_A_BYTES + TC_B_BYTES) + 2 * TC_A_BYTES + (size_t)cs * TC_B2_BYTES +
-                       (size_t)TC_SCL_STAGES * TC_BN * 4 + (size_t)TC_NACC * TC_BM * 8 + 1024;
-  int rs = 4;
-  while (rs > 2 && fixed + (size_t)rs * TC_BM * pitch > (size_t)TC_SMEM_LIMIT) --rs;
-  const size_t smem = fixed + (size_t)rs * TC_BM * pitch;
+  int bs = 12, rs = 4;
+  auto smem_of = [&](int b, int r) {
+    return 1024 + (size_t)as * TC_A_BYTES + (size_t)b * TC_B_BYTES + TC_A_BYTES + (size_t)cs * TC_B2_BYTES +
+           (size_t)TC_SCL_STAGES * TC_BN * 4 + (size_t)TC_NACC * TC_BM * 8 + 1024 + (size_t)r * TC_BM * pitch;
+  };
+  while (smem_of(bs, rs) > (size_t)TC_SMEM_LIMIT && rs > 3) --rs;
+  while (smem_of(bs, rs) > (size_t)TC_SMEM_LIMIT && bs > 4) bs -= 4;
+  const size_t smem = smem_of(bs, rs);
   if (smem > (size_t)TC_SMEM_LIMIT) return -1;
   p.raw_stages = rs;
   p.a_stages = as;
+  p.b_stages = bs;
   p.col_stages = cs;
   int G = num_sms > 0 ? num_sms : 148;
   if (G > TC_GMAX) G = TC_GMAX;
