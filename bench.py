@@ -636,6 +636,53 @@ def prefill_records(ctx, bf16_peak, peak_kind, shapes=PREFILL_SHAPES, ms_list=PR
     return out
 
 
+# Single-kernel cases for profilers (bench.py --case NAME): a few launches of
+# one kernel on one GPU, nothing timed.  (weights, ggml type, layout, N, K, M, kind)
+CASES = {
+    "gemv_gate_up_m1": ("2 x [14336 x 4096] Q4_K (Llama-3-8B gate|up)", 12, 0, 14336, 4096, 1, "gemv2"),
+    "gemv_down_m1": ("[4096 x 14336] Q6_K (Llama-3-8B down)", 14, 0, 4096, 14336, 1, "gemv"),
+    "gemv_down_nodestor_m1": ("[4096 x 14336] Q6_K NODESTOR layout", 14, 1, 4096, 14336, 1, "gemv"),
+    "gemv_tc_70b_gate_up_m16": ("2 x [28672 x 8192] Q4_K at M = 16, tcgen05", 12, 0, 28672, 8192, 16, "gemv2"),
+    "gemv_mma_70b_gate_up_m16": ("2 x [28672 x 8192] Q4_K at M = 16, mma.sync", 12, 0, 28672, 8192, 16, "gemv2_mma"),
+    "gemm_q4k_m128": ("Q4_K [14336 x 4096], M = 128", 12, 0, 14336, 4096, 128, "gemm"),
+    "gemm_q4k_m2048": ("Q4_K [14336 x 4096], M = 2048", 12, 0, 14336, 4096, 2048, "gemm"),
+    "gemm_q6k_m512": ("Q6_K [4096 x 14336], M = 512", 14, 0, 4096, 14336, 512, "gemm"),
+}
+
+
+def run_case(name, reps):
+    """Launches one case `reps` times (after one warm-up launch) on cuda:0."""
+    import torch
+    from planejaja_b200 import _lib
+    from planejaja_b200 import quantize as Q
+    from planejaja_b200.engine import CudaEngine
+    desc, t, lay, n, k, m, kind = CASES[name]
+    eng = CudaEngine(0)
+    if kind == "gemv2_mma":  # the mma.sync kernel: switch the tcgen05 path off
+        os.environ["NSQ_TC_MIN_M"] = "17"
+        eng.lib.nsq_reload_tuning()
+    w = eng.upload(Q.synthetic_weights(n, k, t, seed=SEED_W, q6k_layout=lay))
+    w2 = w.clone() if kind.startswith("gemv2") else None
+    for i in range(reps + 1):
+        if kind == "gemm":
+            x = torch.randn(m, k, device="cuda").to(torch.bfloat16) if i == 0 else x
+            eng.gemm_bf16(w, t, x, n, k, lay)
+        else:
+            x = torch.from_numpy(host_acts_like(m, k)).cuda() if i == 0 else x
+            if w2 is not None:
+                eng.gemv_multi([(w, t, n, lay), (w2, t, n, lay)], x, k)
+            else:
+                eng.gemv(w, t, x, n, k, lay)
+    torch.cuda.synchronize()
+    assert eng.device_status() == 0
+    print(f"case {name}: {desc}, {reps + 1} launches", flush=True)
+
+
+def host_acts_like(m, k):
+    from planejaja_b200 import quantize as Q
+    return Q.synthetic_activations(m, k, seed=SEED_X)
+
+
 def run_gpu(args, rank, world, local_rank):
     import torch
     from planejaja_b200.formats import fmt
@@ -769,6 +816,9 @@ def main():
     ap.add_argument("--cpu-reps", type=int, default=1)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-frac", type=float, default=0.25)
+    ap.add_argument("--case", choices=sorted(CASES), default=None,
+                    help="run only this single-kernel case a few times (for profilers), print nothing else")
+    ap.add_argument("--case-reps", type=int, default=2)
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
                     help="tensor-parallel all-gather: fused into the GEMV (p2p) or NCCL all_gather")
     args = ap.parse_args()
@@ -778,6 +828,9 @@ def main():
     if args.layers is None:
         args.layers = WORKLOADS[args.workload]["layers"]
 
+    if args.case:
+        run_case(args.case, args.case_reps)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
