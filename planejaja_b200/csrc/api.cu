@@ -23,6 +23,7 @@ int run_gemv_fused(const nsq_segment* segs, int nseg, const float* x, const XGro
                    const float* const* res = nullptr);
 bool fused_covers(const nsq_segment* segs, int nseg, int64_t K);
 bool fused_self_prepare_fits(int64_t M, int64_t K);
+bool fused_self_prepare_preferred(int64_t M, int64_t K);
 bool gemv_force_general();
 int run_gemv_mma(const nsq_segment* segs, int nseg, const XGroup* xg, int64_t M, int64_t K, cudaStream_t st,
                  int num_sms, const XchgDesc* xd);
@@ -204,6 +205,16 @@ static size_t records_bytes(int64_t M, int64_t K) {
   return (size_t)(M * (K / 32)) * sizeof(XGroup);
 }
 
+// The fused kernel prepares the activations on chip when they fit there and
+// x is 16-byte aligned, unless the separate preparation kernel is the faster
+// choice and the workspace can hold its records.
+static bool use_self_prepare(int64_t M, int64_t K, const float* x, const void* ws, size_t ws_bytes) {
+  if (!fused_self_prepare_fits(M, K) || (reinterpret_cast<uintptr_t>(x) & 15)) return false;
+  if (fused_self_prepare_preferred(M, K)) return true;
+  const bool ws_ok = ws && !(reinterpret_cast<uintptr_t>(ws) & 15) && ws_bytes >= records_bytes(M, K);
+  return !ws_ok;
+}
+
 size_t nsq_gemv_workspace_size(int64_t M, int64_t K) {
   if (M <= 0 || K <= 0 || K % 32) return 0;
   const size_t rec = records_bytes(M, K);
@@ -280,7 +291,7 @@ int nsq_gemv_multi(const nsq_segment* segs, int nseg, const float* x, int64_t M,
   }
   const bool mma = !gemv_force_general() && M >= gemv_mma_min_m() && gemv_mma_covers(segs, nseg, M, K);
   const bool fused = !gemv_force_general() && fused_covers(segs, nseg, K);
-  const bool self = !mma && fused && fused_self_prepare_fits(M, K) && !(reinterpret_cast<uintptr_t>(x) & 15);
+  const bool self = !mma && fused && use_self_prepare(M, K, x, workspace, workspace_bytes);
   if (!self) {
     if (!workspace) return NSQ_ERR_WORKSPACE;
     if (reinterpret_cast<uintptr_t>(workspace) & 15) return NSQ_ERR_ALIGN;
@@ -321,7 +332,7 @@ static int gemv_epilogue(const nsq_segment* segs, int nseg, const float* x, int6
   if (!x) return NSQ_ERR_NULL;
   if (reinterpret_cast<uintptr_t>(x) & 3) return NSQ_ERR_ALIGN;
   if (!fused_covers(segs, nseg, K)) return NSQ_ERR_SHAPE;
-  const bool self = fused_self_prepare_fits(M, K) && !(reinterpret_cast<uintptr_t>(x) & 15);
+  const bool self = use_self_prepare(M, K, x, workspace, workspace_bytes);
   if (!self) {
     if (!workspace) return NSQ_ERR_WORKSPACE;
     if (reinterpret_cast<uintptr_t>(workspace) & 15) return NSQ_ERR_ALIGN;
@@ -407,7 +418,7 @@ int nsq_gemv_multi_xchg(const nsq_xsegment* segs, int nseg, const float* x, int6
   }
   const bool mma = M >= gemv_mma_min_m() && gemv_mma_covers(sl, nseg, M, K);
   if (!mma && !fused_covers(sl, nseg, K)) return NSQ_ERR_SHAPE;
-  const bool self = !mma && fused_self_prepare_fits(M, K) && !(reinterpret_cast<uintptr_t>(x) & 15);
+  const bool self = !mma && use_self_prepare(M, K, x, workspace, workspace_bytes);
   if (!self) {
     if (!workspace) return NSQ_ERR_WORKSPACE;
     if (reinterpret_cast<uintptr_t>(workspace) & 15) return NSQ_ERR_ALIGN;

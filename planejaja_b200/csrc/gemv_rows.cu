@@ -159,6 +159,19 @@ static cudaError_t launch_fused_e(int epi, int M, const FusedParams& p, bool xse
 // True if the fused kernel can prepare the activations of M tokens on chip.
 bool fused_self_prepare_fits(int64_t M, int64_t K) { return M <= 4 && M * (K / 32) * 80 <= kXSelfMaxBytes; }
 
+// True if preparing the activations on chip is also the faster choice.  One
+// token is quantised one group of 32 per consumer thread; when a CTA (or CTA
+// pair, K >= 8192) has more groups than threads, the rounds delay every
+// consumer and the separate one-warp-per-group kernel is faster (B200, M = 1:
+// Llama-3-8B decode step 1.556 against 1.612 ms with its K = 14336 `down`
+// launch prepared separately, Llama-2-7B 1.281 against 1.329 ms with
+// K = 11008; every K = 4096 launch prepared separately: 1.706 ms).
+bool fused_self_prepare_preferred(int64_t M, int64_t K) {
+  if (M > 1) return true;  // M = 4, K = 4096: 3.80 on chip against 3.87 ms separately
+  const int64_t C = K >= 8192 ? 2 : 1;
+  return K / 32 <= C * kRowsConsumers * 32;
+}
+
 // Fused decode GEMV.  xg == nullptr: activations are prepared on chip from x
 // (requires fused_self_prepare_fits); otherwise xg holds prepared records.
 // Returns NSQ_OK / an error, or -1 if a shape is not covered.

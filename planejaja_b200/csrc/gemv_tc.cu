@@ -32,7 +32,10 @@
 // Warp roles (512 threads, one CTA per SM):
 //   warp 0      raw producer: one 2-D TMA box [128 rows x one super-block
 //               column] of the GGUF bytes per unit (evict-first in L2)
-//   warp 1      TMEM owner; one thread issues the MMAs
+//   warps 1, 3  MMA issue, one thread each, alternate units (warp 1 owns
+//               TMEM).  A thread that issues, commits and waits in turn
+//               keeps the tensor pipe busy less than half the time; two
+//               issuers overlap each other's waits
 //   warp 2      B producer: x tiles (hi, lo) per 64-wide K stage, and per
 //               unit the min-term tile and the token scales, from the
 //               workspace the preparation kernel wrote
@@ -62,6 +65,7 @@ constexpr int TC_B_BYTES = 2 * TC_BN * 128;  // fp16 hi [16 x 64] + lo [16 x 64]
 constexpr int TC_COL_BYTES = 5120;           // workspace stride: B2 hi + lo (4 KB), 16 token scales, pad
 constexpr int TC_B2_BYTES = 4096;            // min-term tile (hi + lo) in shared memory
 constexpr int TC_NACC = 4;                   // units in flight between the MMA and the epilogue
+constexpr int TC_MMA_WARPS = 2;              // MMA issuers (warps 1 and 3): unit n -> issuer n % 2
 constexpr int TC_ACC_COLS = 64;              // per unit: D (hi | lo, 32 columns) and the min-term D2
 constexpr int TC_SCL_STAGES = 16;            // token scales (64 B per unit)
 constexpr int TC_GMAX = 256;                 // most CTAs a launch uses
@@ -273,12 +277,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
   float2* dsc = reinterpret_cast<float2*>(scl_sm + TC_SCL_STAGES * TC_BN);  // [8][128] (d, 32 dmin)
   uint8_t* raw_sm = reinterpret_cast<uint8_t*>(dsc + TC_NACC * TC_BM);
   const uint32_t RAW_BYTES = (uint32_t)(TC_BM * PITCH);
-  uint64_t* full = reinterpret_cast<uint64_t*>(raw_sm + RS * RAW_BYTES);
-  uint64_t* empty = full + AS;
-  uint64_t* bfull = empty + AS;
-  uint64_t* bempty = bfull + BS;
-  uint64_t* col_full = bempty + BS;
-  uint64_t* col_empty = col_full + CS;
+  // The rings' "full" barriers come one set per MMA issuer (unit n fills
+  // set n % 2), their "empty" barriers are shared: a slot's data is used by
+  // both issuers in turn, but each full barrier only by one, in order, so a
+  // parity wait never sees a phase two ahead of the one it waits for.
+  uint64_t* full = reinterpret_cast<uint64_t*>(raw_sm + RS * RAW_BYTES);  // [issuer][AS]
+  uint64_t* empty = full + TC_MMA_WARPS * AS;
+  uint64_t* bfull = empty + AS;                                           // [issuer][BS]
+  uint64_t* bempty = bfull + TC_MMA_WARPS * BS;
+  uint64_t* col_full = bempty + BS;                                       // [issuer][CS]
+  uint64_t* col_empty = col_full + TC_MMA_WARPS * CS;
   uint64_t* scl_full = col_empty + CS;
   uint64_t* scl_empty = scl_full + TC_SCL_STAGES;
   uint64_t* a2_full = scl_empty + TC_SCL_STAGES;
@@ -297,18 +305,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
   const int nunits = (int)(u1 - u0);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < AS; ++s) {
-      mbar_init(&full[s], TC_DQ_WARPS);
-      mbar_init(&empty[s], 1);
-    }
-    for (int s = 0; s < BS; ++s) {
-      mbar_init(&bfull[s], 1);
-      mbar_init(&bempty[s], 1);
-    }
-    for (int s = 0; s < CS; ++s) {
-      mbar_init(&col_full[s], 1);
-      mbar_init(&col_empty[s], 1);
-    }
+    for (int s = 0; s < AS; ++s) mbar_init(&empty[s], 1);
+    for (int s = 0; s < TC_MMA_WARPS * AS; ++s) mbar_init(&full[s], TC_DQ_WARPS);
+    for (int s = 0; s < BS; ++s) mbar_init(&bempty[s], 1);
+    for (int s = 0; s < TC_MMA_WARPS * BS; ++s) mbar_init(&bfull[s], 1);
+    for (int s = 0; s < CS; ++s) mbar_init(&col_empty[s], 1);
+    for (int s = 0; s < TC_MMA_WARPS * CS; ++s) mbar_init(&col_full[s], 1);
     for (int s = 0; s < TC_SCL_STAGES; ++s) {
       mbar_init(&scl_full[s], 1);
       mbar_init(&scl_empty[s], 4);
@@ -323,7 +325,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
       mbar_init(&raw_full[s], 1);
       mbar_init(&raw_empty[s], TC_DQ_WARPS);
     }
-    mbar_init(done, 1);
+    mbar_init(done, TC_MMA_WARPS);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -346,6 +348,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
   };
   // parity of the k-th use of a ring slot: full waits (k / R) & 1, empty waits its complement
   auto ph = [](int k, int R) { return (uint32_t)((k / R) & 1); };
+  // parity of an issuer's own full barrier: use k (per uses per unit) of a
+  // ring of R slots.  Slot uses j = k / R come from units j*r .. (r = R /
+  // per units per turn of the ring); for odd r they alternate between the
+  // issuers, so an issuer sees every other one.
+  auto iph = [](int k, int R, int per) {
+    const int j = k / R, r = R / per;
+    return (uint32_t)((((r & 1) ? (j >> 1) : j)) & 1);
+  };
 
   if (warp == 0) {
     // ---- raw producer: the unit's GGUF column for the tile's 128 rows
@@ -366,22 +376,27 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
             : "memory");
       }
     }
-  } else if (warp == 1) {
-    // ---- MMA issue
+  } else if (warp == 1 || warp == 3) {
+    // ---- MMA issue: issuer i takes units i, i + 2, ... (accumulators a = n % 4
+    // alternate between the issuers)
     if (lane == 0) {
+      const int issuer = warp == 1 ? 0 : 1;
+      uint64_t* my_full = full + issuer * AS;
+      uint64_t* my_bfull = bfull + issuer * BS;
+      uint64_t* my_col_full = col_full + issuer * CS;
       // N = 32: the hi and lo x tiles are adjacent 16-row tiles, one operand
       constexpr uint32_t IDESC = umma_idesc_f16(TC_BM, 2 * TC_BN);
       const uint32_t a_base = smem_u32(a_sm), b_base = smem_u32(b_sm), a2_base = smem_u32(a2_sm);
       const uint32_t col_base = smem_u32(col_sm);
       bool ok = true;
-      for (int n = 0; n < nunits && ok; ++n) {
+      for (int n = issuer; n < nunits && ok; n += TC_MMA_WARPS) {
         const int a = n % TC_NACC;
         const uint32_t dD = tmem + (uint32_t)(TC_ACC_COLS * a), dD2 = dD + 32;
         if (!mbar_wait_bounded(&acc_empty[a], ph(n, TC_NACC) ^ 1)) break;
         tc_fence_after();
         for (int q = 0; q < 4; ++q) {
           const int k = 4 * n + q, s = k % AS, sb = k % BS;
-          if (!mbar_wait_bounded(&full[s], ph(k, AS)) || !mbar_wait_bounded(&bfull[sb], ph(k, BS))) {
+          if (!mbar_wait_bounded(&my_full[s], iph(k, AS, 4)) || !mbar_wait_bounded(&my_bfull[sb], iph(k, BS, 4))) {
             ok = false;
             break;
           }
@@ -397,7 +412,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
         }
         if (!ok) break;
         const int cs = n % CS;
-        if (!mbar_wait_bounded(&col_full[cs], ph(n, CS)) || !mbar_wait_bounded(&a2_full[a], ph(n, TC_NACC))) break;
+        if (!mbar_wait_bounded(&my_col_full[cs], iph(n, CS, 1)) || !mbar_wait_bounded(&a2_full[a], ph(n, TC_NACC)))
+          break;
         tc_fence_after();
         // min-term A slot a: tile a / 4, K columns 16 (a % 4) .. +16
         const uint64_t a2d = umma_desc_sw128(a2_base + a * 32);
@@ -405,7 +421,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
         tc_commit(&col_empty[cs]);
         tc_commit(&acc_full[a]);
       }
-      tc_commit(done);  // every MMA issued above has completed when this arrives
+      tc_commit(done);  // every MMA this thread issued has completed when this arrives
     }
   } else if (warp == 2) {
     // ---- B producer: x tiles per K stage; per unit the min-term tile and the token scales
@@ -422,16 +438,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&bfull[sb], TC_B_BYTES);
-          bulk_g2s_hint(b_sm + sb * TC_B_BYTES, p.ws_b + (int64_t)(4 * c + q) * TC_B_BYTES, TC_B_BYTES, &bfull[sb],
-                        pol);
+          uint64_t* bf = &bfull[(n % TC_MMA_WARPS) * BS + sb];
+          mbar_arrive_expect_tx(bf, TC_B_BYTES);
+          bulk_g2s_hint(b_sm + sb * TC_B_BYTES, p.ws_b + (int64_t)(4 * c + q) * TC_B_BYTES, TC_B_BYTES, bf, pol);
         }
         if (!ok) break;
         const int cs = n % CS, ss = n % TC_SCL_STAGES;
         const uint8_t* col = p.ws_col + (int64_t)c * TC_COL_BYTES;
         if (!mbar_wait_bounded(&col_empty[cs], ph(n, CS) ^ 1)) break;
-        mbar_arrive_expect_tx(&col_full[cs], TC_B2_BYTES);
-        bulk_g2s_hint(col_sm + cs * TC_B2_BYTES, col, TC_B2_BYTES, &col_full[cs], pol);
+        uint64_t* cf = &col_full[(n % TC_MMA_WARPS) * CS + cs];
+        mbar_arrive_expect_tx(cf, TC_B2_BYTES);
+        bulk_g2s_hint(col_sm + cs * TC_B2_BYTES, col, TC_B2_BYTES, cf, pol);
         if (!mbar_wait_bounded(&scl_empty[ss], ph(n, TC_SCL_STAGES) ^ 1)) break;
         mbar_arrive_expect_tx(&scl_full[ss], TC_BN * 4);
         bulk_g2s_hint(scl_sm + ss * TC_BN, col + TC_B2_BYTES, TC_BN * 4, &scl_full[ss], pol);
@@ -510,7 +527,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
         *reinterpret_cast<uint4*>(dst + (((pp + 6) ^ sw) << 4)) = ch[3];
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&full[s]);
+        if (lane == 0) mbar_arrive(&full[(n % TC_MMA_WARPS) * AS + s]);
       }
       if (!ok) break;
       __syncwarp();
@@ -625,7 +642,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
-    // the final commit arrives once every MMA has completed
+    // both issuers' final commits arrive once every MMA has completed
     mbar_wait_bounded(done, 0);
     tc_fence_after();
     tmem_dealloc(tmem, TC_TMEM_COLS);

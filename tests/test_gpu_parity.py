@@ -190,6 +190,30 @@ def test_gemv_multi_workspace_mode(eng, oracle):
         assert rel_err(y.cpu().numpy(), oracle.quant_matmul(w, t, x, n, k, l, threads=8)) <= GEMV_TOL
 
 
+@pytest.mark.parametrize("tid,layout,k", [(Q4_K, 0, 14336), (Q6_K, Q6K_GGML, 14336), (Q6_K, Q6K_NODESTOR, 14336),
+                                          (Q4_0, 0, 11008), (Q5_K, Q6K_GGML, 8448)])
+def test_gemv_long_rows_with_and_without_workspace(eng, oracle, tuning, tid, layout, k):
+    """One token with long rows: given a workspace, the separate preparation
+    kernel writes the records; without one, the fused kernel quantises them on
+    chip (CTA pairs for K >= 8192).  Both against the oracle."""
+    tuning.set("NSQ_TC_MIN_M", "17")
+    lib = eng.lib
+    n = 200
+    w = Q.synthetic_weights(n, k, tid, seed=k + tid, q6k_layout=layout)
+    x = Q.synthetic_activations(1, k, seed=k)
+    ref = oracle.quant_matmul(w, tid, x, n, k, layout, threads=8)
+    wd, xd = eng.upload(w), torch.from_numpy(x).to(eng.device)
+    st = torch.cuda.current_stream().cuda_stream
+    wsb = lib.nsq_gemv_workspace_size(1, k)
+    ws = torch.empty(wsb, dtype=torch.uint8, device=eng.device)
+    for ptr, size in [(ws.data_ptr(), wsb), (None, 0)]:
+        y = torch.full((1, n), float("nan"), device=eng.device)
+        rc = lib.nsq_gemv(wd.data_ptr(), tid, layout, xd.data_ptr(), y.data_ptr(), 1, n, k, ptr, size, st)
+        assert rc == 0, _lib.strerror(rc)
+        torch.cuda.synchronize()
+        assert rel_err(y.cpu().numpy(), ref) <= GEMV_TOL
+
+
 def test_gemv_unaligned_activations(eng, oracle):
     """x only 4-byte aligned: taken through the workspace path."""
     n, k = 96, 1024
