@@ -41,7 +41,8 @@
 //               workspace the preparation kernel wrote
 //   warps 4..7  epilogue (TMEM lane quadrant = warp % 4, one row per thread)
 //   warps 8..15 dequant: raw bytes -> fp16 A tiles (128B-swizzled K-major),
-//               the min-term A tile and the row's d / dmin
+//               the min-term A tile and the row's d / dmin; warp (q, h)
+//               writes K stage q of rows [64h, 64h + 64) of every unit
 // Every wait is bounded (%globaltimer); a wait that gives up records
 // NSQ_ERR_TIMEOUT and the kernel winds down.
 #include <cuda.h>
@@ -306,7 +307,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < AS; ++s) mbar_init(&empty[s], 1);
-    for (int s = 0; s < TC_MMA_WARPS * AS; ++s) mbar_init(&full[s], TC_DQ_WARPS);
+    for (int s = 0; s < TC_MMA_WARPS * AS; ++s) mbar_init(&full[s], TC_DQ_WARPS / 4);  // one warp per row half
     for (int s = 0; s < BS; ++s) mbar_init(&bempty[s], 1);
     for (int s = 0; s < TC_MMA_WARPS * BS; ++s) mbar_init(&bfull[s], 1);
     for (int s = 0; s < CS; ++s) mbar_init(&col_empty[s], 1);
@@ -455,83 +456,72 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
       }
     }
   } else if (warp >= TC_DQ_WARP0) {
-    // ---- dequant: thread (row, pp) produces pairs pp and pp + 2 of every
-    // stage; a quarter-warp is 8 consecutive rows of one pair, so its
-    // 16-byte swizzled stores fall in 8 distinct bank groups
-    const int td = threadIdx.x - TC_DQ_WARP0 * 32;  // 0..255
-    const int row = (td & 7) | ((td >> 4) << 3);    // 0..127
-    const int pp = (td >> 3) & 1;
-    const int sw = row & 7;
+    // ---- dequant: warp (q, h) produces K stage q of every unit for rows
+    // [64h, 64h + 64), rows lane and lane + 32, all 8 chunks of a row in one
+    // thread (a quarter-warp is 8 consecutive rows of one chunk, so its
+    // 16-byte swizzled stores fall in 8 distinct bank groups).  The four
+    // stages of a unit are dequantized at the same time, and each warp meets
+    // its barriers once per unit instead of once per stage.  Warp q also
+    // writes word q of the unit's min-term chunk (the mins of sub-blocks 2q,
+    // 2q + 1); warp 0 the row's d / dmin, warp 1 the zero chunk beside it.
+    const int dw = warp - TC_DQ_WARP0, q = dw & 3, h = dw >> 2;
     for (int n = 0; n < nunits; ++n) {
       int sg, tl, c;
       locate(n, sg, tl, c);
       const int code = CODE == kTcMixed ? p.seg[sg].code : CODE;
       const int rs = n % RS, a = n % TC_NACC;
+      const int k = 4 * n + q, s = k % AS;
       if (!mbar_wait_bounded(&raw_full[rs], ph(n, RS))) break;
-      const int off16 = (int)(((int64_t)c * p.seg[sg].CB) & 15);
-      const uint8_t* raw = raw_sm + rs * RAW_BYTES + row * PITCH + off16;
-      // per-unit row data: d / dmin for the epilogue, mins for the min-term MMA
       if (!mbar_wait_bounded(&a2_empty[a], ph(n, TC_NACC) ^ 1)) break;
-      uint8_t* a2row = a2_sm + row * 128;
-      const int a2c = 2 * a;  // 16-byte chunks of this slot's 16 K columns
-      uint32_t S0 = 0, S1 = 0, S2 = 0;
-      if (code == kTcQ4K) {
-        const uint4 hdr = *reinterpret_cast<const uint4*>(raw);
-        S0 = hdr.y; S1 = hdr.z; S2 = hdr.w;
-        if (pp == 0) {
-          const float d = h2f((uint16_t)(hdr.x & 0xFFFF)), dmin = h2f((uint16_t)(hdr.x >> 16));
-          dsc[a * TC_BM + row] = make_float2(d, 32.0f * dmin);
-          uint32_t mw[4];
-#pragma unroll
-          for (int jj = 0; jj < 4; ++jj) {
-            const uint32_t m0 = q4k_scale_min(S0, S1, S2, 2 * jj) >> 8, m1 = q4k_scale_min(S0, S1, S2, 2 * jj + 1) >> 8;
-            mw[jj] = h2_bits(__halves2half2(__uint2half_rn(m0), __uint2half_rn(m1)));
-          }
-          *reinterpret_cast<uint4*>(a2row + ((a2c ^ sw) << 4)) = make_uint4(mw[0], mw[1], mw[2], mw[3]);
-          *reinterpret_cast<uint4*>(a2row + (((a2c + 1) ^ sw) << 4)) = make_uint4(0, 0, 0, 0);
-        }
-      } else {
-        if (pp == 0) {
-          dsc[a * TC_BM + row] = make_float2(h2f((uint16_t)ld_u16(raw + 208)), 0.f);
-          *reinterpret_cast<uint4*>(a2row + ((a2c ^ sw) << 4)) = make_uint4(0, 0, 0, 0);
-          *reinterpret_cast<uint4*>(a2row + (((a2c + 1) ^ sw) << 4)) = make_uint4(0, 0, 0, 0);
-        }
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&a2_full[a]);
+      const int off16 = (int)(((int64_t)c * p.seg[sg].CB) & 15);
+      const int a2c = 2 * a;  // 16-byte chunks of this unit's 16 K columns of the min-term tile
       bool ok = true;
-      for (int q = 0; q < 4; ++q) {
-        const int k = 4 * n + q, s = k % AS;
-        uint4 ch[4];
+#pragma unroll 1
+      for (int i = 0; i < 2; ++i) {
+        const int row = 64 * h + 32 * i + lane, sw = row & 7;
+        const uint8_t* raw = raw_sm + rs * RAW_BYTES + row * PITCH + off16;
+        uint8_t* a2row = a2_sm + row * 128;
+        uint4 ch[8];
         if (code == kTcQ4K) {
-          const uint32_t sm0 = q4k_scale_min(S0, S1, S2, 2 * q), sm1 = q4k_scale_min(S0, S1, S2, 2 * q + 1);
+          const uint4 hdr = *reinterpret_cast<const uint4*>(raw);
+          const uint32_t sm0 = q4k_scale_min(hdr.y, hdr.z, hdr.w, 2 * q);
+          const uint32_t sm1 = q4k_scale_min(hdr.y, hdr.z, hdr.w, 2 * q + 1);
+          *reinterpret_cast<uint32_t*>(a2row + ((a2c ^ sw) << 4) + 4 * q) =
+              h2_bits(__halves2half2(__uint2half_rn(sm0 >> 8), __uint2half_rn(sm1 >> 8)));
+          if (q == 0) {
+            const float d = h2f((uint16_t)(hdr.x & 0xFFFF)), dmin = h2f((uint16_t)(hdr.x >> 16));
+            dsc[a * TC_BM + row] = make_float2(d, 32.0f * dmin);
+          }
           const __half h0 = __uint2half_rn(sm0 & 0xFF), h1 = __uint2half_rn(sm1 & 0xFF);
           const __half2 s0 = __half2half2(h0), s1 = __half2half2(h1);
           const __half2 b0 = __half2half2(__hmul(h0, __float2half_rn(-1024.f)));
           const __half2 b1 = __half2half2(__hmul(h1, __float2half_rn(-1024.f)));
-          q4k_pair(raw, q, pp, s0, b0, s1, b1, ch[0], ch[1]);
-          q4k_pair(raw, q, pp + 2, s0, b0, s1, b1, ch[2], ch[3]);
+#pragma unroll
+          for (int pp = 0; pp < 4; ++pp) q4k_pair(raw, q, pp, s0, b0, s1, b1, ch[pp], ch[pp + 4]);
         } else {
-          q6k_pair(raw, q, pp, 4 * (q & 1), ch[0], ch[1], off16);
-          q6k_pair(raw, q, pp + 2, 4 * (q & 1), ch[2], ch[3], off16);
+          *reinterpret_cast<uint32_t*>(a2row + ((a2c ^ sw) << 4) + 4 * q) = 0u;
+          if (q == 0) dsc[a * TC_BM + row] = make_float2(h2f((uint16_t)ld_u16(raw + 208)), 0.f);
+#pragma unroll
+          for (int pp = 0; pp < 4; ++pp) q6k_pair(raw, q, pp, 4 * (q & 1), ch[pp], ch[pp + 4], off16);
         }
-        if (!mbar_wait_bounded(&empty[s], ph(k, AS) ^ 1)) {
+        if (q == 1) *reinterpret_cast<uint4*>(a2row + (((a2c + 1) ^ sw) << 4)) = make_uint4(0, 0, 0, 0);
+        // the slot is free once the MMAs of its previous unit have completed
+        if (i == 0 && !mbar_wait_bounded(&empty[s], ph(k, AS) ^ 1)) {
           ok = false;
           break;
         }
         uint8_t* dst = a_sm + s * TC_A_BYTES + row * 128;
-        *reinterpret_cast<uint4*>(dst + ((pp ^ sw) << 4)) = ch[0];
-        *reinterpret_cast<uint4*>(dst + (((pp + 4) ^ sw) << 4)) = ch[1];
-        *reinterpret_cast<uint4*>(dst + (((pp + 2) ^ sw) << 4)) = ch[2];
-        *reinterpret_cast<uint4*>(dst + (((pp + 6) ^ sw) << 4)) = ch[3];
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&full[(n % TC_MMA_WARPS) * AS + s]);
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) *reinterpret_cast<uint4*>(dst + ((cc ^ sw) << 4)) = ch[cc];
       }
       if (!ok) break;
+      fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&raw_empty[rs]);
+      if (lane == 0) {
+        mbar_arrive(&a2_full[a]);
+        mbar_arrive(&full[(n % TC_MMA_WARPS) * AS + s]);
+        mbar_arrive(&raw_empty[rs]);
+      }
     }
   } else if (warp >= TC_EPI_WARP0) {
     // ---- epilogue: one weight row per thread
@@ -754,15 +744,23 @@ int run_gemv_tc(const nsq_segment* segs, int nseg, const float* x, int64_t M, in
   p.ws_part = reinterpret_cast<float*>(const_cast<uint8_t*>(p.ws_col) + (size_t)NSB * TC_COL_BYTES);
   // shared memory: 4 A stages, up to 12 B stages (3 units of x ahead), 3
   // min-term stages; the raw ring takes what is left (3 or 4 units)
-  const int as = 4, cs = 3;
-  int bs = 12, rs = 4;
-  auto smem_of = [&](int b, int r) {
-    return 1024 + (size_t)as * TC_A_BYTES + (size_t)b * TC_B_BYTES + TC_A_BYTES + (size_t)cs * TC_B2_BYTES +
+  // A stages for two units when they fit (Q4_K): the dequant warps then
+  // fill a unit while the MMAs of the one before still read theirs, instead
+  // of waiting stage by stage for the previous unit's MMAs to complete
+  // (70B gate|up pair at M = 16: see the measured table); two units of B
+  // tiles, min-term tiles and raw columns ahead.  Otherwise (Q6_K's wider
+  // raw columns) one unit of A stages with deeper B and raw rings.
+  int as = 8, bs = 8, cs = 2, rs = 2;
+  auto smem_of = [&](int a, int b, int c, int r) {
+    return 1024 + (size_t)a * TC_A_BYTES + (size_t)b * TC_B_BYTES + TC_A_BYTES + (size_t)c * TC_B2_BYTES +
            (size_t)TC_SCL_STAGES * TC_BN * 4 + (size_t)TC_NACC * TC_BM * 8 + 1024 + (size_t)r * TC_BM * pitch;
   };
-  while (smem_of(bs, rs) > (size_t)TC_SMEM_LIMIT && rs > 3) --rs;
-  while (smem_of(bs, rs) > (size_t)TC_SMEM_LIMIT && bs > 4) bs -= 4;
-  const size_t smem = smem_of(bs, rs);
+  if (smem_of(as, bs, cs, rs) > (size_t)TC_SMEM_LIMIT) {
+    as = 4, bs = 12, cs = 3, rs = 4;
+    while (smem_of(as, bs, cs, rs) > (size_t)TC_SMEM_LIMIT && rs > 3) --rs;
+    while (smem_of(as, bs, cs, rs) > (size_t)TC_SMEM_LIMIT && bs > 4) bs -= 4;
+  }
+  const size_t smem = smem_of(as, bs, cs, rs);
   if (smem > (size_t)TC_SMEM_LIMIT) return -1;
   p.raw_stages = rs;
   p.a_stages = as;
