@@ -36,9 +36,9 @@
 //               TMEM).  A thread that issues, commits and waits in turn
 //               keeps the tensor pipe busy less than half the time; two
 //               issuers overlap each other's waits
-//   warp 2      B producer: x tiles (hi, lo) per 64-wide K stage, and per
-//               unit the min-term tile and the token scales, from the
-//               workspace the preparation kernel wrote
+//   warp 2      B producer: per unit the four x tiles (hi, lo), the
+//               min-term tile and the token scales, from the workspace the
+//               preparation kernel wrote
 //   warps 4..7  epilogue (TMEM lane quadrant = warp % 4, one row per thread)
 //   warps 8..15 dequant: raw bytes -> fp16 A tiles (128B-swizzled K-major),
 //               the min-term A tile and the row's d / dmin; warp (q, h)
@@ -65,6 +65,8 @@ constexpr int TC_A_BYTES = TC_BM * 128;      // fp16 [128 x 64], 16 KB
 constexpr int TC_B_BYTES = 2 * TC_BN * 128;  // fp16 hi [16 x 64] + lo [16 x 64], 4 KB
 constexpr int TC_COL_BYTES = 5120;           // workspace stride: B2 hi + lo (4 KB), 16 token scales, pad
 constexpr int TC_B2_BYTES = 4096;            // min-term tile (hi + lo) in shared memory
+constexpr int TC_UA_BYTES = 4 * TC_A_BYTES;  // a unit's four A stage tiles, 64 KB
+constexpr int TC_UB_BYTES = 4 * TC_B_BYTES + TC_B2_BYTES;  // its four x tiles and the min-term tile, 20 KB
 constexpr int TC_NACC = 4;                   // units in flight between the MMA and the epilogue
 constexpr int TC_MMA_WARPS = 2;              // MMA issuers (warps 1 and 3): unit n -> issuer n % 2
 constexpr int TC_ACC_COLS = 64;              // per unit: D (hi | lo, 32 columns) and the min-term D2
@@ -89,7 +91,7 @@ struct TcParams {
   int nseg, T, NSB, M;
   int64_t U;        // units = T * NSB
   int pitch;        // raw bytes per row per unit in shared memory
-  int raw_stages, a_stages, b_stages, col_stages;
+  int raw_stages, unit_slots;  // raw columns in flight; units of A and B tiles in shared memory
   const uint8_t* ws_b;    // [NSB * 4][hi 2 KB | lo 2 KB]
   const uint8_t* ws_col;  // [NSB][B2 hi 2 KB | B2 lo 2 KB | 16 f32 scales | pad]
   float* ws_part;         // [2 * TC_GMAX][128 rows][16 tokens]
@@ -266,29 +268,27 @@ template <int CODE>
 __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_constant__ TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int AS = p.a_stages, BS = p.b_stages, CS = p.col_stages, RS = p.raw_stages, PITCH = p.pitch;
-  // 1024-aligned swizzled tiles first: A stages, B stages (their own, deeper
-  // ring: x tiles come from the L2 and are prefetched several units ahead),
-  // the min-term A tile (4 unit slots, 16 K columns each), min-term B tiles
+  const int US = p.unit_slots, RS = p.raw_stages, PITCH = p.pitch;
+  // 1024-aligned swizzled tiles first: per unit slot the four A stage tiles
+  // and the B tiles (four x stages, then the min-term tile); the min-term A
+  // tile (4 accumulator slots, 16 K columns each)
   uint8_t* a_sm = smem;
-  uint8_t* b_sm = a_sm + AS * TC_A_BYTES;
-  uint8_t* a2_sm = b_sm + BS * TC_B_BYTES;
-  uint8_t* col_sm = a2_sm + TC_A_BYTES;
-  float* scl_sm = reinterpret_cast<float*>(col_sm + CS * TC_B2_BYTES);     // [16][16]
-  float2* dsc = reinterpret_cast<float2*>(scl_sm + TC_SCL_STAGES * TC_BN);  // [8][128] (d, 32 dmin)
+  uint8_t* b_sm = a_sm + US * TC_UA_BYTES;
+  uint8_t* a2_sm = b_sm + US * TC_UB_BYTES;
+  float* scl_sm = reinterpret_cast<float*>(a2_sm + TC_A_BYTES);             // [16][16]
+  float2* dsc = reinterpret_cast<float2*>(scl_sm + TC_SCL_STAGES * TC_BN);  // [4][128] (d, 32 dmin)
   uint8_t* raw_sm = reinterpret_cast<uint8_t*>(dsc + TC_NACC * TC_BM);
   const uint32_t RAW_BYTES = (uint32_t)(TC_BM * PITCH);
-  // The rings' "full" barriers come one set per MMA issuer (unit n fills
-  // set n % 2), their "empty" barriers are shared: a slot's data is used by
-  // both issuers in turn, but each full barrier only by one, in order, so a
-  // parity wait never sees a phase two ahead of the one it waits for.
-  uint64_t* full = reinterpret_cast<uint64_t*>(raw_sm + RS * RAW_BYTES);  // [issuer][AS]
-  uint64_t* empty = full + TC_MMA_WARPS * AS;
-  uint64_t* bfull = empty + AS;                                           // [issuer][BS]
-  uint64_t* bempty = bfull + TC_MMA_WARPS * BS;
-  uint64_t* col_full = bempty + BS;                                       // [issuer][CS]
-  uint64_t* col_empty = col_full + TC_MMA_WARPS * CS;
-  uint64_t* scl_full = col_empty + CS;
+  // A unit slot is filled by the dequant warps (afull) and the B producer
+  // (bfull) and freed by one commit of its MMA thread (uempty).  The full
+  // barriers come one set per MMA thread (unit n fills set n % 2): with one
+  // unit slot both threads use its data in turn, but each full barrier is
+  // waited on by one thread, in order, so a parity wait never sees a phase
+  // two ahead of the one it waits for.
+  uint64_t* afull = reinterpret_cast<uint64_t*>(raw_sm + RS * RAW_BYTES);  // [thread][US]
+  uint64_t* bfull = afull + TC_MMA_WARPS * US;                             // [thread][US]
+  uint64_t* uempty = bfull + TC_MMA_WARPS * US;                            // [US]
+  uint64_t* scl_full = uempty + US;
   uint64_t* scl_empty = scl_full + TC_SCL_STAGES;
   uint64_t* a2_full = scl_empty + TC_SCL_STAGES;
   uint64_t* a2_empty = a2_full + TC_NACC;
@@ -306,12 +306,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
   const int nunits = (int)(u1 - u0);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < AS; ++s) mbar_init(&empty[s], 1);
-    for (int s = 0; s < TC_MMA_WARPS * AS; ++s) mbar_init(&full[s], TC_DQ_WARPS / 4);  // one warp per row half
-    for (int s = 0; s < BS; ++s) mbar_init(&bempty[s], 1);
-    for (int s = 0; s < TC_MMA_WARPS * BS; ++s) mbar_init(&bfull[s], 1);
-    for (int s = 0; s < CS; ++s) mbar_init(&col_empty[s], 1);
-    for (int s = 0; s < TC_MMA_WARPS * CS; ++s) mbar_init(&col_full[s], 1);
+    for (int s = 0; s < US; ++s) mbar_init(&uempty[s], 1);
+    for (int s = 0; s < TC_MMA_WARPS * US; ++s) {
+      mbar_init(&afull[s], TC_DQ_WARPS);
+      mbar_init(&bfull[s], 1);
+    }
     for (int s = 0; s < TC_SCL_STAGES; ++s) {
       mbar_init(&scl_full[s], 1);
       mbar_init(&scl_empty[s], 4);
@@ -375,6 +374,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
             "l"(reinterpret_cast<uint64_t>(&p.wmap[sg])), "r"(x0), "r"(tl * TC_BM), "r"(smem_u32(&raw_full[rs])),
             "l"(pol)
             : "memory");
+        // the column that takes this slot next is fetched into the L2 now, so
+        // its copy (issued once this one is consumed) reads the L2, not HBM
+        if (n + RS < nunits) {
+          int sg2, tl2, c2;
+          locate(n + RS, sg2, tl2, c2);
+          const int x2 = (int)(((int64_t)c2 * p.seg[sg2].CB) & ~int64_t(15)) / 2;
+          asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                           reinterpret_cast<uint64_t>(&p.wmap[sg2])),
+                       "r"(x2), "r"(tl2 * TC_BM)
+                       : "memory");
+        }
       }
     }
   } else if (warp == 1 || warp == 3) {
@@ -382,44 +392,33 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
     // alternate between the issuers)
     if (lane == 0) {
       const int issuer = warp == 1 ? 0 : 1;
-      uint64_t* my_full = full + issuer * AS;
-      uint64_t* my_bfull = bfull + issuer * BS;
-      uint64_t* my_col_full = col_full + issuer * CS;
+      uint64_t* my_afull = afull + issuer * US;
+      uint64_t* my_bfull = bfull + issuer * US;
       // N = 32: the hi and lo x tiles are adjacent 16-row tiles, one operand
       constexpr uint32_t IDESC = umma_idesc_f16(TC_BM, 2 * TC_BN);
       const uint32_t a_base = smem_u32(a_sm), b_base = smem_u32(b_sm), a2_base = smem_u32(a2_sm);
-      const uint32_t col_base = smem_u32(col_sm);
-      bool ok = true;
-      for (int n = issuer; n < nunits && ok; n += TC_MMA_WARPS) {
-        const int a = n % TC_NACC;
+      for (int n = issuer; n < nunits; n += TC_MMA_WARPS) {
+        const int a = n % TC_NACC, u = n % US;
         const uint32_t dD = tmem + (uint32_t)(TC_ACC_COLS * a), dD2 = dD + 32;
-        if (!mbar_wait_bounded(&acc_empty[a], ph(n, TC_NACC) ^ 1)) break;
-        tc_fence_after();
-        for (int q = 0; q < 4; ++q) {
-          const int k = 4 * n + q, s = k % AS, sb = k % BS;
-          if (!mbar_wait_bounded(&my_full[s], iph(k, AS, 4)) || !mbar_wait_bounded(&my_bfull[sb], iph(k, BS, 4))) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t ad = umma_desc_sw128(a_base + s * TC_A_BYTES + kk * 32);
-            const uint64_t bd = umma_desc_sw128(b_base + sb * TC_B_BYTES + kk * 32);
-            tc_mma_bf16(dD, ad, bd, IDESC, (q | kk) ? 1u : 0u);
-          }
-          tc_commit(&empty[s]);
-          tc_commit(&bempty[sb]);
-        }
-        if (!ok) break;
-        const int cs = n % CS;
-        if (!mbar_wait_bounded(&my_col_full[cs], iph(n, CS, 1)) || !mbar_wait_bounded(&a2_full[a], ph(n, TC_NACC)))
+        // the accumulator is free, the unit's A tiles (and its min-term A
+        // column, written before the same arrivals) and B tiles are in place
+        if (!mbar_wait_bounded(&acc_empty[a], ph(n, TC_NACC) ^ 1) || !mbar_wait_bounded(&my_afull[u], iph(n, US, 1)) ||
+            !mbar_wait_bounded(&my_bfull[u], iph(n, US, 1)))
           break;
         tc_fence_after();
-        // min-term A slot a: tile a / 4, K columns 16 (a % 4) .. +16
-        const uint64_t a2d = umma_desc_sw128(a2_base + a * 32);
-        tc_mma_bf16(dD2, a2d, umma_desc_sw128(col_base + cs * TC_B2_BYTES), IDESC, 0u);
-        tc_commit(&col_empty[cs]);
+        const uint32_t ua = a_base + u * TC_UA_BYTES, ub = b_base + u * TC_UB_BYTES;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t ad = umma_desc_sw128(ua + q * TC_A_BYTES + kk * 32);
+            const uint64_t bd = umma_desc_sw128(ub + q * TC_B_BYTES + kk * 32);
+            tc_mma_bf16(dD, ad, bd, IDESC, (q | kk) ? 1u : 0u);
+          }
+        }
+        // min-term A slot a: K columns 16a .. 16a + 16 of the min-term tile
+        tc_mma_bf16(dD2, umma_desc_sw128(a2_base + a * 32), umma_desc_sw128(ub + 4 * TC_B_BYTES), IDESC, 0u);
+        tc_commit(&uempty[u]);
         tc_commit(&acc_full[a]);
       }
       tc_commit(done);  // every MMA this thread issued has completed when this arrives
@@ -432,24 +431,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
       for (int n = 0; n < nunits; ++n) {
         int sg, tl, c;
         locate(n, sg, tl, c);
-        bool ok = true;
-        for (int q = 0; q < 4; ++q) {
-          const int k = 4 * n + q, sb = k % BS;
-          if (!mbar_wait_bounded(&bempty[sb], ph(k, BS) ^ 1)) {
-            ok = false;
-            break;
-          }
-          uint64_t* bf = &bfull[(n % TC_MMA_WARPS) * BS + sb];
-          mbar_arrive_expect_tx(bf, TC_B_BYTES);
-          bulk_g2s_hint(b_sm + sb * TC_B_BYTES, p.ws_b + (int64_t)(4 * c + q) * TC_B_BYTES, TC_B_BYTES, bf, pol);
-        }
-        if (!ok) break;
-        const int cs = n % CS, ss = n % TC_SCL_STAGES;
+        const int u = n % US, ss = n % TC_SCL_STAGES;
+        // the x tiles of super-block c's four K stages are contiguous in the workspace
         const uint8_t* col = p.ws_col + (int64_t)c * TC_COL_BYTES;
-        if (!mbar_wait_bounded(&col_empty[cs], ph(n, CS) ^ 1)) break;
-        uint64_t* cf = &col_full[(n % TC_MMA_WARPS) * CS + cs];
-        mbar_arrive_expect_tx(cf, TC_B2_BYTES);
-        bulk_g2s_hint(col_sm + cs * TC_B2_BYTES, col, TC_B2_BYTES, cf, pol);
+        if (!mbar_wait_bounded(&uempty[u], ph(n, US) ^ 1)) break;
+        uint64_t* bf = &bfull[(n % TC_MMA_WARPS) * US + u];
+        mbar_arrive_expect_tx(bf, TC_UB_BYTES);
+        uint8_t* dst = b_sm + u * TC_UB_BYTES;
+        bulk_g2s_hint(dst, p.ws_b + (int64_t)(4 * c) * TC_B_BYTES, 4 * TC_B_BYTES, bf, pol);
+        bulk_g2s_hint(dst + 4 * TC_B_BYTES, col, TC_B2_BYTES, bf, pol);
         if (!mbar_wait_bounded(&scl_empty[ss], ph(n, TC_SCL_STAGES) ^ 1)) break;
         mbar_arrive_expect_tx(&scl_full[ss], TC_BN * 4);
         bulk_g2s_hint(scl_sm + ss * TC_BN, col + TC_B2_BYTES, TC_BN * 4, &scl_full[ss], pol);
@@ -469,8 +459,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
       int sg, tl, c;
       locate(n, sg, tl, c);
       const int code = CODE == kTcMixed ? p.seg[sg].code : CODE;
-      const int rs = n % RS, a = n % TC_NACC;
-      const int k = 4 * n + q, s = k % AS;
+      const int rs = n % RS, a = n % TC_NACC, u = n % US;
       if (!mbar_wait_bounded(&raw_full[rs], ph(n, RS))) break;
       if (!mbar_wait_bounded(&a2_empty[a], ph(n, TC_NACC) ^ 1)) break;
       const int off16 = (int)(((int64_t)c * p.seg[sg].CB) & 15);
@@ -505,12 +494,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
           for (int pp = 0; pp < 4; ++pp) q6k_pair(raw, q, pp, 4 * (q & 1), ch[pp], ch[pp + 4], off16);
         }
         if (q == 1) *reinterpret_cast<uint4*>(a2row + (((a2c + 1) ^ sw) << 4)) = make_uint4(0, 0, 0, 0);
-        // the slot is free once the MMAs of its previous unit have completed
-        if (i == 0 && !mbar_wait_bounded(&empty[s], ph(k, AS) ^ 1)) {
+        // the unit slot is free once the MMAs of its previous unit have completed
+        if (i == 0 && !mbar_wait_bounded(&uempty[u], ph(n, US) ^ 1)) {
           ok = false;
           break;
         }
-        uint8_t* dst = a_sm + s * TC_A_BYTES + row * 128;
+        uint8_t* dst = a_sm + u * TC_UA_BYTES + q * TC_A_BYTES + row * 128;
 #pragma unroll
         for (int cc = 0; cc < 8; ++cc) *reinterpret_cast<uint4*>(dst + ((cc ^ sw) << 4)) = ch[cc];
       }
@@ -519,7 +508,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&a2_full[a]);
-        mbar_arrive(&full[(n % TC_MMA_WARPS) * AS + s]);
+        mbar_arrive(&afull[(n % TC_MMA_WARPS) * US + u]);
         mbar_arrive(&raw_empty[rs]);
       }
     }
@@ -744,28 +733,24 @@ int run_gemv_tc(const nsq_segment* segs, int nseg, const float* x, int64_t M, in
   p.ws_part = reinterpret_cast<float*>(const_cast<uint8_t*>(p.ws_col) + (size_t)NSB * TC_COL_BYTES);
   // shared memory: 4 A stages, up to 12 B stages (3 units of x ahead), 3
   // min-term stages; the raw ring takes what is left (3 or 4 units)
-  // A stages for two units when they fit (Q4_K): the dequant warps then
-  // fill a unit while the MMAs of the one before still read theirs, instead
-  // of waiting stage by stage for the previous unit's MMAs to complete
-  // (70B gate|up pair at M = 16: see the measured table); two units of B
-  // tiles, min-term tiles and raw columns ahead.  Otherwise (Q6_K's wider
-  // raw columns) one unit of A stages with deeper B and raw rings.
-  int as = 8, bs = 8, cs = 2, rs = 2;
-  auto smem_of = [&](int a, int b, int c, int r) {
-    return 1024 + (size_t)a * TC_A_BYTES + (size_t)b * TC_B_BYTES + TC_A_BYTES + (size_t)c * TC_B2_BYTES +
-           (size_t)TC_SCL_STAGES * TC_BN * 4 + (size_t)TC_NACC * TC_BM * 8 + 1024 + (size_t)r * TC_BM * pitch;
+  // Shared memory: two unit slots of A and B tiles when they fit beside two
+  // raw columns (Q4_K), so that the dequant warps and the B producer fill a
+  // unit while the MMAs of the one before still read theirs; otherwise (Q6_K's
+  // wider raw columns) one unit slot and up to four raw columns.
+  auto smem_of = [&](int us, int r) {
+    return 1024 + (size_t)us * (TC_UA_BYTES + TC_UB_BYTES) + TC_A_BYTES + (size_t)TC_SCL_STAGES * TC_BN * 4 +
+           (size_t)TC_NACC * TC_BM * 8 + 1024 + (size_t)r * TC_BM * pitch;
   };
-  if (smem_of(as, bs, cs, rs) > (size_t)TC_SMEM_LIMIT) {
-    as = 4, bs = 12, cs = 3, rs = 4;
-    while (smem_of(as, bs, cs, rs) > (size_t)TC_SMEM_LIMIT && rs > 3) --rs;
-    while (smem_of(as, bs, cs, rs) > (size_t)TC_SMEM_LIMIT && bs > 4) bs -= 4;
+  int us = 2, rs = 2;
+  if (smem_of(us, rs) > (size_t)TC_SMEM_LIMIT) {
+    us = 1;
+    rs = 4;
+    while (smem_of(us, rs) > (size_t)TC_SMEM_LIMIT && rs > 2) --rs;
   }
-  const size_t smem = smem_of(as, bs, cs, rs);
+  const size_t smem = smem_of(us, rs);
   if (smem > (size_t)TC_SMEM_LIMIT) return -1;
   p.raw_stages = rs;
-  p.a_stages = as;
-  p.b_stages = bs;
-  p.col_stages = cs;
+  p.unit_slots = us;
   int G = num_sms > 0 ? num_sms : 148;
   if (G > TC_GMAX) G = TC_GMAX;
   if ((int64_t)G > p.U) G = (int)p.U;
