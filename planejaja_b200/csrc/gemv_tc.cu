@@ -465,7 +465,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
       const int off16 = (int)(((int64_t)c * p.seg[sg].CB) & 15);
       const int a2c = 2 * a;  // 16-byte chunks of this unit's 16 K columns of the min-term tile
       bool ok = true;
-#pragma unroll 1
+      // both rows unrolled: their independent integer / half chains interleave
+      // (70B gate|up pair at M = 16: 200 -> 187 us)
+#pragma unroll
       for (int i = 0; i < 2; ++i) {
         const int row = 64 * h + 32 * i + lane, sw = row & 7;
         const uint8_t* raw = raw_sm + rs * RAW_BYTES + row * PITCH + off16;
