@@ -120,7 +120,7 @@ int nsq_dequant(const void *w, int ggml_type, int q6k_layout, int out_dtype, voi
  * not needed); the GEMV accumulates exact integer dot products per 16 or 32
  * weights and combines them in fp32.
  *
- * For 9..16 tokens over Q4_K and ggml-layout Q6_K (K % 256 == 0) the GEMV
+ * For 5..16 tokens over Q4_K and ggml-layout Q6_K (K % 256 == 0) the GEMV
  * runs on the tcgen05 tensor cores: the 6-bit sub-scales folded into fp16
  * weight operands (exact products), x as fp16 hi + lo parts (22 bits), fp32
  * accumulation, one fp32 epilogue per 256 weights.  Its workspace (fp16

@@ -663,7 +663,10 @@ bool tc_covers(const nsq_segment* segs, int nseg, int64_t M, int64_t K) {
   return true;
 }
 
-int tc_min_m() { return tune(kTuneTcMinM, 9); }
+// From 5 tokens the tcgen05 kernel beats the dp4a kernel's passes of 4 tokens
+// (B200: Llama-3-8B decode step at M = 5: 4.96 against 5.43 ms, M = 8: 4.98
+// against 7.42 ms; at M = 4 the single dp4a pass wins, 3.78 against 4.96 ms).
+int tc_min_m() { return tune(kTuneTcMinM, 5); }
 
 template <int CODE>
 static cudaError_t launch_tc(const TcParams& p, int blocks, size_t smem, cudaStream_t st) {
