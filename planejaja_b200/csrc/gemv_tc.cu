@@ -261,6 +261,43 @@ __device__ __forceinline__ void q6k_pair(const uint8_t* raw, int q, int p, uint3
   }
 }
 
+// Walk of a CTA's units: segment, tile within it and super-block column of
+// unit u0 + n, advanced one unit at a time (the per-unit 64-bit division of a
+// direct lookup cost every role's threads more integer work than the dequant
+// of a unit's rows).
+struct TcCursor {
+  int sg, tl, c, t;
+  __device__ void init(const TcParams& p, int64_t u) {
+    t = (int)(u / p.NSB);
+    c = (int)(u - (int64_t)t * p.NSB);
+    sg = 0;
+    while (sg + 1 < p.nseg && t >= p.seg[sg + 1].tile0) ++sg;
+    tl = t - p.seg[sg].tile0;
+  }
+  __device__ void next(const TcParams& p) {
+    if (++c < p.NSB) return;
+    c = 0;
+    ++t;
+    ++tl;
+    while (sg + 1 < p.nseg && t >= p.seg[sg + 1].tile0) {
+      ++sg;
+      tl = t - p.seg[sg].tile0;
+    }
+  }
+};
+// Use j of a ring of R slots, one use at a time: slot j % R, phase parity (j / R) & 1.
+struct TcRing {
+  int R, slot;
+  uint32_t par;
+  __device__ explicit TcRing(int r) : R(r), slot(0), par(0u) {}
+  __device__ void next() {
+    if (++slot == R) {
+      slot = 0;
+      par ^= 1u;
+    }
+  }
+};
+
 // CTA index owning unit u (unit ranges [U i / G, U (i+1) / G)).
 __device__ __forceinline__ int tc_owner(int64_t u, int64_t U, int G) { return (int)(((u + 1) * G - 1) / U); }
 
@@ -337,15 +374,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  // unit n of this CTA -> segment, tile within it, super-block column
-  auto locate = [&](int n, int& sg, int& tl, int& c) {
-    const int64_t u = u0 + n;
-    const int t = (int)(u / p.NSB);
-    c = (int)(u - (int64_t)t * p.NSB);
-    sg = 0;
-    while (sg + 1 < p.nseg && t >= p.seg[sg + 1].tile0) ++sg;
-    tl = t - p.seg[sg].tile0;
-  };
   // parity of the k-th use of a ring slot: full waits (k / R) & 1, empty waits its complement
   auto ph = [](int k, int R) { return (uint32_t)((k / R) & 1); };
   // parity of an issuer's own full barrier: use k (per uses per unit) of a
@@ -361,11 +389,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
     // ---- raw producer: the unit's GGUF column for the tile's 128 rows
     if (lane == 0) {
       const uint64_t pol = l2_policy_evict_first();
-      for (int n = 0; n < nunits; ++n) {
-        int sg, tl, c;
-        locate(n, sg, tl, c);
-        const int rs = n % RS;
-        if (!mbar_wait_bounded(&raw_empty[rs], ph(n, RS) ^ 1)) break;
+      TcCursor cur, ahead;  // unit n, and unit n + RS (the next user of n's slot)
+      cur.init(p, u0);
+      ahead.init(p, u0 + RS);
+      TcRing rr(RS);
+      for (int n = 0; n < nunits; ++n, cur.next(p), ahead.next(p), rr.next()) {
+        const int sg = cur.sg, tl = cur.tl, c = cur.c, rs = rr.slot;
+        if (!mbar_wait_bounded(&raw_empty[rs], rr.par ^ 1)) break;
         const int x0 = (int)(((int64_t)c * p.seg[sg].CB) & ~int64_t(15)) / 2;
         mbar_arrive_expect_tx(&raw_full[rs], RAW_BYTES);
         asm volatile(
@@ -377,8 +407,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
         // the column that takes this slot next is fetched into the L2 now, so
         // its copy (issued once this one is consumed) reads the L2, not HBM
         if (n + RS < nunits) {
-          int sg2, tl2, c2;
-          locate(n + RS, sg2, tl2, c2);
+          const int sg2 = ahead.sg, tl2 = ahead.tl, c2 = ahead.c;
           const int x2 = (int)(((int64_t)c2 * p.seg[sg2].CB) & ~int64_t(15)) / 2;
           asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
                            reinterpret_cast<uint64_t>(&p.wmap[sg2])),
@@ -428,13 +457,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
     if (lane == 0) {
       tc_grid_wait();  // the workspace is written by the preparation kernel
       const uint64_t pol = l2_policy_evict_last();
-      for (int n = 0; n < nunits; ++n) {
-        int sg, tl, c;
-        locate(n, sg, tl, c);
-        const int u = n % US, ss = n % TC_SCL_STAGES;
+      TcCursor cur;
+      cur.init(p, u0);
+      TcRing ur(US);
+      for (int n = 0; n < nunits; ++n, cur.next(p), ur.next()) {
+        const int c = cur.c, u = ur.slot, ss = n % TC_SCL_STAGES;
         // the x tiles of super-block c's four K stages are contiguous in the workspace
         const uint8_t* col = p.ws_col + (int64_t)c * TC_COL_BYTES;
-        if (!mbar_wait_bounded(&uempty[u], ph(n, US) ^ 1)) break;
+        if (!mbar_wait_bounded(&uempty[u], ur.par ^ 1)) break;
         uint64_t* bf = &bfull[(n % TC_MMA_WARPS) * US + u];
         mbar_arrive_expect_tx(bf, TC_UB_BYTES);
         uint8_t* dst = b_sm + u * TC_UB_BYTES;
@@ -455,12 +485,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
     // writes word q of the unit's min-term chunk (the mins of sub-blocks 2q,
     // 2q + 1); warp 0 the row's d / dmin, warp 1 the zero chunk beside it.
     const int dw = warp - TC_DQ_WARP0, q = dw & 3, h = dw >> 2;
-    for (int n = 0; n < nunits; ++n) {
-      int sg, tl, c;
-      locate(n, sg, tl, c);
+    TcCursor cur;
+    cur.init(p, u0);
+    TcRing rr(RS), ur(US);
+    for (int n = 0; n < nunits; ++n, cur.next(p), rr.next(), ur.next()) {
+      const int sg = cur.sg, c = cur.c;
       const int code = CODE == kTcMixed ? p.seg[sg].code : CODE;
-      const int rs = n % RS, a = n % TC_NACC, u = n % US;
-      if (!mbar_wait_bounded(&raw_full[rs], ph(n, RS))) break;
+      const int rs = rr.slot, a = n % TC_NACC, u = ur.slot;
+      if (!mbar_wait_bounded(&raw_full[rs], rr.par)) break;
       if (!mbar_wait_bounded(&a2_empty[a], ph(n, TC_NACC) ^ 1)) break;
       const int off16 = (int)(((int64_t)c * p.seg[sg].CB) & 15);
       const int a2c = 2 * a;  // 16-byte chunks of this unit's 16 K columns of the min-term tile
@@ -497,7 +529,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
         }
         if (q == 1) *reinterpret_cast<uint4*>(a2row + (((a2c + 1) ^ sw) << 4)) = make_uint4(0, 0, 0, 0);
         // the unit slot is free once the MMAs of its previous unit have completed
-        if (i == 0 && !mbar_wait_bounded(&uempty[u], ph(n, US) ^ 1)) {
+        if (i == 0 && !mbar_wait_bounded(&uempty[u], ur.par ^ 1)) {
           ok = false;
           break;
         }
@@ -525,9 +557,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
     // A wait that gives up stops the work but not the walk: the four warps
     // pass the same named barriers whatever happens.
     bool ok = true;
-    for (int n = 0; n < nunits; ++n) {
-      int sg, tl, c;
-      locate(n, sg, tl, c);
+    TcCursor cur;
+    cur.init(p, u0);
+    for (int n = 0; n < nunits; ++n, cur.next(p)) {
+      const int sg = cur.sg, tl = cur.tl, c = cur.c;
       if (seg_first_c < 0) seg_first_c = c;
       const int a = n % TC_NACC, ss = n % TC_SCL_STAGES;
       if (ok)
