@@ -668,15 +668,23 @@ __global__ void __launch_bounds__(kRowsThreads, 4) gemv_fused_kernel(const __gri
         cluster_wait_acquire();
       }
       for (int t = 0; t < npre; ++t) issue(pre[t], t, false, true);
-      for (int t = npre; more; ++t) {
-        const int s = t % p.nstages;
-        if (!mbar_wait_bounded(&empty[s], (uint32_t)(((t / p.nstages) - 1) & 1))) {
+      // stage t = npre, npre + 1, ...: slot t % nstages, waiting for the
+      // consumers' release of its previous use (parity (t / nstages - 1) & 1),
+      // counted incrementally
+      int s = npre == p.nstages ? 0 : npre;
+      uint32_t epar = npre == p.nstages ? 0u : 1u;
+      while (more) {
+        if (!mbar_wait_bounded(&empty[s], epar)) {
           s_fail = 1;
           break;
         }
         fence_proxy_async_smem();
         issue(it, s, true, true);
         more = it.next(p, r_end);
+        if (++s == p.nstages) {
+          s = 0;
+          epar ^= 1u;
+        }
       }
     } else {
       grid_dep_wait();
@@ -763,10 +771,12 @@ __global__ void __launch_bounds__(kRowsThreads, 4) gemv_fused_kernel(const __gri
       ItemCursor it;
       it.first(p, r_begin, r_end);
       bool more = true;
-      for (int t = 0; more; ++t) {
-        const int s = t % p.nstages;
+      // stage t: slot t % nstages, parity (t / nstages) & 1, counted incrementally
+      int s = 0;
+      uint32_t fpar = 0u;
+      for (; more; s = (s + 1 == p.nstages) ? 0 : s + 1, fpar ^= (s == 0) ? 1u : 0u) {
         const FSeg& sg = p.seg[it.seg];
-        if (ok) ok = mbar_wait_bounded(&full[s], (uint32_t)((t / p.nstages) & 1));
+        if (ok) ok = mbar_wait_bounded(&full[s], fpar);
         if (ok) {
           const int np = (int)min((int64_t)p.PPS, (int64_t)p.npieces - (int64_t)it.c * p.PPS);
           const uint8_t* slot = stages + (size_t)s * p.stage_bytes;
