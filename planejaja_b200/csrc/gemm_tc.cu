@@ -305,6 +305,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_tc_kernel(const __grid_c
   constexpr int TN = TOK / NH;
   constexpr uint32_t IDESC = umma_idesc_bf16(GEMM_BM, TN);
   constexpr int GEMM_STAGES = gemm_stages<TYPE, TOK>();
+  // When the ring holds a whole 256-wide column (four K stages, TOK = 128),
+  // dequant warp (q, h) writes K stage q of rows [32h, 32h + 32) of every
+  // column: 64 weights per thread and one set of barrier waits per column,
+  // instead of 16 weights per thread and per stage.
+  constexpr bool kColumnWarps = GEMM_STAGES >= 4;
+  constexpr int kFullArrivals = 1 + (kColumnWarps ? 4 : GEMM_DQ_THREADS / 32);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* w_sm = smem;
@@ -331,7 +337,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_tc_kernel(const __grid_c
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < GEMM_STAGES; ++s) {
-      mbar_init(&full[s], 1 + GEMM_DQ_THREADS / 32);
+      mbar_init(&full[s], kFullArrivals);
       mbar_init(&empty[s], 1);
     }
     for (int s = 0; s < GEMM_RAW_STAGES; ++s) {
@@ -439,13 +445,75 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_tc_kernel(const __grid_c
       }
     }
   } else if (warp >= GEMM_DQ_WARP0) {
+    bool ok = true;
+    if constexpr (kColumnWarps) {
+    // ---- dequant, one warp per (K stage q, 32-row quarter h) of every
+    // column; a thread writes all 8 chunks of its row's stage, so a
+    // quarter-warp's stores (8 consecutive rows, one chunk) hit 8 distinct
+    // bank groups
+    const int dw = warp - GEMM_DQ_WARP0, q = dw & 3, r = 32 * (dw >> 2) + lane;
+    const bool row_ok = r < rows_valid;
+    // stage kb - kb0 = 4 (c - c0) + q: slot and parity advanced by 4 per column
+    int s = q, rs = 0;
+    uint32_t spar = 0u, rpar = 0u;
+    for (int c = c0; c < c1; ++c) {
+      if (!mbar_wait_bounded(&raw_full[rs], rpar)) {
+        ok = false;
+        break;
+      }
+      uint32_t pk[4][8];
+      int chunk[4][2];
+      if (row_ok) {
+        const int64_t off = (n0 + r) * p.RB + (int64_t)c * CB;
+        const uint8_t* raw = raw_sm + rs * RAW_STAGE + r * RawCol<TYPE>::pitch + (int)(off & 15);
+#pragma unroll
+        for (int qq = 0; qq < 4; ++qq) dequant_col_kblock<TYPE, LAYOUT>(raw, q, qq, pk[qq], chunk[qq]);
+      } else {
+#pragma unroll
+        for (int qq = 0; qq < 4; ++qq) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) pk[qq][i] = 0u;
+          chunk[qq][0] = 2 * qq;
+          chunk[qq][1] = 2 * qq + 1;
+        }
+      }
+      // this column's raw bytes are no longer read by this warp
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&raw_empty[rs]);
+      if (!mbar_wait_bounded(&empty[s], spar ^ 1u)) {
+        ok = false;
+        break;
+      }
+      uint8_t* dst = w_sm + s * W_STAGE + r * 128;
+#pragma unroll
+      for (int qq = 0; qq < 4; ++qq) {
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const int cc = chunk[qq][i] ^ (r & 7);
+          *reinterpret_cast<uint4*>(dst + cc * 16) =
+              make_uint4(pk[qq][4 * i], pk[qq][4 * i + 1], pk[qq][4 * i + 2], pk[qq][4 * i + 3]);
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full[s]);
+      s += 4;
+      if (s >= GEMM_STAGES) {
+        s -= GEMM_STAGES;
+        spar ^= 1u;
+      }
+      if (++rs == GEMM_RAW_STAGES) {
+        rs = 0;
+        rpar ^= 1u;
+      }
+    }
+    } else {
     // ---- dequant: each quarter-warp covers 8 distinct rows of one K
     // quarter, so its 16-byte swizzled stores hit 8 distinct bank groups
     const int t = threadIdx.x - GEMM_DQ_WARP0 * 32;  // 0..511
     const int qq = (t >> 3) & 3;
     const int r = (t & 7) | ((t >> 5) << 3);
     const bool row_ok = r < rows_valid;
-    bool ok = true;
     for (int kb = kb0; kb < kb1; ++kb) {
       const int c = kb >> 2, q = kb & 3, rs = (c - c0) % GEMM_RAW_STAGES;
       const int s = (kb - kb0) % GEMM_STAGES;
@@ -483,6 +551,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_tc_kernel(const __grid_c
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&full[s]);
+    }
     }
     // ---- epilogue: warp w reads TMEM lanes 32*(w%4).. (its W rows) for a
     // quarter of the TOK accumulator columns
