@@ -489,7 +489,9 @@ __global__ void __launch_bounds__(kMmaThreads, 2) gemv_mma_kernel(const __grid_c
       grid_dep_wait_m();
       grid_dep_launch_m();
       bool ok = true;
-      int t = 0;
+      // stage t: slot ts = t % nstages, parity tph = (t / nstages) & 1, counted incrementally
+      int t = 0, ts = 0;
+      uint32_t tph = 0u;
       for (int c = 0; c < p.nchunks && ok; ++c) {
         const int b = c & 1;
         if (c >= 2 && !mbar_wait_bounded(&xempty[b], (uint32_t)(((c >> 1) - 1) & 1))) {
@@ -506,10 +508,11 @@ __global__ void __launch_bounds__(kMmaThreads, 2) gemv_mma_kernel(const __grid_c
         __syncwarp();
         MRowCursor it;
         bool more = it.first(p, r_begin, r_end);
-        for (; more; ++t, more = it.next(p, r_end)) {
+        for (; more; ++t, ts = (ts + 1 == p.nstages) ? 0 : ts + 1, tph ^= (ts == 0) ? 1u : 0u,
+                     more = it.next(p, r_end)) {
           if (t < npre) continue;  // issued before the dependency wait
-          const int s = t % p.nstages;
-          if (!mbar_wait_bounded(&empty[s], (uint32_t)(((t / p.nstages) - 1) & 1))) {
+          const int s = ts;
+          if (!mbar_wait_bounded(&empty[s], tph ^ 1u)) {
             ok = false;
             break;
           }
@@ -529,7 +532,8 @@ __global__ void __launch_bounds__(kMmaThreads, 2) gemv_mma_kernel(const __grid_c
     grid_dep_wait_m();
     grid_dep_launch_m();
     bool ok = true;
-    int t = 0;
+    int t = 0, ts = 0;  // stage t: slot ts = t % nstages, parity tph = (t / nstages) & 1
+    uint32_t tph = 0u;
     MRowCursor probe;
     const bool any = probe.first(p, r_begin, r_end);
     for (int c = 0; any && c < p.nchunks; ++c) {
@@ -539,9 +543,10 @@ __global__ void __launch_bounds__(kMmaThreads, 2) gemv_mma_kernel(const __grid_c
       const int np = min(p.PPS, p.npieces - c * p.PPS);
       MRowCursor it;
       bool more = it.first(p, r_begin, r_end);
-      for (int item = 0; more; ++t, ++item, more = it.next(p, r_end)) {
-        const int s = t % p.nstages;
-        if (ok) ok = mbar_wait_bounded(&full[s], (uint32_t)((t / p.nstages) & 1));
+      for (int item = 0; more; ++t, ++item, ts = (ts + 1 == p.nstages) ? 0 : ts + 1, tph ^= (ts == 0) ? 1u : 0u,
+                                   more = it.next(p, r_end)) {
+        const int s = ts;
+        if (ok) ok = mbar_wait_bounded(&full[s], tph);
         if (item >= p.max_items) ok = false;  // the plan bounds the items; never taken
         float acc[NOCT][4];
         float* slot_acc = accs + ((size_t)(item * kMmaConsumers + cw) * 32 + lane) * NOCT * 4;
