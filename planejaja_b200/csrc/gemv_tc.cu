@@ -1,5 +1,5 @@
 // gemv_tc.cu -- batched decode GEMV (M = 2..16 tokens) on 5th-generation
-// tensor cores (tcgen05), for the K-quant formats Q4_K and Q6_K (ggml layout).
+// tensor cores (tcgen05), for Q4_K, Q6_K (ggml layout), Q4_0 and Q8_0.
 //
 //   y[m, n] = sum_k x[m, k] * W[n, k],   x f32 [M x K], W GGUF blocks [N x K]
 //
@@ -9,11 +9,15 @@
 //
 //   Q4_K  w = d * sc_j * q - dmin * m_j       A = sc_j * q        (<= 945)
 //   Q6_K  w = d * sc_j * (q - 32)             A = sc_j * (q - 32) (|A| <= 4096)
+//   Q4_0  w = d_b * (q - 8)                   A = fp16(d_b * (q - 8))
+//   Q8_0  w = d_b * s                         A = fp16(d_b * s)
 //
 // A is fp16: Q4_K's products are integers below 2048 and exact; Q6_K's are
 // exact up to 2048 in magnitude (every product the quantizer here writes)
 // and above that rounded to the nearest even integer (relative error at most
-// 2^-12 on those weights).  x enters as two fp16 operands, hi = fp16(x') and
+// 2^-12 on those weights).  Q4_0 and Q8_0 carry their per-32 block scale in
+// A, rounded once to fp16 (relative error at most 2^-11 per weight; the
+// epilogue factor is 1).  x enters as two fp16 operands, hi = fp16(x') and
 // lo = fp16(x' - hi), where x' = x * 2^-e_{m,s} with one power of two per
 // token and super-block chosen so that |x'| < 2^15: hi + lo carries 22 bits.
 // One MMA with N = 32 takes both (the hi and lo tiles are adjacent rows of
@@ -75,7 +79,7 @@ constexpr int TC_GMAX = 256;                 // most CTAs a launch uses
 constexpr int TC_TMEM_COLS = TC_NACC * TC_ACC_COLS;
 constexpr int TC_SMEM_LIMIT = 232448;
 
-enum : int { kTcQ4K = 0, kTcQ6KG = 1, kTcMixed = -1 };
+enum : int { kTcQ4K = 0, kTcQ6KG = 1, kTcQ40 = 2, kTcQ80 = 3, kTcMixed = -1 };
 
 struct TcSeg {
   const uint8_t* w;
@@ -258,6 +262,62 @@ __device__ __forceinline__ void q6k_pair(const uint8_t* raw, int q, int p, uint3
     } else {
       c0.z = a01; c0.w = a23; c1.z = b01; c1.w = b23;
     }
+  }
+}
+
+// Q4_0 / Q8_0 stage q: blocks 2q and 2q + 1 of the 256-weight column, whose
+// scale d (fp16) is folded into the operand: A = fp16(d * (q - 8)) or
+// fp16(d * s).  The magic 1024 + byte less 1032 (Q4_0) or 1152 (Q8_0, the
+// int8 as byte s + 128) is q - 8 or s exactly, and one multiply by d rounds
+// once (relative error at most 2^-11 per weight, as for any fp16 weight).
+// The column starts 16-byte aligned and blocks are 18 / 34 bytes, so block
+// 2q's quants sit 2 bytes past a word boundary and block 2q + 1's are aligned.
+// Chunk k8 holds K 8 k8 .. 8 k8 + 7 of the stage.
+__device__ __forceinline__ uint32_t q_half2(uint32_t bytes, uint32_t sel, __half2 off, __half2 d) {
+  return h2_bits(__hmul2(__hadd2(magic2(bytes, 0x64646464u, sel), off), d));
+}
+__device__ __forceinline__ uint4 q_chunk(uint32_t w0, uint32_t w1, __half2 off, __half2 d) {
+  return make_uint4(q_half2(w0, 0x4140, off, d), q_half2(w0, 0x4342, off, d), q_half2(w1, 0x4140, off, d),
+                    q_half2(w1, 0x4342, off, d));
+}
+__device__ __forceinline__ void q40_stage(const uint8_t* raw, int q, uint4 (&ch)[8]) {
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(raw + 36 * q);
+  uint32_t v[9];
+#pragma unroll
+  for (int i = 0; i < 9; ++i) v[i] = w[i];
+  const __half2 off = __float2half2_rn(-1032.f);
+  // block 2q: d in bytes 0..1, quants 2..17; block 2q + 1: d in 18..19, quants 20..35
+  const __half2 dA = __half2half2(__ushort_as_half((unsigned short)(v[0] & 0xFFFFu)));
+  const __half2 dB = __half2half2(__ushort_as_half((unsigned short)(v[4] >> 16)));
+  uint32_t qa[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) qa[i] = __byte_perm(v[i], v[i + 1], 0x5432);
+  const uint32_t L = 0x0F0F0F0Fu;
+  ch[0] = q_chunk(qa[0] & L, qa[1] & L, off, dA);                // weights 0..7: low nibbles of quants 0..7
+  ch[1] = q_chunk(qa[2] & L, qa[3] & L, off, dA);                // 8..15
+  ch[2] = q_chunk((qa[0] >> 4) & L, (qa[1] >> 4) & L, off, dA);  // 16..23: high nibbles of quants 0..7
+  ch[3] = q_chunk((qa[2] >> 4) & L, (qa[3] >> 4) & L, off, dA);  // 24..31
+  ch[4] = q_chunk(v[5] & L, v[6] & L, off, dB);
+  ch[5] = q_chunk(v[7] & L, v[8] & L, off, dB);
+  ch[6] = q_chunk((v[5] >> 4) & L, (v[6] >> 4) & L, off, dB);
+  ch[7] = q_chunk((v[7] >> 4) & L, (v[8] >> 4) & L, off, dB);
+}
+__device__ __forceinline__ void q80_stage(const uint8_t* raw, int q, uint4 (&ch)[8]) {
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(raw + 68 * q);
+  uint32_t v[17];
+#pragma unroll
+  for (int i = 0; i < 17; ++i) v[i] = w[i];
+  const __half2 off = __float2half2_rn(-1152.f);
+  const uint32_t F = 0x80808080u;  // int8 s -> byte s + 128
+  // block 2q: d in bytes 0..1, quants 2..33; block 2q + 1: d in 34..35, quants 36..67
+  const __half2 dA = __half2half2(__ushort_as_half((unsigned short)(v[0] & 0xFFFFu)));
+  const __half2 dB = __half2half2(__ushort_as_half((unsigned short)(v[8] >> 16)));
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t a0 = __byte_perm(v[2 * k], v[2 * k + 1], 0x5432) ^ F;
+    const uint32_t a1 = __byte_perm(v[2 * k + 1], v[2 * k + 2], 0x5432) ^ F;
+    ch[k] = q_chunk(a0, a1, off, dA);
+    ch[4 + k] = q_chunk(v[9 + 2 * k] ^ F, v[10 + 2 * k] ^ F, off, dB);
   }
 }
 
@@ -521,11 +581,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
           const __half2 b1 = __half2half2(__hmul(h1, __float2half_rn(-1024.f)));
 #pragma unroll
           for (int pp = 0; pp < 4; ++pp) q4k_pair(raw, q, pp, s0, b0, s1, b1, ch[pp], ch[pp + 4]);
-        } else {
+        } else if (code == kTcQ6KG) {
           *reinterpret_cast<uint32_t*>(a2row + ((a2c ^ sw) << 4) + 4 * q) = 0u;
           if (q == 0) dsc[a * TC_BM + row] = make_float2(h2f((uint16_t)ld_u16(raw + 208)), 0.f);
 #pragma unroll
           for (int pp = 0; pp < 4; ++pp) q6k_pair(raw, q, pp, 4 * (q & 1), ch[pp], ch[pp + 4], off16);
+        } else {
+          // Q4_0 / Q8_0: the block scales are in A, no min term
+          *reinterpret_cast<uint32_t*>(a2row + ((a2c ^ sw) << 4) + 4 * q) = 0u;
+          if (q == 0) dsc[a * TC_BM + row] = make_float2(1.0f, 0.f);
+          if (code == kTcQ40) q40_stage(raw, q, ch);
+          else q80_stage(raw, q, ch);
         }
         if (q == 1) *reinterpret_cast<uint4*>(a2row + (((a2c + 1) ^ sw) << 4)) = make_uint4(0, 0, 0, 0);
         // the unit slot is free once the MMAs of its previous unit have completed
@@ -681,16 +747,18 @@ static PFN_cuTensorMapEncodeTiled_v12000 tc_encode_fn() {
 static int tc_code(int type, int layout) {
   if (type == NSQ_TYPE_Q4_K) return kTcQ4K;
   if (type == NSQ_TYPE_Q6_K && layout == NSQ_Q6K_GGML) return kTcQ6KG;
+  if (type == NSQ_TYPE_Q4_0) return kTcQ40;
+  if (type == NSQ_TYPE_Q8_0) return kTcQ80;
   return -2;
 }
 
-// True if the batched tensor-core path covers these segments: Q4_K or ggml
-// Q6_K, K % 256 == 0, whole 16-byte rows, M in [2, 16].
+// True if the batched tensor-core path covers these segments: Q4_K, ggml
+// Q6_K, Q4_0 or Q8_0, K % 256 == 0, whole 16-byte rows, M in [2, 16].
 bool tc_covers(const nsq_segment* segs, int nseg, int64_t M, int64_t K) {
   if (M < 2 || M > TC_BN || K % 256 || K <= 0 || nseg < 1 || nseg > NSQ_MAX_SEGMENTS) return false;
   for (int i = 0; i < nseg; ++i) {
     if (tc_code(segs[i].ggml_type, segs[i].q6k_layout) < -1) return false;
-    const int64_t rb = (K / 256) * nsq_block_bytes(segs[i].ggml_type);
+    const int64_t rb = K / nsq_block_weights(segs[i].ggml_type) * nsq_block_bytes(segs[i].ggml_type);
     if (rb % 16 || segs[i].N > 0x7FFFFFFF) return false;
   }
   return true;
@@ -738,7 +806,8 @@ int run_gemv_tc(const nsq_segment* segs, int nseg, const float* x, int64_t M, in
   for (int i = 0; i < nseg; ++i) {
     TcSeg& s = p.seg[i];
     s.code = tc_code(segs[i].ggml_type, segs[i].q6k_layout);
-    s.CB = (int)nsq_block_bytes(segs[i].ggml_type);
+    // bytes of one 256-weight column: one K-quant super-block, 8 Q4_0 / Q8_0 blocks
+    s.CB = (int)(nsq_block_bytes(segs[i].ggml_type) * (256 / nsq_block_weights(segs[i].ggml_type)));
     s.w = static_cast<const uint8_t*>(segs[i].w);
     s.y = segs[i].y;
     s.N = segs[i].N;
@@ -746,7 +815,8 @@ int run_gemv_tc(const nsq_segment* segs, int nseg, const float* x, int64_t M, in
     s.tile0 = tiles;
     tiles += (int)((s.N + TC_BM - 1) / TC_BM);
     code = (i == 0 || code == s.code) ? s.code : kTcMixed;
-    if (s.code == kTcQ6KG) pitch = 240;  // 210-byte columns start on any even offset
+    if (s.code == kTcQ6KG && pitch < 240) pitch = 240;  // 210-byte columns start on any even offset
+    if (s.code == kTcQ80) pitch = 272;                   // 272-byte columns, 16-byte aligned
   }
   for (int i = 0; i < nseg; ++i) {
     cuuint64_t dims[2] = {(cuuint64_t)(p.seg[i].RB / 2), (cuuint64_t)p.seg[i].N};
@@ -811,6 +881,8 @@ int run_gemv_tc(const nsq_segment* segs, int nseg, const float* x, int64_t M, in
   switch (code) {
     case kTcQ4K: e = launch_tc<kTcQ4K>(p, G, smem, st); break;
     case kTcQ6KG: e = launch_tc<kTcQ6KG>(p, G, smem, st); break;
+    case kTcQ40: e = launch_tc<kTcQ40>(p, G, smem, st); break;
+    case kTcQ80: e = launch_tc<kTcQ80>(p, G, smem, st); break;
     default: e = launch_tc<kTcMixed>(p, G, smem, st); break;
   }
   return e == cudaSuccess ? NSQ_OK : NSQ_ERR_CUDA;
