@@ -1,5 +1,5 @@
 // gemv_tc.cu -- batched decode GEMV (M = 2..16 tokens) on 5th-generation
-// tensor cores (tcgen05), for Q4_K, Q6_K (ggml layout), Q4_0 and Q8_0.
+// tensor cores (tcgen05), for Q4_K, Q6_K (ggml and NodeStor layouts), Q4_0 and Q8_0.
 //
 //   y[m, n] = sum_k x[m, k] * W[n, k],   x f32 [M x K], W GGUF blocks [N x K]
 //
@@ -79,7 +79,7 @@ constexpr int TC_GMAX = 256;                 // most CTAs a launch uses
 constexpr int TC_TMEM_COLS = TC_NACC * TC_ACC_COLS;
 constexpr int TC_SMEM_LIMIT = 232448;
 
-enum : int { kTcQ4K = 0, kTcQ6KG = 1, kTcQ40 = 2, kTcQ80 = 3, kTcMixed = -1 };
+enum : int { kTcQ4K = 0, kTcQ6KG = 1, kTcQ40 = 2, kTcQ80 = 3, kTcQ6KN = 4, kTcMixed = -1 };
 
 struct TcSeg {
   const uint8_t* w;
@@ -318,6 +318,40 @@ __device__ __forceinline__ void q80_stage(const uint8_t* raw, int q, uint4 (&ch)
     const uint32_t a1 = __byte_perm(v[2 * k + 1], v[2 * k + 2], 0x5432) ^ F;
     ch[k] = q_chunk(a0, a1, off, dA);
     ch[4 + k] = q_chunk(v[9 + 2 * k] ^ F, v[10 + 2 * k] ^ F, off, dB);
+  }
+}
+
+// Q6_K, NodeStor layout (dequant_q6k.comp:50-99), stage q = elements
+// 64q .. 64q + 63: element i is nibble (i & 1) of ql[i >> 1], bits 2(i & 3) of
+// qh[128 + (i >> 2)], scale (b[192 + (i >> 4)] - 128) / 64, d at 208.  With
+// sc = b - 128, A = sc * (q - 32) as for the ggml layout (the same fp16
+// magic and one hfma2), and the epilogue factor is d / 64.  `raw` is 2-byte
+// aligned (210-byte columns).
+__device__ __forceinline__ void q6kn_stage(const uint8_t* raw, int q, uint4 (&ch)[8]) {
+  uint32_t ql[8], qh[4], scw[1];
+  ld_words_unaligned<8>(raw + 32 * q, ql);
+  ld_words_unaligned<4>(raw + 128 + 16 * q, qh);
+  ld_words_unaligned<1>(raw + 192 + 4 * q, scw);
+  const uint32_t K54 = 0x54545454u;
+#pragma unroll
+  for (int k8 = 0; k8 < 8; ++k8) {
+    const int sc = (int)((scw[0] >> (8 * (k8 >> 1))) & 0xFF) - 128;
+    const __half2 s4 = __half2half2(__int2half_rn(4 * sc)), c = __half2half2(__int2half_rn(-288 * sc));
+    const uint32_t h16 = (qh[k8 >> 1] >> (16 * (k8 & 1))) & 0xFFFFu;
+    uint32_t b4[2];
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      // elements 4hh .. 4hh + 3 of the chunk: low nibbles spread to bytes, high bits beside them
+      const uint32_t tt = __byte_perm(ql[k8] >> (16 * hh), 0, 0x1100);
+      const uint32_t lo4 = (tt & 0x000F000Fu) | ((tt >> 4) & 0x0F000F00u);
+      const uint32_t h = (h16 >> (8 * hh)) & 0xFFu;
+      const uint32_t hi2 = (h | (h << 6) | (h << 12) | (h << 18)) & 0x03030303u;
+      b4[hh] = (lo4 | (hi2 << 4)) << 2;  // 4q as bytes
+    }
+    ch[k8] = make_uint4(h2_bits(__hfma2(magic2(b4[0], K54, 0x4140), s4, c)),
+                        h2_bits(__hfma2(magic2(b4[0], K54, 0x4342), s4, c)),
+                        h2_bits(__hfma2(magic2(b4[1], K54, 0x4140), s4, c)),
+                        h2_bits(__hfma2(magic2(b4[1], K54, 0x4342), s4, c)));
   }
 }
 
@@ -586,6 +620,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
           if (q == 0) dsc[a * TC_BM + row] = make_float2(h2f((uint16_t)ld_u16(raw + 208)), 0.f);
 #pragma unroll
           for (int pp = 0; pp < 4; ++pp) q6k_pair(raw, q, pp, 4 * (q & 1), ch[pp], ch[pp + 4], off16);
+        } else if (code == kTcQ6KN) {
+          *reinterpret_cast<uint32_t*>(a2row + ((a2c ^ sw) << 4) + 4 * q) = 0u;
+          if (q == 0) dsc[a * TC_BM + row] = make_float2(h2f((uint16_t)ld_u16(raw + 208)) * 0.015625f, 0.f);
+          q6kn_stage(raw, q, ch);
         } else {
           // Q4_0 / Q8_0: the block scales are in A, no min term
           *reinterpret_cast<uint32_t*>(a2row + ((a2c ^ sw) << 4) + 4 * q) = 0u;
@@ -747,13 +785,14 @@ static PFN_cuTensorMapEncodeTiled_v12000 tc_encode_fn() {
 static int tc_code(int type, int layout) {
   if (type == NSQ_TYPE_Q4_K) return kTcQ4K;
   if (type == NSQ_TYPE_Q6_K && layout == NSQ_Q6K_GGML) return kTcQ6KG;
+  if (type == NSQ_TYPE_Q6_K && layout == NSQ_Q6K_NODESTOR) return kTcQ6KN;
   if (type == NSQ_TYPE_Q4_0) return kTcQ40;
   if (type == NSQ_TYPE_Q8_0) return kTcQ80;
   return -2;
 }
 
-// True if the batched tensor-core path covers these segments: Q4_K, ggml
-// Q6_K, Q4_0 or Q8_0, K % 256 == 0, whole 16-byte rows, M in [2, 16].
+// True if the batched tensor-core path covers these segments: Q4_K, Q6_K
+// (both layouts), Q4_0 or Q8_0, K % 256 == 0, whole 16-byte rows, M in [2, 16].
 bool tc_covers(const nsq_segment* segs, int nseg, int64_t M, int64_t K) {
   if (M < 2 || M > TC_BN || K % 256 || K <= 0 || nseg < 1 || nseg > NSQ_MAX_SEGMENTS) return false;
   for (int i = 0; i < nseg; ++i) {
@@ -815,7 +854,7 @@ int run_gemv_tc(const nsq_segment* segs, int nseg, const float* x, int64_t M, in
     s.tile0 = tiles;
     tiles += (int)((s.N + TC_BM - 1) / TC_BM);
     code = (i == 0 || code == s.code) ? s.code : kTcMixed;
-    if (s.code == kTcQ6KG && pitch < 240) pitch = 240;  // 210-byte columns start on any even offset
+    if ((s.code == kTcQ6KG || s.code == kTcQ6KN) && pitch < 240) pitch = 240;  // 210-byte columns, any even offset
     if (s.code == kTcQ80) pitch = 272;                   // 272-byte columns, 16-byte aligned
   }
   for (int i = 0; i < nseg; ++i) {
@@ -883,6 +922,7 @@ int run_gemv_tc(const nsq_segment* segs, int nseg, const float* x, int64_t M, in
     case kTcQ6KG: e = launch_tc<kTcQ6KG>(p, G, smem, st); break;
     case kTcQ40: e = launch_tc<kTcQ40>(p, G, smem, st); break;
     case kTcQ80: e = launch_tc<kTcQ80>(p, G, smem, st); break;
+    case kTcQ6KN: e = launch_tc<kTcQ6KN>(p, G, smem, st); break;
     default: e = launch_tc<kTcMixed>(p, G, smem, st); break;
   }
   return e == cudaSuccess ? NSQ_OK : NSQ_ERR_CUDA;
