@@ -1,5 +1,6 @@
 // gemv_tc.cu -- batched decode GEMV (M = 2..16 tokens) on 5th-generation
-// tensor cores (tcgen05), for Q4_K, Q6_K (ggml and NodeStor layouts), Q4_0 and Q8_0.
+// tensor cores (tcgen05), for Q4_K, Q5_K and Q6_K (ggml and NodeStor layouts),
+// Q4_0 and Q8_0.
 //
 //   y[m, n] = sum_k x[m, k] * W[n, k],   x f32 [M x K], W GGUF blocks [N x K]
 //
@@ -8,7 +9,9 @@
 // of once per scale group (the cost that bounds an integer-MMA design):
 //
 //   Q4_K  w = d * sc_j * q - dmin * m_j       A = sc_j * q        (<= 945)
+//   Q5_K  the same with 5-bit q               A = sc_j * q        (<= 1953)
 //   Q6_K  w = d * sc_j * (q - 32)             A = sc_j * (q - 32) (|A| <= 4096)
+//         (NodeStor layout: sc_j = b_j - 128 and d / 64 in the epilogue)
 //   Q4_0  w = d_b * (q - 8)                   A = fp16(d_b * (q - 8))
 //   Q8_0  w = d_b * s                         A = fp16(d_b * s)
 //
@@ -79,7 +82,7 @@ constexpr int TC_GMAX = 256;                 // most CTAs a launch uses
 constexpr int TC_TMEM_COLS = TC_NACC * TC_ACC_COLS;
 constexpr int TC_SMEM_LIMIT = 232448;
 
-enum : int { kTcQ4K = 0, kTcQ6KG = 1, kTcQ40 = 2, kTcQ80 = 3, kTcQ6KN = 4, kTcMixed = -1 };
+enum : int { kTcQ4K = 0, kTcQ6KG = 1, kTcQ40 = 2, kTcQ80 = 3, kTcQ6KN = 4, kTcQ5KG = 5, kTcQ5KN = 6, kTcMixed = -1 };
 
 struct TcSeg {
   const uint8_t* w;
@@ -210,6 +213,40 @@ __device__ __forceinline__ void q4k_pair(const uint8_t* raw, int q, int p, __hal
   const uint32_t H0 = (w.x >> 4) & 0x0F0F0F0Fu, H1 = (w.y >> 4) & 0x0F0F0F0Fu;
   const uint32_t K64 = 0x64646464u;
   // (1024 + q) * sc - 1024 * sc = sc * q exactly (one rounding of an integer <= 945)
+  lo_chunk.x = h2_bits(__hfma2(magic2(L0, K64, 0x4140), s0, b0));
+  lo_chunk.y = h2_bits(__hfma2(magic2(L0, K64, 0x4342), s0, b0));
+  lo_chunk.z = h2_bits(__hfma2(magic2(L1, K64, 0x4140), s0, b0));
+  lo_chunk.w = h2_bits(__hfma2(magic2(L1, K64, 0x4342), s0, b0));
+  hi_chunk.x = h2_bits(__hfma2(magic2(H0, K64, 0x4140), s1, b1));
+  hi_chunk.y = h2_bits(__hfma2(magic2(H0, K64, 0x4342), s1, b1));
+  hi_chunk.z = h2_bits(__hfma2(magic2(H1, K64, 0x4140), s1, b1));
+  hi_chunk.w = h2_bits(__hfma2(magic2(H1, K64, 0x4342), s1, b1));
+}
+
+// Q5_K stage q, pair p: Q4_K's nibbles (qs at byte 48) widened by the fifth
+// bit of each weight -- ggml: bit j of qh[l]; NodeStor (q5_k.rs:57-70): bit
+// l % 8 of qh[8 (j >> 1) + 4 (j & 1) + l / 8] (qh at byte 16) -- so that
+// A = sc * q (at most 63 * 31 = 1953) stays exact in fp16.
+template <bool NODESTOR>
+__device__ __forceinline__ void q5k_pair(const uint8_t* raw, int q, int p, __half2 s0, __half2 b0, __half2 s1,
+                                         __half2 b1, uint4& lo_chunk, uint4& hi_chunk) {
+  const uint2 w = *reinterpret_cast<const uint2*>(raw + 48 + 32 * q + 8 * p);
+  uint32_t L0 = w.x & 0x0F0F0F0Fu, L1 = w.y & 0x0F0F0F0Fu;
+  uint32_t H0 = (w.x >> 4) & 0x0F0F0F0Fu, H1 = (w.y >> 4) & 0x0F0F0F0Fu;
+  if constexpr (NODESTOR) {
+    const uint32_t bl = raw[16 + 8 * q + p], bh = raw[16 + 8 * q + 4 + p];
+    L0 |= spread4(bl & 0xF) << 4;
+    L1 |= spread4(bl >> 4) << 4;
+    H0 |= spread4(bh & 0xF) << 4;
+    H1 |= spread4(bh >> 4) << 4;
+  } else {
+    const uint2 hq = *reinterpret_cast<const uint2*>(raw + 16 + 8 * p);
+    L0 |= ((hq.x >> (2 * q)) & 0x01010101u) << 4;
+    L1 |= ((hq.y >> (2 * q)) & 0x01010101u) << 4;
+    H0 |= ((hq.x >> (2 * q + 1)) & 0x01010101u) << 4;
+    H1 |= ((hq.y >> (2 * q + 1)) & 0x01010101u) << 4;
+  }
+  const uint32_t K64 = 0x64646464u;
   lo_chunk.x = h2_bits(__hfma2(magic2(L0, K64, 0x4140), s0, b0));
   lo_chunk.y = h2_bits(__hfma2(magic2(L0, K64, 0x4342), s0, b0));
   lo_chunk.z = h2_bits(__hfma2(magic2(L1, K64, 0x4140), s0, b0));
@@ -599,7 +636,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
         const uint8_t* raw = raw_sm + rs * RAW_BYTES + row * PITCH + off16;
         uint8_t* a2row = a2_sm + row * 128;
         uint4 ch[8];
-        if (code == kTcQ4K) {
+        if (code == kTcQ4K || code == kTcQ5KG || code == kTcQ5KN) {
+          // Q4_K and Q5_K share the header: d, dmin, the packed 6-bit scales and mins
           const uint4 hdr = *reinterpret_cast<const uint4*>(raw);
           const uint32_t sm0 = q4k_scale_min(hdr.y, hdr.z, hdr.w, 2 * q);
           const uint32_t sm1 = q4k_scale_min(hdr.y, hdr.z, hdr.w, 2 * q + 1);
@@ -613,8 +651,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
           const __half2 s0 = __half2half2(h0), s1 = __half2half2(h1);
           const __half2 b0 = __half2half2(__hmul(h0, __float2half_rn(-1024.f)));
           const __half2 b1 = __half2half2(__hmul(h1, __float2half_rn(-1024.f)));
+          if (code == kTcQ4K) {
 #pragma unroll
-          for (int pp = 0; pp < 4; ++pp) q4k_pair(raw, q, pp, s0, b0, s1, b1, ch[pp], ch[pp + 4]);
+            for (int pp = 0; pp < 4; ++pp) q4k_pair(raw, q, pp, s0, b0, s1, b1, ch[pp], ch[pp + 4]);
+          } else if (code == kTcQ5KG) {
+#pragma unroll
+            for (int pp = 0; pp < 4; ++pp) q5k_pair<false>(raw, q, pp, s0, b0, s1, b1, ch[pp], ch[pp + 4]);
+          } else {
+#pragma unroll
+            for (int pp = 0; pp < 4; ++pp) q5k_pair<true>(raw, q, pp, s0, b0, s1, b1, ch[pp], ch[pp + 4]);
+          }
         } else if (code == kTcQ6KG) {
           *reinterpret_cast<uint32_t*>(a2row + ((a2c ^ sw) << 4) + 4 * q) = 0u;
           if (q == 0) dsc[a * TC_BM + row] = make_float2(h2f((uint16_t)ld_u16(raw + 208)), 0.f);
@@ -786,13 +832,15 @@ static int tc_code(int type, int layout) {
   if (type == NSQ_TYPE_Q4_K) return kTcQ4K;
   if (type == NSQ_TYPE_Q6_K && layout == NSQ_Q6K_GGML) return kTcQ6KG;
   if (type == NSQ_TYPE_Q6_K && layout == NSQ_Q6K_NODESTOR) return kTcQ6KN;
+  if (type == NSQ_TYPE_Q5_K) return layout == NSQ_Q6K_NODESTOR ? kTcQ5KN : kTcQ5KG;
   if (type == NSQ_TYPE_Q4_0) return kTcQ40;
   if (type == NSQ_TYPE_Q8_0) return kTcQ80;
   return -2;
 }
 
-// True if the batched tensor-core path covers these segments: Q4_K, Q6_K
-// (both layouts), Q4_0 or Q8_0, K % 256 == 0, whole 16-byte rows, M in [2, 16].
+// True if the batched tensor-core path covers these segments: Q4_K, Q5_K and
+// Q6_K (both layouts), Q4_0 or Q8_0, K % 256 == 0, whole 16-byte rows, M in
+// [2, 16].
 bool tc_covers(const nsq_segment* segs, int nseg, int64_t M, int64_t K) {
   if (M < 2 || M > TC_BN || K % 256 || K <= 0 || nseg < 1 || nseg > NSQ_MAX_SEGMENTS) return false;
   for (int i = 0; i < nseg; ++i) {
@@ -856,6 +904,7 @@ int run_gemv_tc(const nsq_segment* segs, int nseg, const float* x, int64_t M, in
     code = (i == 0 || code == s.code) ? s.code : kTcMixed;
     if ((s.code == kTcQ6KG || s.code == kTcQ6KN) && pitch < 240) pitch = 240;  // 210-byte columns, any even offset
     if (s.code == kTcQ80) pitch = 272;                   // 272-byte columns, 16-byte aligned
+    if ((s.code == kTcQ5KG || s.code == kTcQ5KN) && pitch < 176) pitch = 176;  // 176-byte columns, aligned
   }
   for (int i = 0; i < nseg; ++i) {
     cuuint64_t dims[2] = {(cuuint64_t)(p.seg[i].RB / 2), (cuuint64_t)p.seg[i].N};
@@ -923,6 +972,8 @@ int run_gemv_tc(const nsq_segment* segs, int nseg, const float* x, int64_t M, in
     case kTcQ40: e = launch_tc<kTcQ40>(p, G, smem, st); break;
     case kTcQ80: e = launch_tc<kTcQ80>(p, G, smem, st); break;
     case kTcQ6KN: e = launch_tc<kTcQ6KN>(p, G, smem, st); break;
+    case kTcQ5KG: e = launch_tc<kTcQ5KG>(p, G, smem, st); break;
+    case kTcQ5KN: e = launch_tc<kTcQ5KN>(p, G, smem, st); break;
     default: e = launch_tc<kTcMixed>(p, G, smem, st); break;
   }
   return e == cudaSuccess ? NSQ_OK : NSQ_ERR_CUDA;
