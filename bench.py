@@ -478,18 +478,16 @@ class DecodeStep:
     def step(self):
         import torch
         st = torch.cuda.current_stream(self.ctx.dev).cuda_stream
-        n = 0
+        k0 = self.ctx.lib.nsq_kernel_launches()  # libnsq's own kernels (NCCL's are not counted)
         for li in range(self.L):
             for gi, (a, names, arr) in enumerate(self.calls[li]):
                 self.launch(li, gi, st)
-                n += 1
                 if self.mode == "nccl":
                     for nm in names:
                         self._dist.all_gather_into_tensor(self.outs_full[li][nm], self.outs_local[li][nm])
         if self.mode == "p2p":
             self.exchange.wait(st)  # the step ends when every rank's rows have landed here
-            n += 1
-        self.n_launch = n
+        self.n_launch = self.ctx.lib.nsq_kernel_launches() - k0
 
     def run(self):
         if self.graph is not None:

@@ -76,6 +76,11 @@ int nsq_version(void);
  * the reference, which has no such switches. */
 void nsq_reload_tuning(void);
 
+/* Number of kernels this library has launched since it was loaded (a launch
+ * captured into a CUDA graph counts once, at capture).  For benchmarks that
+ * report how many kernels a step runs; no counterpart in the reference. */
+uint64_t nsq_kernel_launches(void);
+
 /* Text of a status code; static storage. */
 const char *nsq_strerror(int status);
 

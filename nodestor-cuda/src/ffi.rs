@@ -59,6 +59,7 @@ pub struct NsqComm {
 extern "C" {
     pub fn nsq_version() -> c_int;
     pub fn nsq_reload_tuning();
+    pub fn nsq_kernel_launches() -> u64;
     pub fn nsq_strerror(status: c_int) -> *const c_char;
     pub fn nsq_block_bytes(ggml_type: c_int) -> i64;
     pub fn nsq_block_weights(ggml_type: c_int) -> i64;

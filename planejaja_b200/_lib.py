@@ -37,6 +37,7 @@ _vp, _i64, _int, _sz = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_s
 SIGNATURES = [
     ("nsq_version", _int, []),
     ("nsq_reload_tuning", None, []),
+    ("nsq_kernel_launches", ctypes.c_uint64, []),
     ("nsq_strerror", ctypes.c_char_p, [_int]),
     ("nsq_block_bytes", _i64, [_int]),
     ("nsq_block_weights", _i64, [_int]),

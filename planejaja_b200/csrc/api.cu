@@ -60,6 +60,9 @@ static void read_tuning() {
   }
 }
 
+std::atomic<uint64_t> g_launches{0};
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
 int tune(TuneId id, int dflt) {
   std::call_once(g_tune_once, read_tuning);
   return g_tune_set[id].load(std::memory_order_acquire) ? g_tune_val[id].load(std::memory_order_relaxed) : dflt;
@@ -130,6 +133,8 @@ void nsq_reload_tuning(void) {
   std::call_once(g_tune_once, read_tuning);
   read_tuning();
 }
+
+uint64_t nsq_kernel_launches(void) { return nsq::g_launches.load(std::memory_order_relaxed); }
 
 const char* nsq_strerror(int status) {
   switch (status) {

@@ -58,6 +58,7 @@ cudaError_t comm_launch_wait(const nsq_comm* c, cudaStream_t st) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  note_launch();
   return cudaLaunchKernelEx(&cfg, comm_wait_kernel, reinterpret_cast<const uint32_t*>(c->local), c->world, c->rank);
 }
 

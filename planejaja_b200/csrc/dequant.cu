@@ -118,6 +118,7 @@ static cudaError_t launch_dequant_t(const uint8_t* w, int layout, int out_dtype,
   const int64_t cap = (int64_t)num_sms * 8;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
+  note_launch();
   if (out_dtype == NSQ_OUT_F32)
     dequant_kernel<TYPE, float><<<(unsigned)blocks, threads, 0, st>>>(w, layout, (float*)out, n_groups);
   else

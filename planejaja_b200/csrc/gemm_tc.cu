@@ -723,6 +723,7 @@ static int launch_gemm_t(const void* x, const CUtensorMap& wmap, const GemmParam
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = S > 1 ? 1 : 0;
+  note_launch();
   return cudaLaunchKernelEx(&cfg, kern, map, wmap, p) == cudaSuccess ? NSQ_OK : NSQ_ERR_CUDA;
 }
 

@@ -508,6 +508,7 @@ static cudaError_t launch_gemv_inst(const GemvParams& p, int blocks, size_t smem
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) configured[dev] = smem;
   }
+  note_launch();
   kern<<<blocks, kGemvThreads, smem, st>>>(p);
   return cudaGetLastError();
 }
@@ -644,6 +645,7 @@ cudaError_t launch_prepare_x(const float* x, XGroup* xg, int64_t M, int64_t K, c
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  note_launch();
   return cudaLaunchKernelEx(&cfg, prepare_x_kernel, x, xg, total, K / 32);
 }
 

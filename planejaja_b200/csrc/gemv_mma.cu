@@ -746,6 +746,7 @@ static cudaError_t launch_mma(const MmaParams& p, int blocks, size_t smem, cudaS
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  note_launch();
   return cudaLaunchKernelEx(&cfg, kern, p);
 }
 

@@ -908,6 +908,7 @@ static cudaError_t launch_fused(const FusedParams& p, int blocks, size_t smem, c
       return static_cast<cudaError_t>(kNoRoom);
     }
   }
+  note_launch();
   return cudaLaunchKernelEx(&cfg, kern, p);
 }
 

@@ -877,6 +877,7 @@ static cudaError_t launch_tc(const TcParams& p, int blocks, size_t smem, cudaStr
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  note_launch();
   return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
@@ -961,6 +962,7 @@ int run_gemv_tc(const nsq_segment* segs, int nseg, const float* x, int64_t M, in
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    note_launch();
     if (cudaLaunchKernelEx(&cfg, tc_prep_kernel, x, (int)M, K, NSB, ws + 1024,
                            const_cast<uint8_t*>(p.ws_col), p.ws_cnt) != cudaSuccess)
       return NSQ_ERR_CUDA;

@@ -60,6 +60,7 @@ cudaError_t launch_matmul_f32(const float* a, const float* b, float* c, int64_t 
   const int64_t gx = (N + NT - 1) / NT, gy = (M + MT - 1) / MT;
   if (gy > 65535) return cudaErrorInvalidValue;
   dim3 grid((unsigned)gx, (unsigned)gy);
+  note_launch();
   matmul_f32_kernel<<<grid, 256, 0, st>>>(a, b, c, M, K, N);
   return cudaGetLastError();
 }

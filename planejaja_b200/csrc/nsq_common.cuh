@@ -274,5 +274,7 @@ enum TuneId : int {
   kTuneGemmTok, kTuneTcMinM, kTuneCount
 };
 int tune(TuneId id, int dflt);
+// Counts one kernel launch (nsq_kernel_launches).
+void note_launch();
 
 }  // namespace nsq

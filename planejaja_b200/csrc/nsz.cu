@@ -613,6 +613,7 @@ static int run_decode(const uint8_t* tiles, const uint32_t* off, int64_t count, 
   const int64_t ctas = imax64(1, imin64(occupancy_ctas(kern, smem, num_sms), (ntiles + 7) / 8));
   DecodeParams p{tiles, off, out, count, ntiles, (ntiles + ctas - 1) / ctas};
   const int64_t grid = (ntiles + p.per_cta - 1) / p.per_cta;
+  note_launch();
   kern<<<(unsigned)grid, kNszWarps * 32, smem, st>>>(p);
   return cudaGetLastError() == cudaSuccess ? NSQ_OK : NSQ_ERR_CUDA;
 }
@@ -633,6 +634,7 @@ static int launch_zip(ZipParams p, cudaStream_t st, int num_sms) {
   p.rpc = rpc;
   const int64_t grid = (p.N + rpc - 1) / rpc;
   const size_t smem = base + (size_t)MT * rpc * 4;
+  note_launch();
   kern<<<(unsigned)grid, kNszWarps * 32, smem, st>>>(p);
   return cudaGetLastError() == cudaSuccess ? NSQ_OK : NSQ_ERR_CUDA;
 }

@@ -404,3 +404,19 @@ def test_gemv_swiglu_rejects_mismatched_pairs(eng):
     x = torch.zeros(1, 300, device=eng.device)
     with pytest.raises(_lib.NsqError):  # K % 256
         eng.gemv_swiglu(wg, wu, Q4_K, x, 64, 300)
+
+
+def test_kernel_launch_counter(eng, tuning):
+    """nsq_kernel_launches counts the library's kernels: one fused launch for a
+    one-token GEMV prepared on chip, two (preparation + fused) when the
+    activations go through the workspace, two (tile preparation + tcgen05) for
+    16 tokens."""
+    tuning.set("NSQ_TC_MIN_M", "5")
+    lib = eng.lib
+    n = 256
+    for k, m, kernels in [(4096, 1, 1), (14336, 1, 2), (4096, 16, 2)]:
+        w = eng.upload(Q.synthetic_weights(n, k, Q4_K, seed=k))
+        x = torch.from_numpy(Q.synthetic_activations(m, k, seed=m)).to(eng.device)
+        before = lib.nsq_kernel_launches()
+        eng.gemv(w, Q4_K, x, n, k)
+        assert lib.nsq_kernel_launches() - before == kernels, (k, m)
