@@ -92,7 +92,7 @@ def test_dequant_empty(eng):
 def gemv_kernel(request, tuning):
     """Runs a test with each GEMV kernel: one lane per row (dp4a, every M),
     integer tensor cores (mma.sync, every M), the general kernel, and the
-    tcgen05 kernel (M >= 2, Q4_K and ggml Q6_K)."""
+    tcgen05 kernel (M >= 2, every format)."""
     tuning.unset("NSQ_GEMV_GENERAL")
     tuning.set("NSQ_TC_MIN_M", "17")
     if request.param == "general":
@@ -100,8 +100,7 @@ def gemv_kernel(request, tuning):
     elif request.param == "mma":
         tuning.set("NSQ_MMA_MIN_M", "1")
     elif request.param == "tc":
-        # tcgen05 path for M >= 2 over Q4_K / ggml Q6_K; the other formats
-        # (and M = 1) take the one-lane-per-row kernel
+        # tcgen05 path for M >= 2; M = 1 takes the one-lane-per-row kernel
         tuning.set("NSQ_TC_MIN_M", "2")
         tuning.set("NSQ_MMA_MIN_M", "17")
     else:

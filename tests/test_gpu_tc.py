@@ -1,4 +1,4 @@
-"""The tcgen05 batched decode GEMV (2..16 tokens, Q4_K and ggml Q6_K).
+"""The tcgen05 batched decode GEMV (2..16 tokens, every format and layout).
 
 Covered beside the parity suites (which run it as their "tc" kernel):
   * stream-K: shapes whose 128-row tiles are split over many CTAs, so most
@@ -91,3 +91,18 @@ def test_tc_mixed_segments(eng, oracle, m):
         ref = oracle.quant_matmul(np.concatenate([w[r * rb:(r + 1) * rb] for r in rows]), t, x, len(rows), k,
                                   threads=8)
         assert rel_err(y.cpu().numpy()[:, rows], ref) <= GEMV_TOL
+
+
+@pytest.mark.parametrize("m", [5, 16])
+def test_tc_every_format_in_one_launch(eng, oracle, m):
+    """Q4_0, Q8_0, NodeStor Q5_K and NodeStor Q6_K segments in one launch: the
+    mixed-format kernel with the widest raw column (Q8_0's 272 bytes)."""
+    from planejaja_b200.formats import Q4_0, Q8_0, Q5_K, Q6K_NODESTOR
+    k = 2048
+    specs = [(Q4_0, 0, 200), (Q8_0, 0, 72), (Q5_K, Q6K_NODESTOR, 64), (Q6_K, Q6K_NODESTOR, 40)]
+    ws = [Q.synthetic_weights(n, k, t, seed=40 + i, q6k_layout=l) for i, (t, l, n) in enumerate(specs)]
+    x = Q.synthetic_activations(m, k, seed=41)
+    outs = eng.gemv_multi([(eng.upload(w), t, n, l) for w, (t, l, n) in zip(ws, specs)],
+                          torch.from_numpy(x).to(eng.device), k)
+    for w, (t, l, n), y in zip(ws, specs, outs):
+        assert rel_err(y.cpu().numpy(), oracle.quant_matmul(w, t, x, n, k, l, threads=8)) <= GEMV_TOL
