@@ -33,7 +33,7 @@ bool tc_covers(const nsq_segment* segs, int nseg, int64_t M, int64_t K);
 int tc_min_m();
 size_t tc_workspace_bytes(int64_t K);
 int run_gemv_tc(const nsq_segment* segs, int nseg, const float* x, int64_t M, int64_t K, void* workspace,
-                cudaStream_t st, int num_sms);
+                cudaStream_t st, int num_sms, const XchgDesc* xd = nullptr);
 int run_gemm_bf16(const uint8_t* w, int type, int layout, const void* x, void* y, int64_t M, int64_t N, int64_t K,
                   cudaStream_t st, int num_sms);
 cudaError_t launch_matmul_f32(const float* a, const float* b, float* c, int64_t M, int64_t K, int64_t N,
@@ -420,6 +420,18 @@ int nsq_gemv_multi_xchg(const nsq_xsegment* segs, int nseg, const float* x, int6
       if (segs[i].row0 != 0 || segs[i].n_full != segs[i].N) return NSQ_ERR_SHAPE;  // one rank holds every row
       sl[i].y = reinterpret_cast<float*>(base + segs[i].y_off);
     }
+  }
+  if (!gemv_force_general() && M >= tc_min_m() && tc_covers(sl, nseg, M, K) && workspace &&
+      !(reinterpret_cast<uintptr_t>(workspace) & 15) && workspace_bytes >= tc_workspace_bytes(K)) {
+    // tcgen05 batched path with the exchange epilogue; every rank's previous
+    // exchange lands here before its tile-preparation kernel reads x
+    DevInfo di;
+    if ((rc = check_device(di))) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (xd.P > 1 && comm_launch_wait(comm, st) != cudaSuccess) return NSQ_ERR_CUDA;
+    xd.wait = false;
+    rc = run_gemv_tc(sl, nseg, x, M, K, workspace, st, di.num_sms, &xd);
+    if (rc != -1) return rc;
   }
   const bool mma = M >= gemv_mma_min_m() && gemv_mma_covers(sl, nseg, M, K);
   if (!mma && !fused_covers(sl, nseg, K)) return NSQ_ERR_SHAPE;

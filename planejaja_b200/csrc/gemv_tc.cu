@@ -103,6 +103,13 @@ struct TcParams {
   const uint8_t* ws_col;  // [NSB][B2 hi 2 KB | B2 lo 2 KB | 16 f32 scales | pad]
   float* ws_part;         // [2 * TC_GMAX][128 rows][16 tokens]
   uint32_t* ws_cnt;       // [TC_GMAX]
+  // Row-sharded exchange (P > 1), as in the fused kernel: every output row
+  // goes into the exchange buffer of each of the P ranks (segment s: y[M x
+  // xnfull] f32 at byte kXchgCtlBytes + xoff[s], this rank's rows from
+  // xrow0[s]), and the grid's last CTA publishes this rank's count.
+  int P, rank;
+  uint8_t* xbuf[NSQ_MAX_RANKS];
+  int64_t xrow0[NSQ_MAX_SEGMENTS], xnfull[NSQ_MAX_SEGMENTS], xoff[NSQ_MAX_SEGMENTS];
 };
 
 // Workspace of the batched path: counters, B tiles, min-term tiles, partials.
@@ -428,6 +435,17 @@ struct TcRing {
     }
   }
 };
+
+// Output y[m, nrow] of segment sg: to the segment's y, or (row-sharded
+// exchange) into every rank's exchange buffer.
+__device__ __forceinline__ void tc_store_y(const TcParams& p, const TcSeg& S, int sg, int m, int64_t nrow, float v) {
+  if (p.P > 1) {
+    const int64_t idx = (int64_t)m * p.xnfull[sg] + p.xrow0[sg] + nrow;
+    for (int pr = 0; pr < p.P; ++pr) reinterpret_cast<float*>(p.xbuf[pr] + kXchgCtlBytes + p.xoff[sg])[idx] = v;
+  } else {
+    S.y[(int64_t)m * S.N + nrow] = v;
+  }
+}
 
 // CTA index owning unit u (unit ranges [U i / G, U (i+1) / G)).
 __device__ __forceinline__ int tc_owner(int64_t u, int64_t U, int G) { return (int)(((u + 1) * G - 1) / U); }
@@ -756,7 +774,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
         if (row_ok && ok) {
 #pragma unroll
           for (int m = 0; m < TC_BN; ++m)
-            if (m < p.M) S.y[(int64_t)m * S.N + nrow] = acc[m];
+            if (m < p.M) tc_store_y(p, S, sg, m, nrow, acc[m]);
         }
       } else {
         // partial: slot 2i for the first segment of CTA i, 2i + 1 for its last
@@ -792,7 +810,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
           if (row_ok) {
 #pragma unroll
             for (int m = 0; m < TC_BN; ++m)
-              if (m < p.M) S.y[(int64_t)m * S.N + nrow] = sum[m];
+              if (m < p.M) tc_store_y(p, S, sg, m, nrow, sum[m]);
           }
           if (threadIdx.x == TC_EPI_WARP0 * 32) p.ws_cnt[i_first] = 0u;
         }
@@ -805,6 +823,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
   }
   tc_fence_before();
   __syncthreads();
+  if (p.P > 1 && threadIdx.x == 0) {
+    // Publish, as the fused kernel does: the fence orders this CTA's peer
+    // stores before its count; the grid's last CTA advances the exchange
+    // count and writes it to this rank's flag word in every buffer.
+    fence_acq_rel_gpu();
+    uint32_t* ctl = reinterpret_cast<uint32_t*>(p.xbuf[p.rank]);
+    if (atomicAdd(ctl + kXchgDone, 1u) == gridDim.x - 1) {
+      fence_acq_rel_gpu();
+      ctl[kXchgDone] = 0;
+      const uint32_t seq = ctl[kXchgSeq] + 1;
+      ctl[kXchgSeq] = seq;
+      for (int pr = 0; pr < p.P; ++pr) st_release_sys(reinterpret_cast<uint32_t*>(p.xbuf[pr]) + p.rank, seq);
+    }
+  }
   if (warp == 1) {
     // both issuers' final commits arrive once every MMA has completed
     mbar_wait_bounded(done, 0);
@@ -884,7 +916,7 @@ static cudaError_t launch_tc(const TcParams& p, int blocks, size_t smem, cudaStr
 // Batched decode GEMV; -1 if not covered.  workspace: tc_workspace_bytes(K)
 // bytes, 16-byte aligned.
 int run_gemv_tc(const nsq_segment* segs, int nseg, const float* x, int64_t M, int64_t K, void* workspace,
-                cudaStream_t st, int num_sms) {
+                cudaStream_t st, int num_sms, const XchgDesc* xd) {
   if (!tc_covers(segs, nseg, M, K)) return -1;
   auto enc = tc_encode_fn();
   if (!enc) return -1;
@@ -918,6 +950,17 @@ int run_gemv_tc(const nsq_segment* segs, int nseg, const float* x, int64_t M, in
       return -1;
   }
   p.nseg = nseg;
+  p.P = 1;
+  if (xd && xd->P > 1) {
+    p.P = xd->P;
+    p.rank = xd->rank;
+    for (int r = 0; r < xd->P; ++r) p.xbuf[r] = xd->buf[r];
+    for (int i = 0; i < nseg; ++i) {
+      p.xrow0[i] = xd->row0[i];
+      p.xnfull[i] = xd->nfull[i];
+      p.xoff[i] = xd->off[i];
+    }
+  }
   p.T = tiles;
   p.NSB = NSB;
   p.M = (int)M;

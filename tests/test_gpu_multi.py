@@ -2,7 +2,8 @@
 
 Each rank (one process per GPU) holds a row slice of every matrix; the
 exchange kernel stores its rows into both ranks' buffers over NVLink and the
-flag protocol orders consecutive exchanges.  Both ranks must end with the
+flag protocol orders consecutive exchanges (the fused dp4a kernel for 1..2
+tokens, the tcgen05 kernel for 6..16).  Both ranks must end with the
 same full outputs, within the GEMV tolerance of the oracle on the full
 matrices.  A second test lets one rank skip an exchange: the other rank's
 bounded wait must give up and report NSQ_ERR_TIMEOUT (no fault, no hang).
@@ -30,6 +31,8 @@ CASES = [
     ("down", 512, 14336, Q6_K, 1, "down"),
     ("down_m2", 512, 14336, Q6_K, 2, "down_m2"),
     ("q40_m6", 512, 2048, Q4_0, 6, "q40_m6"),
+    ("gate_m16", 512, 4096, Q4_K, 16, "gu_m16"), ("up_m16", 512, 4096, Q4_K, 16, "gu_m16"),
+    ("down_m8", 384, 8192, Q6_K, 8, "down_m8"),
     ("q", 512, 2048, Q4_K, 1, "qkv"), ("k", 128, 2048, Q4_K, 1, "qkv"), ("v", 128, 2048, Q6_K, 1, "qkv"),
 ]
 
@@ -71,7 +74,8 @@ def _worker(rank, world, port, out_dir, skip_one):
             groups.setdefault(g, {"k": k, "m": m, "mats": [], "names": []})
             groups[g]["mats"].append((w, t, n))
             groups[g]["names"].append(name)
-        ws = eng.workspace(1 << 22)
+        # room for the tcgen05 tiles, so the 5..16-token cases take that kernel
+        ws = eng.workspace(eng.lib.nsq_gemv_workspace_size(16, 14336))
         st = torch.cuda.current_stream().cuda_stream
         runs = []
         for g, d in groups.items():
