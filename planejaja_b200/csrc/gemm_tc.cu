@@ -129,9 +129,17 @@ __device__ __forceinline__ void dequant_col_kblock(const uint8_t* raw, int q, in
       const uint32_t wv = w2 ? qv.y : qv.x;
       const uint32_t lo = wv & 0x0F0F0F0Fu, hi = (wv >> 4) & 0x0F0F0F0Fu;
 #pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        v[4 * w2 + b] = __fmaf_rn(d1, (float)((lo >> (8 * b)) & 0xFF), -m1);
-        v[8 + 4 * w2 + b] = __fmaf_rn(d2, (float)((hi >> (8 * b)) & 0xFF), -m2);
+      for (int b = 0; b < 4; b += 2) {
+        const float2 l = __ffma2_rn(make_float2(d1, d1),
+                                    make_float2((float)((lo >> (8 * b)) & 0xFF), (float)((lo >> (8 * b + 8)) & 0xFF)),
+                                    make_float2(-m1, -m1));
+        const float2 h = __ffma2_rn(make_float2(d2, d2),
+                                    make_float2((float)((hi >> (8 * b)) & 0xFF), (float)((hi >> (8 * b + 8)) & 0xFF)),
+                                    make_float2(-m2, -m2));
+        v[4 * w2 + b] = l.x;
+        v[4 * w2 + b + 1] = l.y;
+        v[8 + 4 * w2 + b] = h.x;
+        v[8 + 4 * w2 + b + 1] = h.y;
       }
     }
     chunk[0] = qq;
@@ -224,7 +232,12 @@ __device__ __forceinline__ void dequant_col_kblock(const uint8_t* raw, int q, in
         // the four 6-bit values of word w as bytes; q - 32 exactly from 2^23 + q
         const uint32_t qb = ((ql[w] >> (4 * nib)) & 0x0F0F0F0Fu) | (((qh[w] >> (2 * j)) & 0x03030303u) << 4);
 #pragma unroll
-        for (int b = 0; b < 4; ++b) v[4 * w + b] = __fmul_rn(sa, __fsub_rn(byte_magic(qb, b), kTwo23 + 32.0f));
+        for (int b = 0; b < 4; b += 2) {
+          const float2 t = __fmul2_rn(make_float2(sa, sa), __fadd2_rn(make_float2(byte_magic(qb, b), byte_magic(qb, b + 1)),
+                                                                      make_float2(-(kTwo23 + 32.0f), -(kTwo23 + 32.0f))));
+          v[4 * w + b] = t.x;
+          v[4 * w + b + 1] = t.y;
+        }
       }
     }
     chunk[0] = 2 * qq;
@@ -241,7 +254,13 @@ __device__ __forceinline__ void dequant_col_kblock(const uint8_t* raw, int q, in
     for (int w = 0; w < 4; ++w) {
       const uint32_t nb = (qs[w] >> sh) & 0x0F0F0F0Fu;
 #pragma unroll
-      for (int b = 0; b < 4; ++b) v[4 * w + b] = __fmul_rn(__fsub_rn(byte_magic(nb, b), kTwo23 + 8.0f), d);
+      for (int b = 0; b < 4; b += 2) {
+        const float2 t = __fmul2_rn(__fadd2_rn(make_float2(byte_magic(nb, b), byte_magic(nb, b + 1)),
+                                               make_float2(-(kTwo23 + 8.0f), -(kTwo23 + 8.0f))),
+                                    make_float2(d, d));
+        v[4 * w + b] = t.x;
+        v[4 * w + b + 1] = t.y;
+      }
     }
     chunk[0] = 2 * qq;
     chunk[1] = 2 * qq + 1;
@@ -254,7 +273,12 @@ __device__ __forceinline__ void dequant_col_kblock(const uint8_t* raw, int q, in
     for (int w = 0; w < 4; ++w) {
       const uint32_t ub = qs[w] ^ 0x80808080u;  // int8 s as the byte s + 128
 #pragma unroll
-      for (int b = 0; b < 4; ++b) v[4 * w + b] = __fmul_rn(d, __fsub_rn(byte_magic(ub, b), kTwo23 + 128.0f));
+      for (int b = 0; b < 4; b += 2) {
+        const float2 t = __fmul2_rn(make_float2(d, d), __fadd2_rn(make_float2(byte_magic(ub, b), byte_magic(ub, b + 1)),
+                                                                  make_float2(-(kTwo23 + 128.0f), -(kTwo23 + 128.0f))));
+        v[4 * w + b] = t.x;
+        v[4 * w + b + 1] = t.y;
+      }
     }
     chunk[0] = 2 * qq;
     chunk[1] = 2 * qq + 1;
