@@ -11,14 +11,17 @@ synthetic data and random-init weights stand in for the Llama checkpoints.  The
 than the 126 MB L2 and consecutive steps never hit in L2.
 
 Per layer, one fused GEMV launch per shared activation: q|k|v (attention
-input), o, gate|up (FFN input), down -- 4 kernels, activations quantized on
-chip.  A step is captured once as a CUDA graph and replayed.
+input), o, gate|up (FFN input), down -- 4 launches (down's K = 14336
+activations quantised by a separate preparation kernel, the others on chip).
+A step is captured once as a CUDA graph and replayed.
 
 metric  : decode GEMV HBM GB/s = (weight bytes + fp32 activations + fp32
           outputs) of the whole step / step time (max over ranks), all ranks.
 e2e     : the same step through the C-ABI calls with host buffers: pinned-host
-          -> device copy of the step's activation vectors, the GEMVs, one
-          device -> pinned-host copy of all outputs of all layers, stream sync.
+          -> device copy of the step's activation vectors, the GEMVs, device ->
+          pinned-host copies of all outputs of all layers (each layer's outputs
+          copied by a second stream as soon as the layer is done, overlapped
+          with the later layers), stream sync.
 roofline: dominant kernel = the fused M = 1 Q4_K gate|up launch (2 x [14336 x
           4096], 66.19 MB), timed alone with CUDA events over the 32 layer
           copies; bound = HBM, peak = MEASURED_PEAKS.json hbm_gbs.  "kernels"
@@ -475,7 +478,7 @@ class DecodeStep:
                                     self.act_k[a], self.ws.data_ptr(), self.ws.numel(), st)
         assert rc == 0, rc
 
-    def step(self):
+    def step(self, after_layer=None):
         import torch
         st = torch.cuda.current_stream(self.ctx.dev).cuda_stream
         k0 = self.ctx.lib.nsq_kernel_launches()  # libnsq's own kernels (NCCL's are not counted)
@@ -485,6 +488,8 @@ class DecodeStep:
                 if self.mode == "nccl":
                     for nm in names:
                         self._dist.all_gather_into_tensor(self.outs_full[li][nm], self.outs_local[li][nm])
+            if after_layer is not None:
+                after_layer(li)
         if self.mode == "p2p":
             self.exchange.wait(st)  # the step ends when every rank's rows have landed here
         self.n_launch = self.ctx.lib.nsq_kernel_launches() - k0
@@ -515,18 +520,52 @@ class DecodeStep:
         ctx.launches += self.n_launch * steps
         return ctx.max_over_ranks(e0.elapsed_time(e1)) / steps
 
+    def _e2e_graph(self, out_pin):
+        """One step captured with its outputs streamed back to pinned host memory
+        layer by layer: after each layer's launches a second stream copies that
+        layer's outputs while the compute stream goes on with the next layer."""
+        import torch
+        dev = self.ctx.dev
+        per_layer = self.out_dev.numel() // self.L
+        s, side = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        events = [torch.cuda.Event() for _ in range(self.L)]
+
+        def after_layer(li):
+            events[li].record(s)
+            side.wait_event(events[li])
+            with torch.cuda.stream(side):
+                sl = slice(li * per_layer, (li + 1) * per_layer)
+                out_pin[sl].copy_(self.out_dev[sl], non_blocking=True)
+
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            side.wait_stream(s)  # the copy stream joins the capture
+            self.step(after_layer)
+            s.wait_stream(side)  # every copy is part of the step
+        torch.cuda.synchronize()
+        return g
+
     def time_e2e(self, steps, warmup):
-        """The same step with pinned-host inputs copied in and all outputs read back, per step."""
+        """The same step with pinned-host inputs copied in and all outputs read back, per step.
+        Single-GPU steps copy each layer's outputs back as soon as the layer is done,
+        overlapped with the later layers (one graph); sharded steps copy the whole
+        output once the step's exchanges have landed."""
         import torch
         ctx, dev = self.ctx, self.ctx.dev
         acts_pin = [torch.from_numpy(a).pin_memory() for a in self.acts_h]
         out_pin = torch.empty(self.out_dev.numel(), dtype=torch.float32).pin_memory()
+        overlapped = self.mode == "single" and self.graph is not None and self.out_dev.numel() % self.L == 0
+        g = self._e2e_graph(out_pin) if overlapped else None
 
         def e2e_step():
             for a, src in enumerate(acts_pin):
                 self.acts[a].copy_(src, non_blocking=True)
-            self.run()
-            out_pin.copy_(self.out_dev, non_blocking=True)
+            if g is not None:
+                g.replay()
+            else:
+                self.run()
+                out_pin.copy_(self.out_dev, non_blocking=True)
             torch.cuda.current_stream(dev).synchronize()
 
         for _ in range(warmup):
