@@ -112,6 +112,15 @@ struct TcParams {
   int64_t xrow0[NSQ_MAX_SEGMENTS], xnfull[NSQ_MAX_SEGMENTS], xoff[NSQ_MAX_SEGMENTS];
 };
 
+// Formats with a min term (Q4_K, Q5_K) need the min-term tiles and MMA; a
+// single-format launch of Q6_K, Q4_0 or Q8_0 leaves them out, and the shared
+// memory they free holds a second unit slot.
+template <int CODE>
+constexpr bool tc_has_min() {
+  return CODE == kTcQ4K || CODE == kTcQ5KG || CODE == kTcQ5KN || CODE == kTcMixed;
+}
+__host__ __device__ constexpr int tc_ub_bytes(bool has_min) { return has_min ? TC_UB_BYTES : 4 * TC_B_BYTES; }
+
 // Workspace of the batched path: counters, B tiles, min-term tiles, partials.
 size_t tc_workspace_bytes(int64_t K) {
   const int64_t nsb = K / 256;
@@ -459,9 +468,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
   // and the B tiles (four x stages, then the min-term tile); the min-term A
   // tile (4 accumulator slots, 16 K columns each)
   uint8_t* a_sm = smem;
+  constexpr bool HM = tc_has_min<CODE>();
+  constexpr int UB = tc_ub_bytes(HM);
   uint8_t* b_sm = a_sm + US * TC_UA_BYTES;
-  uint8_t* a2_sm = b_sm + US * TC_UB_BYTES;
-  float* scl_sm = reinterpret_cast<float*>(a2_sm + TC_A_BYTES);             // [16][16]
+  uint8_t* a2_sm = b_sm + US * UB;
+  float* scl_sm = reinterpret_cast<float*>(a2_sm + (HM ? TC_A_BYTES : 0));  // [16][16]
   float2* dsc = reinterpret_cast<float2*>(scl_sm + TC_SCL_STAGES * TC_BN);  // [4][128] (d, 32 dmin)
   uint8_t* raw_sm = reinterpret_cast<uint8_t*>(dsc + TC_NACC * TC_BM);
   const uint32_t RAW_BYTES = (uint32_t)(TC_BM * PITCH);
@@ -584,7 +595,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
             !mbar_wait_bounded(&my_bfull[u], iph(n, US, 1)))
           break;
         tc_fence_after();
-        const uint32_t ua = a_base + u * TC_UA_BYTES, ub = b_base + u * TC_UB_BYTES;
+        const uint32_t ua = a_base + u * TC_UA_BYTES, ub = b_base + u * UB;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
 #pragma unroll
@@ -595,7 +606,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
           }
         }
         // min-term A slot a: K columns 16a .. 16a + 16 of the min-term tile
-        tc_mma_bf16(dD2, umma_desc_sw128(a2_base + a * 32), umma_desc_sw128(ub + 4 * TC_B_BYTES), IDESC, 0u);
+        if (HM) tc_mma_bf16(dD2, umma_desc_sw128(a2_base + a * 32), umma_desc_sw128(ub + 4 * TC_B_BYTES), IDESC, 0u);
         tc_commit(&uempty[u]);
         tc_commit(&acc_full[a]);
       }
@@ -615,10 +626,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
         const uint8_t* col = p.ws_col + (int64_t)c * TC_COL_BYTES;
         if (!mbar_wait_bounded(&uempty[u], ur.par ^ 1)) break;
         uint64_t* bf = &bfull[(n % TC_MMA_WARPS) * US + u];
-        mbar_arrive_expect_tx(bf, TC_UB_BYTES);
-        uint8_t* dst = b_sm + u * TC_UB_BYTES;
+        mbar_arrive_expect_tx(bf, UB);
+        uint8_t* dst = b_sm + u * UB;
         bulk_g2s_hint(dst, p.ws_b + (int64_t)(4 * c) * TC_B_BYTES, 4 * TC_B_BYTES, bf, pol);
-        bulk_g2s_hint(dst + 4 * TC_B_BYTES, col, TC_B2_BYTES, bf, pol);
+        if (HM) bulk_g2s_hint(dst + 4 * TC_B_BYTES, col, TC_B2_BYTES, bf, pol);
         if (!mbar_wait_bounded(&scl_empty[ss], ph(n, TC_SCL_STAGES) ^ 1)) break;
         mbar_arrive_expect_tx(&scl_full[ss], TC_BN * 4);
         bulk_g2s_hint(scl_sm + ss * TC_BN, col + TC_B2_BYTES, TC_BN * 4, &scl_full[ss], pol);
@@ -680,22 +691,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
             for (int pp = 0; pp < 4; ++pp) q5k_pair<true>(raw, q, pp, s0, b0, s1, b1, ch[pp], ch[pp + 4]);
           }
         } else if (code == kTcQ6KG) {
-          *reinterpret_cast<uint32_t*>(a2row + ((a2c ^ sw) << 4) + 4 * q) = 0u;
+          if (HM) *reinterpret_cast<uint32_t*>(a2row + ((a2c ^ sw) << 4) + 4 * q) = 0u;
           if (q == 0) dsc[a * TC_BM + row] = make_float2(h2f((uint16_t)ld_u16(raw + 208)), 0.f);
 #pragma unroll
           for (int pp = 0; pp < 4; ++pp) q6k_pair(raw, q, pp, 4 * (q & 1), ch[pp], ch[pp + 4], off16);
         } else if (code == kTcQ6KN) {
-          *reinterpret_cast<uint32_t*>(a2row + ((a2c ^ sw) << 4) + 4 * q) = 0u;
+          if (HM) *reinterpret_cast<uint32_t*>(a2row + ((a2c ^ sw) << 4) + 4 * q) = 0u;
           if (q == 0) dsc[a * TC_BM + row] = make_float2(h2f((uint16_t)ld_u16(raw + 208)) * 0.015625f, 0.f);
           q6kn_stage(raw, q, ch);
         } else {
           // Q4_0 / Q8_0: the block scales are in A, no min term
-          *reinterpret_cast<uint32_t*>(a2row + ((a2c ^ sw) << 4) + 4 * q) = 0u;
+          if (HM) *reinterpret_cast<uint32_t*>(a2row + ((a2c ^ sw) << 4) + 4 * q) = 0u;
           if (q == 0) dsc[a * TC_BM + row] = make_float2(1.0f, 0.f);
           if (code == kTcQ40) q40_stage(raw, q, ch);
           else q80_stage(raw, q, ch);
         }
-        if (q == 1) *reinterpret_cast<uint4*>(a2row + (((a2c + 1) ^ sw) << 4)) = make_uint4(0, 0, 0, 0);
+        if (HM && q == 1) *reinterpret_cast<uint4*>(a2row + (((a2c + 1) ^ sw) << 4)) = make_uint4(0, 0, 0, 0);
         // the unit slot is free once the MMAs of its previous unit have completed
         if (i == 0 && !mbar_wait_bounded(&uempty[u], ur.par ^ 1)) {
           ok = false;
@@ -742,6 +753,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           uint32_t v[32];
+          if (h == 1 && !HM) {
+#pragma unroll
+            for (int t = 0; t < TC_BN; ++t) d2sum[t] = 0.f;
+            continue;
+          }
           tc_ld_32x32b_x32(taddr + 32 * h, v);
 #pragma unroll
           for (int t = 0; t < TC_BN; ++t) {
@@ -971,15 +987,15 @@ int run_gemv_tc(const nsq_segment* segs, int nseg, const float* x, int64_t M, in
   p.ws_b = ws + 1024;
   p.ws_col = p.ws_b + (size_t)NSB * 4 * TC_B_BYTES;
   p.ws_part = reinterpret_cast<float*>(const_cast<uint8_t*>(p.ws_col) + (size_t)NSB * TC_COL_BYTES);
-  // shared memory: 4 A stages, up to 12 B stages (3 units of x ahead), 3
-  // min-term stages; the raw ring takes what is left (3 or 4 units)
   // Shared memory: two unit slots of A and B tiles when they fit beside two
-  // raw columns (Q4_K), so that the dequant warps and the B producer fill a
-  // unit while the MMAs of the one before still read theirs; otherwise (Q6_K's
-  // wider raw columns) one unit slot and up to four raw columns.
+  // raw columns, so that the dequant warps and the B producer fill a unit
+  // while the MMAs of the one before still read theirs: Q4_K, Q4_0, and a
+  // single-format Q6_K launch, which leaves out the min-term tiles; otherwise
+  // one unit slot and up to four raw columns.
+  const bool hm = code == kTcMixed || code == kTcQ4K || code == kTcQ5KG || code == kTcQ5KN;
   auto smem_of = [&](int us, int r) {
-    return 1024 + (size_t)us * (TC_UA_BYTES + TC_UB_BYTES) + TC_A_BYTES + (size_t)TC_SCL_STAGES * TC_BN * 4 +
-           (size_t)TC_NACC * TC_BM * 8 + 1024 + (size_t)r * TC_BM * pitch;
+    return 1024 + (size_t)us * (TC_UA_BYTES + tc_ub_bytes(hm)) + (hm ? TC_A_BYTES : 0) +
+           (size_t)TC_SCL_STAGES * TC_BN * 4 + (size_t)TC_NACC * TC_BM * 8 + 1024 + (size_t)r * TC_BM * pitch;
   };
   int us = 2, rs = 2;
   if (smem_of(us, rs) > (size_t)TC_SMEM_LIMIT) {
