@@ -38,7 +38,8 @@
 //
 // Warp roles (512 threads, one CTA per SM):
 //   warp 0      raw producer: one 2-D TMA box [128 rows x one super-block
-//               column] of the GGUF bytes per unit (evict-first in L2)
+//               column] of the GGUF bytes per unit (evict-first in L2), and
+//               an L2 prefetch of the column that takes the slot next
 //   warps 1, 3  MMA issue, one thread each, alternate units (warp 1 owns
 //               TMEM).  A thread that issues, commits and waits in turn
 //               keeps the tensor pipe busy less than half the time; two
@@ -51,7 +52,9 @@
 //               the min-term A tile and the row's d / dmin; warp (q, h)
 //               writes K stage q of rows [64h, 64h + 64) of every unit
 // Every wait is bounded (%globaltimer); a wait that gives up records
-// NSQ_ERR_TIMEOUT and the kernel winds down.
+// NSQ_ERR_TIMEOUT and the kernel winds down.  With a row-sharded exchange
+// (P > 1) the outputs go into every rank's exchange buffer and the grid's
+// last CTA publishes the count, as in the fused kernel.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
