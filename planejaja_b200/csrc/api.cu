@@ -46,7 +46,7 @@ cudaError_t comm_launch_wait(const nsq_comm* c, cudaStream_t st);
 static const char* const kTuneNames[kTuneCount] = {
     "NSQ_ROWS_R", "NSQ_ROWS_PPSM", "NSQ_ROWS_STAGES", "NSQ_ROWS_PRE", "NSQ_ROWS_L2HINT", "NSQ_ROWS_CPS",
     "NSQ_ROWS_C", "NSQ_ROWS_BAL", "NSQ_ROWS_CARVE", "NSQ_MMA_MIN_M", "NSQ_MMA_PPS", "NSQ_MMA_STAGES",
-    "NSQ_GEMV_GENERAL", "NSQ_GEMM_SPLIT", "NSQ_GEMM_TOK", "NSQ_TC_MIN_M"};
+    "NSQ_GEMV_GENERAL", "NSQ_GEMM_SPLIT", "NSQ_GEMM_TOK", "NSQ_TC_MIN_M", "NSQ_TC_A"};
 static std::atomic<int> g_tune_val[kTuneCount];
 static std::atomic<bool> g_tune_set[kTuneCount];
 static std::once_flag g_tune_once;

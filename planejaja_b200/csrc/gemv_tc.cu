@@ -34,12 +34,21 @@
 // tile-major order; CTA i of G takes units [U i / G, U (i+1) / G).  A tile
 // that spans CTAs is finished by the last of them to arrive (a counter per
 // split tile), which sums the partials in CTA order -- deterministic, and no
-// CTA ever waits for another.
+// CTA ever waits for another.  A CTA that finds every other partial of the
+// tile in place already finishes it from its registers.
+//
+// The fp16 A operand lives in tensor memory by default: the dequant warps
+// write it with tcgen05.st (each warp into its own 32-lane quadrant) and the
+// MMA reads it in its A-from-TMEM form, so shared memory carries only the
+// raw columns, the x tiles and the min-term tiles (NSQ_TC_A=0 puts A in
+// 128B-swizzled shared-memory tiles instead).  TMEM: four accumulator slots
+// (D and D2, 64 columns each) and two unit slots of A (128 columns each).
 //
 // Warp roles (512 threads, one CTA per SM):
 //   warp 0      raw producer: one 2-D TMA box [128 rows x one super-block
-//               column] of the GGUF bytes per unit (evict-first in L2), and
-//               an L2 prefetch of the column that takes the slot next
+//               column] of the GGUF bytes per unit (evict-first in L2), the
+//               first ones before the setup sync; with a short ring, an L2
+//               prefetch of the column that takes the slot next
 //   warps 1, 3  MMA issue, one thread each, alternate units (warp 1 owns
 //               TMEM).  A thread that issues, commits and waits in turn
 //               keeps the tensor pipe busy less than half the time; two
@@ -48,9 +57,10 @@
 //               min-term tile and the token scales, from the workspace the
 //               preparation kernel wrote
 //   warps 4..7  epilogue (TMEM lane quadrant = warp % 4, one row per thread)
-//   warps 8..15 dequant: raw bytes -> fp16 A tiles (128B-swizzled K-major),
-//               the min-term A tile and the row's d / dmin; warp (q, h)
-//               writes K stage q of rows [64h, 64h + 64) of every unit
+//   warps 8..15 dequant: raw bytes -> fp16 A, the min-term A tile and the
+//               row's d / dmin; A in TMEM: warp (r, h) writes row 32r + lane
+//               (r = warp % 4), K stages 2h and 2h + 1; A in shared memory:
+//               warp (q, h) writes K stage q of rows [64h, 64h + 64)
 // Every wait is bounded (%globaltimer); a wait that gives up records
 // NSQ_ERR_TIMEOUT and the kernel winds down.  With a row-sharded exchange
 // (P > 1) the outputs go into every rank's exchange buffer and the grid's
@@ -83,6 +93,8 @@ constexpr int TC_ACC_COLS = 64;              // per unit: D (hi | lo, 32 columns
 constexpr int TC_SCL_STAGES = 16;            // token scales (64 B per unit)
 constexpr int TC_GMAX = 256;                 // most CTAs a launch uses
 constexpr int TC_TMEM_COLS = TC_NACC * TC_ACC_COLS;
+constexpr int TC_A_TMEM_COLS = 128;          // a unit's fp16 A in TMEM: 256 K per lane, two per column
+constexpr int TC_TMEM_COLS_A = TC_TMEM_COLS + 2 * TC_A_TMEM_COLS;  // with two unit slots of A in TMEM: 512
 constexpr int TC_SMEM_LIMIT = 232448;
 
 enum : int { kTcQ4K = 0, kTcQ6KG = 1, kTcQ40 = 2, kTcQ80 = 3, kTcQ6KN = 4, kTcQ5KG = 5, kTcQ5KN = 6, kTcMixed = -1 };
@@ -416,7 +428,7 @@ __device__ __forceinline__ void q6kn_stage(const uint8_t* raw, int q, uint4 (&ch
 // direct lookup cost every role's threads more integer work than the dequant
 // of a unit's rows).
 struct TcCursor {
-  int sg, tl, c, t;
+  int sg = 0, tl = 0, c = 0, t = 0;
   __device__ void init(const TcParams& p, int64_t u) {
     t = (int)(u / p.NSB);
     c = (int)(u - (int64_t)t * p.NSB);
@@ -462,7 +474,60 @@ __device__ __forceinline__ void tc_store_y(const TcParams& p, const TcSeg& S, in
 // CTA index owning unit u (unit ranges [U i / G, U (i+1) / G)).
 __device__ __forceinline__ int tc_owner(int64_t u, int64_t U, int G) { return (int)(((u + 1) * G - 1) / U); }
 
+// One row's K stage q (64 weights) of a unit: the fp16 A chunks in natural K
+// order (chunk k8 = K 8 k8 .. 8 k8 + 7 of the stage), word q of the row's
+// min-term chunk a2c (Q4_K / Q5_K: the mins of sub-blocks 2q and 2q + 1, else
+// zero), for q == 0 the row's epilogue factors (d, 32 dmin), and for q == 1
+// the zero chunk beside the min-term chunk.
 template <int CODE>
+__device__ __forceinline__ void tc_stage(int code, const uint8_t* raw, int q, int off16, uint8_t* a2row, int a2c,
+                                         int sw, float2* dsc_row, uint4 (&ch)[8]) {
+  constexpr bool HM = tc_has_min<CODE>();
+  if (code == kTcQ4K || code == kTcQ5KG || code == kTcQ5KN) {
+    // Q4_K and Q5_K share the header: d, dmin, the packed 6-bit scales and mins
+    const uint4 hdr = *reinterpret_cast<const uint4*>(raw);
+    const uint32_t sm0 = q4k_scale_min(hdr.y, hdr.z, hdr.w, 2 * q);
+    const uint32_t sm1 = q4k_scale_min(hdr.y, hdr.z, hdr.w, 2 * q + 1);
+    *reinterpret_cast<uint32_t*>(a2row + ((a2c ^ sw) << 4) + 4 * q) =
+        h2_bits(__halves2half2(__uint2half_rn(sm0 >> 8), __uint2half_rn(sm1 >> 8)));
+    if (q == 0) {
+      const float d = h2f((uint16_t)(hdr.x & 0xFFFF)), dmin = h2f((uint16_t)(hdr.x >> 16));
+      *dsc_row = make_float2(d, 32.0f * dmin);
+    }
+    const __half h0 = __uint2half_rn(sm0 & 0xFF), h1 = __uint2half_rn(sm1 & 0xFF);
+    const __half2 s0 = __half2half2(h0), s1 = __half2half2(h1);
+    const __half2 b0 = __half2half2(__hmul(h0, __float2half_rn(-1024.f)));
+    const __half2 b1 = __half2half2(__hmul(h1, __float2half_rn(-1024.f)));
+    if (code == kTcQ4K) {
+#pragma unroll
+      for (int pp = 0; pp < 4; ++pp) q4k_pair(raw, q, pp, s0, b0, s1, b1, ch[pp], ch[pp + 4]);
+    } else if (code == kTcQ5KG) {
+#pragma unroll
+      for (int pp = 0; pp < 4; ++pp) q5k_pair<false>(raw, q, pp, s0, b0, s1, b1, ch[pp], ch[pp + 4]);
+    } else {
+#pragma unroll
+      for (int pp = 0; pp < 4; ++pp) q5k_pair<true>(raw, q, pp, s0, b0, s1, b1, ch[pp], ch[pp + 4]);
+    }
+  } else if (code == kTcQ6KG) {
+    if (HM) *reinterpret_cast<uint32_t*>(a2row + ((a2c ^ sw) << 4) + 4 * q) = 0u;
+    if (q == 0) *dsc_row = make_float2(h2f((uint16_t)ld_u16(raw + 208)), 0.f);
+#pragma unroll
+    for (int pp = 0; pp < 4; ++pp) q6k_pair(raw, q, pp, 4 * (q & 1), ch[pp], ch[pp + 4], off16);
+  } else if (code == kTcQ6KN) {
+    if (HM) *reinterpret_cast<uint32_t*>(a2row + ((a2c ^ sw) << 4) + 4 * q) = 0u;
+    if (q == 0) *dsc_row = make_float2(h2f((uint16_t)ld_u16(raw + 208)) * 0.015625f, 0.f);
+    q6kn_stage(raw, q, ch);
+  } else {
+    // Q4_0 / Q8_0: the block scales are in A, no min term
+    if (HM) *reinterpret_cast<uint32_t*>(a2row + ((a2c ^ sw) << 4) + 4 * q) = 0u;
+    if (q == 0) *dsc_row = make_float2(1.0f, 0.f);
+    if (code == kTcQ40) q40_stage(raw, q, ch);
+    else q80_stage(raw, q, ch);
+  }
+  if (HM && q == 1) *reinterpret_cast<uint4*>(a2row + (((a2c + 1) ^ sw) << 4)) = make_uint4(0, 0, 0, 0);
+}
+
+template <int CODE, bool ATM>
 __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_constant__ TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -473,7 +538,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
   uint8_t* a_sm = smem;
   constexpr bool HM = tc_has_min<CODE>();
   constexpr int UB = tc_ub_bytes(HM);
-  uint8_t* b_sm = a_sm + US * TC_UA_BYTES;
+  uint8_t* b_sm = a_sm + (ATM ? 0 : US * TC_UA_BYTES);  // A in TMEM: no A tiles here
   uint8_t* a2_sm = b_sm + US * UB;
   float* scl_sm = reinterpret_cast<float*>(a2_sm + (HM ? TC_A_BYTES : 0));  // [16][16]
   float2* dsc = reinterpret_cast<float2*>(scl_sm + TC_SCL_STAGES * TC_BN);  // [4][128] (d, 32 dmin)
@@ -505,6 +570,45 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
   const int64_t u0 = p.U * blockIdx.x / G, u1 = p.U * (blockIdx.x + 1) / G;
   const int nunits = (int)(u1 - u0);
 
+  // ---- raw producer (thread 0): per unit one 2-D TMA box [128 rows x one
+  // super-block column] of the GGUF bytes, evict-first in L2.  A short ring
+  // (fewer than 4 columns) is backed by an L2 prefetch of the column that
+  // takes the slot next, so that its copy reads the L2, not HBM; a deep ring
+  // is not (the prefetches would double the burst at the start).  The first
+  // columns are issued before the block-wide setup sync.
+  TcCursor rcur, rahead;
+  TcRing rring(RS);
+  int rn = 0;
+  uint64_t rpol = 0;
+  const bool l2_ahead = RS < 4;
+  auto raw_issue = [&]() -> bool {
+    const int sg = rcur.sg, tl = rcur.tl, c = rcur.c, rs = rring.slot;
+    if (!mbar_wait_bounded(&raw_empty[rs], rring.par ^ 1)) return false;
+    const int x0 = (int)(((int64_t)c * p.seg[sg].CB) & ~int64_t(15)) / 2;
+    mbar_arrive_expect_tx(&raw_full[rs], RAW_BYTES);
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(raw_sm + rs * RAW_BYTES)),
+        "l"(reinterpret_cast<uint64_t>(&p.wmap[sg])), "r"(x0), "r"(tl * TC_BM), "r"(smem_u32(&raw_full[rs])),
+        "l"(rpol)
+        : "memory");
+    if (l2_ahead) {
+      if (rn + RS < nunits) {
+        const int sg2 = rahead.sg, tl2 = rahead.tl, c2 = rahead.c;
+        const int x2 = (int)(((int64_t)c2 * p.seg[sg2].CB) & ~int64_t(15)) / 2;
+        asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                         reinterpret_cast<uint64_t>(&p.wmap[sg2])),
+                     "r"(x2), "r"(tl2 * TC_BM)
+                     : "memory");
+      }
+      rahead.next(p);
+    }
+    ++rn;
+    rcur.next(p);
+    rring.next();
+    return true;
+  };
+
   if (threadIdx.x == 0) {
     for (int s = 0; s < US; ++s) mbar_init(&uempty[s], 1);
     for (int s = 0; s < TC_MMA_WARPS * US; ++s) {
@@ -527,15 +631,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
     }
     mbar_init(done, TC_MMA_WARPS);
     fence_mbar_init();
+    // the first columns depend on nothing: their slots are fresh (the empty
+    // waits pass at once)
+    rpol = l2_policy_evict_first();
+    rcur.init(p, u0);
+    if (l2_ahead) rahead.init(p, u0 + RS);
+    while (rn < nunits && rn < RS) raw_issue();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, TC_TMEM_COLS);
+    tmem_alloc(tmem_slot, ATM ? TC_TMEM_COLS_A : TC_TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // The next kernel may launch now: each of ours waits for this grid
+  // (griddepcontrol.wait) before it reads or writes anything this one uses,
+  // so only its launch latency overlaps this grid's work.
+  tc_grid_launch();
 
   // parity of the k-th use of a ring slot: full waits (k / R) & 1, empty waits its complement
   auto ph = [](int k, int R) { return (uint32_t)((k / R) & 1); };
@@ -549,36 +663,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
   };
 
   if (warp == 0) {
-    // ---- raw producer: the unit's GGUF column for the tile's 128 rows
-    if (lane == 0) {
-      const uint64_t pol = l2_policy_evict_first();
-      TcCursor cur, ahead;  // unit n, and unit n + RS (the next user of n's slot)
-      cur.init(p, u0);
-      ahead.init(p, u0 + RS);
-      TcRing rr(RS);
-      for (int n = 0; n < nunits; ++n, cur.next(p), ahead.next(p), rr.next()) {
-        const int sg = cur.sg, tl = cur.tl, c = cur.c, rs = rr.slot;
-        if (!mbar_wait_bounded(&raw_empty[rs], rr.par ^ 1)) break;
-        const int x0 = (int)(((int64_t)c * p.seg[sg].CB) & ~int64_t(15)) / 2;
-        mbar_arrive_expect_tx(&raw_full[rs], RAW_BYTES);
-        asm volatile(
-            "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-            " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(raw_sm + rs * RAW_BYTES)),
-            "l"(reinterpret_cast<uint64_t>(&p.wmap[sg])), "r"(x0), "r"(tl * TC_BM), "r"(smem_u32(&raw_full[rs])),
-            "l"(pol)
-            : "memory");
-        // the column that takes this slot next is fetched into the L2 now, so
-        // its copy (issued once this one is consumed) reads the L2, not HBM
-        if (n + RS < nunits) {
-          const int sg2 = ahead.sg, tl2 = ahead.tl, c2 = ahead.c;
-          const int x2 = (int)(((int64_t)c2 * p.seg[sg2].CB) & ~int64_t(15)) / 2;
-          asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
-                           reinterpret_cast<uint64_t>(&p.wmap[sg2])),
-                       "r"(x2), "r"(tl2 * TC_BM)
-                       : "memory");
-        }
-      }
-    }
+    // ---- raw producer: the rest of the columns, as their slots free up
+    if (lane == 0)
+      while (rn < nunits)
+        if (!raw_issue()) break;
   } else if (warp == 1 || warp == 3) {
     // ---- MMA issue: issuer i takes units i, i + 2, ... (accumulators a = n % 4
     // alternate between the issuers)
@@ -599,13 +687,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
           break;
         tc_fence_after();
         const uint32_t ua = a_base + u * TC_UA_BYTES, ub = b_base + u * UB;
+        const uint32_t ta = tmem + (uint32_t)(TC_TMEM_COLS + TC_A_TMEM_COLS * u);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t ad = umma_desc_sw128(ua + q * TC_A_BYTES + kk * 32);
             const uint64_t bd = umma_desc_sw128(ub + q * TC_B_BYTES + kk * 32);
-            tc_mma_bf16(dD, ad, bd, IDESC, (q | kk) ? 1u : 0u);
+            if constexpr (ATM) {
+              // K step 16 q' of the unit: TMEM columns 8 q' .. 8 q' + 7 of its A slot
+              tc_mma_ts(dD, ta + (uint32_t)(32 * q + 8 * kk), bd, IDESC, (q | kk) ? 1u : 0u);
+            } else {
+              const uint64_t ad = umma_desc_sw128(ua + q * TC_A_BYTES + kk * 32);
+              tc_mma_bf16(dD, ad, bd, IDESC, (q | kk) ? 1u : 0u);
+            }
           }
         }
         // min-term A slot a: K columns 16a .. 16a + 16 of the min-term tile
@@ -638,6 +732,55 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
         bulk_g2s_hint(scl_sm + ss * TC_BN, col + TC_B2_BYTES, TC_BN * 4, &scl_full[ss], pol);
       }
     }
+  } else if (ATM && warp >= TC_DQ_WARP0) {
+    // ---- dequant into TMEM: warp (r, h), r = warp % 4 its TMEM lane
+    // quadrant, writes row 32r + lane of every unit, K stages 2h and 2h + 1
+    // (one tcgen05.st of 32 columns each) into the unit slot's A columns.
+    // The warps of stage q = 0 / 1 also write the row's d / dmin and the
+    // min-term chunk's zero half; stage q's writer owns min-term word q.
+    // The TMEM stores and the MMAs that read them are ordered through the
+    // unit slot's barriers (wait::st, fence, arrive / wait, fence), and the
+    // stores into a slot wait for the commit of the MMAs that read it last.
+    // The waits' outcomes are made warp-uniform before the .aligned stores.
+    const int dw = warp - TC_DQ_WARP0, r = dw & 3, h = dw >> 2;
+    const int row = 32 * r + lane, sw = row & 7;
+    const uint32_t trow = tmem + ((uint32_t)(32 * r) << 16) + (uint32_t)TC_TMEM_COLS;
+    TcCursor cur;
+    cur.init(p, u0);
+    TcRing rr(RS), ur(US);
+    for (int n = 0; n < nunits; ++n, cur.next(p), rr.next(), ur.next()) {
+      const int sg = cur.sg, c = cur.c;
+      const int code = CODE == kTcMixed ? p.seg[sg].code : CODE;
+      const int rs = rr.slot, a = n % TC_NACC, u = ur.slot;
+      bool ok = mbar_wait_bounded(&raw_full[rs], rr.par) && mbar_wait_bounded(&a2_empty[a], ph(n, TC_NACC) ^ 1);
+      if (!__all_sync(0xFFFFFFFFu, ok)) break;
+      const int off16 = (int)(((int64_t)c * p.seg[sg].CB) & 15);
+      const uint8_t* raw = raw_sm + rs * RAW_BYTES + row * PITCH + off16;
+      uint8_t* a2row = a2_sm + row * 128;
+#pragma unroll
+      for (int s = 0; s < 2; ++s) {
+        const int q = 2 * h + s;
+        uint4 ch[8];
+        tc_stage<CODE>(code, raw, q, off16, a2row, 2 * a, sw, &dsc[a * TC_BM + row], ch);
+        if (s == 0) {
+          // the slot's A columns are free once the MMAs of its previous unit have completed
+          ok = __all_sync(0xFFFFFFFFu, mbar_wait_bounded(&uempty[u], ur.par ^ 1));
+          if (!ok) break;
+          tc_fence_after();
+        }
+        tc_st_32x32b_x32(trow + (uint32_t)(TC_A_TMEM_COLS * u + 32 * q), ch);
+      }
+      if (!ok) break;
+      tc_wait_st();
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&a2_full[a]);
+        mbar_arrive(&afull[(n % TC_MMA_WARPS) * US + u]);
+        mbar_arrive(&raw_empty[rs]);
+      }
+    }
   } else if (warp >= TC_DQ_WARP0) {
     // ---- dequant: warp (q, h) produces K stage q of every unit for rows
     // [64h, 64h + 64), rows lane and lane + 32, all 8 chunks of a row in one
@@ -666,50 +809,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
       for (int i = 0; i < 2; ++i) {
         const int row = 64 * h + 32 * i + lane, sw = row & 7;
         const uint8_t* raw = raw_sm + rs * RAW_BYTES + row * PITCH + off16;
-        uint8_t* a2row = a2_sm + row * 128;
         uint4 ch[8];
-        if (code == kTcQ4K || code == kTcQ5KG || code == kTcQ5KN) {
-          // Q4_K and Q5_K share the header: d, dmin, the packed 6-bit scales and mins
-          const uint4 hdr = *reinterpret_cast<const uint4*>(raw);
-          const uint32_t sm0 = q4k_scale_min(hdr.y, hdr.z, hdr.w, 2 * q);
-          const uint32_t sm1 = q4k_scale_min(hdr.y, hdr.z, hdr.w, 2 * q + 1);
-          *reinterpret_cast<uint32_t*>(a2row + ((a2c ^ sw) << 4) + 4 * q) =
-              h2_bits(__halves2half2(__uint2half_rn(sm0 >> 8), __uint2half_rn(sm1 >> 8)));
-          if (q == 0) {
-            const float d = h2f((uint16_t)(hdr.x & 0xFFFF)), dmin = h2f((uint16_t)(hdr.x >> 16));
-            dsc[a * TC_BM + row] = make_float2(d, 32.0f * dmin);
-          }
-          const __half h0 = __uint2half_rn(sm0 & 0xFF), h1 = __uint2half_rn(sm1 & 0xFF);
-          const __half2 s0 = __half2half2(h0), s1 = __half2half2(h1);
-          const __half2 b0 = __half2half2(__hmul(h0, __float2half_rn(-1024.f)));
-          const __half2 b1 = __half2half2(__hmul(h1, __float2half_rn(-1024.f)));
-          if (code == kTcQ4K) {
-#pragma unroll
-            for (int pp = 0; pp < 4; ++pp) q4k_pair(raw, q, pp, s0, b0, s1, b1, ch[pp], ch[pp + 4]);
-          } else if (code == kTcQ5KG) {
-#pragma unroll
-            for (int pp = 0; pp < 4; ++pp) q5k_pair<false>(raw, q, pp, s0, b0, s1, b1, ch[pp], ch[pp + 4]);
-          } else {
-#pragma unroll
-            for (int pp = 0; pp < 4; ++pp) q5k_pair<true>(raw, q, pp, s0, b0, s1, b1, ch[pp], ch[pp + 4]);
-          }
-        } else if (code == kTcQ6KG) {
-          if (HM) *reinterpret_cast<uint32_t*>(a2row + ((a2c ^ sw) << 4) + 4 * q) = 0u;
-          if (q == 0) dsc[a * TC_BM + row] = make_float2(h2f((uint16_t)ld_u16(raw + 208)), 0.f);
-#pragma unroll
-          for (int pp = 0; pp < 4; ++pp) q6k_pair(raw, q, pp, 4 * (q & 1), ch[pp], ch[pp + 4], off16);
-        } else if (code == kTcQ6KN) {
-          if (HM) *reinterpret_cast<uint32_t*>(a2row + ((a2c ^ sw) << 4) + 4 * q) = 0u;
-          if (q == 0) dsc[a * TC_BM + row] = make_float2(h2f((uint16_t)ld_u16(raw + 208)) * 0.015625f, 0.f);
-          q6kn_stage(raw, q, ch);
-        } else {
-          // Q4_0 / Q8_0: the block scales are in A, no min term
-          if (HM) *reinterpret_cast<uint32_t*>(a2row + ((a2c ^ sw) << 4) + 4 * q) = 0u;
-          if (q == 0) dsc[a * TC_BM + row] = make_float2(1.0f, 0.f);
-          if (code == kTcQ40) q40_stage(raw, q, ch);
-          else q80_stage(raw, q, ch);
-        }
-        if (HM && q == 1) *reinterpret_cast<uint4*>(a2row + (((a2c + 1) ^ sw) << 4)) = make_uint4(0, 0, 0, 0);
+        tc_stage<CODE>(code, raw, q, off16, a2_sm + row * 128, a2c, sw, &dsc[a * TC_BM + row], ch);
         // the unit slot is free once the MMAs of its previous unit have completed
         if (i == 0 && !mbar_wait_bounded(&uempty[u], ur.par ^ 1)) {
           ok = false;
@@ -796,27 +897,44 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
             if (m < p.M) tc_store_y(p, S, sg, m, nrow, acc[m]);
         }
       } else {
-        // partial: slot 2i for the first segment of CTA i, 2i + 1 for its last
-        const bool first_seg = (int64_t)t_glob * p.NSB <= u0;
-        const int slot = 2 * (int)blockIdx.x + (first_seg ? 0 : 1);
-        float4* dst = reinterpret_cast<float4*>(p.ws_part + ((int64_t)slot * TC_BM + row) * TC_BN);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) __stcg(dst + i, make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]));
-        __threadfence();
-        asm volatile("bar.sync 1, 128;" ::: "memory");
         const int64_t ut0 = (int64_t)t_glob * p.NSB;
         const int i_first = tc_owner(ut0, p.U, G), i_last = tc_owner(ut0 + p.NSB - 1, p.U, G);
-        if (threadIdx.x == TC_EPI_WARP0 * 32) {
-          const uint32_t old = atomicAdd(p.ws_cnt + i_first, 1u);
-          *s_last = (old == (uint32_t)(i_last - i_first)) ? 1 : 0;
-        }
+        // Every other CTA of the tile has added its partial already (usual for
+        // a CTA's last segment: the next CTA starts with that tile): this CTA
+        // finishes the tile from its registers, without a partial of its own,
+        // a fence or an arrival.  The sum runs in CTA order either way, so
+        // the bits do not depend on the path.
+        if (threadIdx.x == TC_EPI_WARP0 * 32)
+          *s_last = ld_acquire_gpu(p.ws_cnt + i_first) == (uint32_t)(i_last - i_first) ? 2 : 0;
         asm volatile("bar.sync 1, 128;" ::: "memory");
+        const bool fast = *s_last == 2;
+        if (!fast) {
+          // partial: slot 2i for the first segment of CTA i, 2i + 1 for its last
+          const bool first_seg = ut0 <= u0;
+          const int slot = 2 * (int)blockIdx.x + (first_seg ? 0 : 1);
+          float4* dst = reinterpret_cast<float4*>(p.ws_part + ((int64_t)slot * TC_BM + row) * TC_BN);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            __stcg(dst + i, make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]));
+          __threadfence();
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          if (threadIdx.x == TC_EPI_WARP0 * 32) {
+            const uint32_t old = atomicAdd(p.ws_cnt + i_first, 1u);
+            *s_last = (old == (uint32_t)(i_last - i_first)) ? 1 : 0;
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+        }
         if (*s_last) {
           __threadfence();
           float sum[TC_BN];
 #pragma unroll
           for (int t = 0; t < TC_BN; ++t) sum[t] = 0.f;
           for (int i = i_first; i <= i_last; ++i) {
+            if (fast && i == (int)blockIdx.x) {
+#pragma unroll
+              for (int t = 0; t < TC_BN; ++t) sum[t] += acc[t];
+              continue;
+            }
             const int64_t ui0 = p.U * i / G;
             const int sl = 2 * i + ((i == i_first && ui0 < ut0) ? 1 : 0);
             const float4* src = reinterpret_cast<const float4*>(p.ws_part + ((int64_t)sl * TC_BM + row) * TC_BN);
@@ -860,7 +978,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
     // both issuers' final commits arrive once every MMA has completed
     mbar_wait_bounded(done, 0);
     tc_fence_after();
-    tmem_dealloc(tmem, TC_TMEM_COLS);
+    tmem_dealloc(tmem, ATM ? TC_TMEM_COLS_A : TC_TMEM_COLS);
   }
 }
 
@@ -907,9 +1025,9 @@ bool tc_covers(const nsq_segment* segs, int nseg, int64_t M, int64_t K) {
 // against 7.42 ms; at M = 4 the single dp4a pass wins, 3.78 against 4.96 ms).
 int tc_min_m() { return tune(kTuneTcMinM, 5); }
 
-template <int CODE>
+template <int CODE, bool ATM>
 static cudaError_t launch_tc(const TcParams& p, int blocks, size_t smem, cudaStream_t st) {
-  auto kern = gemv_tc_kernel<CODE>;
+  auto kern = gemv_tc_kernel<CODE, ATM>;
   static size_t configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -930,6 +1048,20 @@ static cudaError_t launch_tc(const TcParams& p, int blocks, size_t smem, cudaStr
   cfg.numAttrs = 1;
   note_launch();
   return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+template <bool ATM>
+static cudaError_t launch_code(int code, const TcParams& p, int G, size_t smem, cudaStream_t st) {
+  switch (code) {
+    case kTcQ4K: return launch_tc<kTcQ4K, ATM>(p, G, smem, st);
+    case kTcQ6KG: return launch_tc<kTcQ6KG, ATM>(p, G, smem, st);
+    case kTcQ40: return launch_tc<kTcQ40, ATM>(p, G, smem, st);
+    case kTcQ80: return launch_tc<kTcQ80, ATM>(p, G, smem, st);
+    case kTcQ6KN: return launch_tc<kTcQ6KN, ATM>(p, G, smem, st);
+    case kTcQ5KG: return launch_tc<kTcQ5KG, ATM>(p, G, smem, st);
+    case kTcQ5KN: return launch_tc<kTcQ5KN, ATM>(p, G, smem, st);
+    default: return launch_tc<kTcMixed, ATM>(p, G, smem, st);
+  }
 }
 
 // Batched decode GEMV; -1 if not covered.  workspace: tc_workspace_bytes(K)
@@ -990,18 +1122,24 @@ int run_gemv_tc(const nsq_segment* segs, int nseg, const float* x, int64_t M, in
   p.ws_b = ws + 1024;
   p.ws_col = p.ws_b + (size_t)NSB * 4 * TC_B_BYTES;
   p.ws_part = reinterpret_cast<float*>(const_cast<uint8_t*>(p.ws_col) + (size_t)NSB * TC_COL_BYTES);
-  // Shared memory: two unit slots of A and B tiles when they fit beside two
-  // raw columns, so that the dequant warps and the B producer fill a unit
-  // while the MMAs of the one before still read theirs: Q4_K, Q4_0, and a
-  // single-format Q6_K launch, which leaves out the min-term tiles; otherwise
-  // one unit slot and up to four raw columns.
+  // A in TMEM (the default): two unit slots of A in TMEM beside the
+  // accumulators, their B tiles in shared memory, and as many raw columns as
+  // fit (up to 8).  A in shared memory: two unit slots of A and B tiles when
+  // they fit beside two raw columns, so that the dequant warps and the B
+  // producer fill a unit while the MMAs of the one before still read theirs:
+  // Q4_K, Q4_0, and a single-format Q6_K launch, which leaves out the
+  // min-term tiles; otherwise one unit slot and up to four raw columns.
   const bool hm = code == kTcMixed || code == kTcQ4K || code == kTcQ5KG || code == kTcQ5KN;
+  const bool atm = tune(kTuneTcA, 1) != 0;
   auto smem_of = [&](int us, int r) {
-    return 1024 + (size_t)us * (TC_UA_BYTES + tc_ub_bytes(hm)) + (hm ? TC_A_BYTES : 0) +
+    return 1024 + (size_t)us * ((atm ? 0 : TC_UA_BYTES) + tc_ub_bytes(hm)) + (hm ? TC_A_BYTES : 0) +
            (size_t)TC_SCL_STAGES * TC_BN * 4 + (size_t)TC_NACC * TC_BM * 8 + 1024 + (size_t)r * TC_BM * pitch;
   };
   int us = 2, rs = 2;
-  if (smem_of(us, rs) > (size_t)TC_SMEM_LIMIT) {
+  if (atm) {
+    rs = 8;
+    while (smem_of(us, rs) > (size_t)TC_SMEM_LIMIT && rs > 2) --rs;
+  } else if (smem_of(us, rs) > (size_t)TC_SMEM_LIMIT) {
     us = 1;
     rs = 4;
     while (smem_of(us, rs) > (size_t)TC_SMEM_LIMIT && rs > 2) --rs;
@@ -1029,17 +1167,7 @@ int run_gemv_tc(const nsq_segment* segs, int nseg, const float* x, int64_t M, in
                            const_cast<uint8_t*>(p.ws_col), p.ws_cnt) != cudaSuccess)
       return NSQ_ERR_CUDA;
   }
-  cudaError_t e;
-  switch (code) {
-    case kTcQ4K: e = launch_tc<kTcQ4K>(p, G, smem, st); break;
-    case kTcQ6KG: e = launch_tc<kTcQ6KG>(p, G, smem, st); break;
-    case kTcQ40: e = launch_tc<kTcQ40>(p, G, smem, st); break;
-    case kTcQ80: e = launch_tc<kTcQ80>(p, G, smem, st); break;
-    case kTcQ6KN: e = launch_tc<kTcQ6KN>(p, G, smem, st); break;
-    case kTcQ5KG: e = launch_tc<kTcQ5KG>(p, G, smem, st); break;
-    case kTcQ5KN: e = launch_tc<kTcQ5KN>(p, G, smem, st); break;
-    default: e = launch_tc<kTcMixed>(p, G, smem, st); break;
-  }
+  const cudaError_t e = atm ? launch_code<true>(code, p, G, smem, st) : launch_code<false>(code, p, G, smem, st);
   return e == cudaSuccess ? NSQ_OK : NSQ_ERR_CUDA;
 }
 

@@ -245,6 +245,11 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -271,7 +276,7 @@ __device__ __forceinline__ bool wait_geq_bounded(const uint32_t* p, uint32_t wan
 enum TuneId : int {
   kTuneRowsR, kTuneRowsPPSM, kTuneRowsStages, kTuneRowsPre, kTuneRowsL2Hint, kTuneRowsCPS, kTuneRowsC,
   kTuneRowsBal, kTuneRowsCarve, kTuneMmaMinM, kTuneMmaPPS, kTuneMmaStages, kTuneGemvGeneral, kTuneGemmSplit,
-  kTuneGemmTok, kTuneTcMinM, kTuneCount
+  kTuneGemmTok, kTuneTcMinM, kTuneTcA, kTuneCount
 };
 int tune(TuneId id, int dflt);
 // Counts one kernel launch (nsq_kernel_launches).

@@ -106,3 +106,23 @@ def test_tc_every_format_in_one_launch(eng, oracle, m):
                           torch.from_numpy(x).to(eng.device), k)
     for w, (t, l, n), y in zip(ws, specs, outs):
         assert rel_err(y.cpu().numpy(), oracle.quant_matmul(w, t, x, n, k, l, threads=8)) <= GEMV_TOL
+
+
+@pytest.mark.parametrize("a_in", ["1", "0"])
+@pytest.mark.parametrize("tid,layout", [("Q4_K", 0), ("Q6_K", 0), ("Q6_K", 1), ("Q5_K", 0), ("Q5_K", 1),
+                                        ("Q4_0", 0), ("Q8_0", 0)])
+def test_tc_a_operand_in_tmem_and_smem(eng, oracle, tuning, a_in, tid, layout):
+    """Both homes of the fp16 weight operand (NSQ_TC_A=1: tensor memory, written
+    by tcgen05.st and read by the MMA's A-from-TMEM form; 0: 128B-swizzled
+    shared-memory tiles), every format and layout, against the oracle on a
+    stream-K shape (tiles split over CTAs) at 16 and 7 tokens."""
+    from planejaja_b200 import formats as F
+    t = getattr(F, tid)
+    tuning.set("NSQ_TC_A", a_in)
+    n, k = 1100, 4096
+    w = Q.synthetic_weights(n, k, t, seed=50 + layout, q6k_layout=layout)
+    wd = eng.upload(w)
+    for m in (16, 7):
+        x = Q.synthetic_activations(m, k, seed=51 + m)
+        y = eng.gemv(wd, t, torch.from_numpy(x).to(eng.device), n, k, q6k_layout=layout).cpu().numpy()
+        assert rel_err(y, oracle.quant_matmul(w, t, x, n, k, layout, threads=8)) <= GEMV_TOL
