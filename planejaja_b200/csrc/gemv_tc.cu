@@ -299,36 +299,56 @@ __device__ __forceinline__ uint32_t q4k_scale_min(uint32_t S0, uint32_t S1, uint
 
 // Q6_K (ggml) stage q = 64 weights of half n = q / 2: chunk k8 = p + 4h is
 // group j = 2(q & 1) + h, elements l = 8p .. 8p + 7: ql[64n + 32(j & 1) + l]
-// nibble (q & 1), qh[32n + l] bits 2j, scale sc[8n + 2j + p / 2].  The 6-bit
+// nibble (q & 1), qh[32n + l] bits 2j, scale sc[8n + 2j + l / 16].  The 6-bit
 // value enters as fp16 64 + 4q/16 and (4 sc) * v - 288 sc = sc (q - 32).
-__device__ __forceinline__ void q6k_pair(const uint8_t* raw, int q, int p, uint32_t ql_shift, uint4& c0, uint4& c1,
-                                         int off16) {
-  const int n = q >> 1, j0 = 2 * (q & 1);
-  uint32_t la[2], lb[2], h[2];
-  // raw is 2-byte aligned inside the column's 16-byte span (off16 = its
-  // offset); the qh / ql byte runs are read with unaligned word loads
-  ld_words_unaligned<2>(raw + 64 * n + 8 * p, la);
-  ld_words_unaligned<2>(raw + 64 * n + 32 + 8 * p, lb);
-  ld_words_unaligned<2>(raw + 128 + 32 * n + 8 * p, h);
-  (void)off16;
-  const int8_t sa = (int8_t)raw[192 + 8 * n + 2 * j0 + (p >> 1)];
-  const int8_t sb = (int8_t)raw[192 + 8 * n + 2 * (j0 + 1) + (p >> 1)];
-  const __half2 s4a = __half2half2(__int2half_rn(4 * sa)), s4b = __half2half2(__int2half_rn(4 * sb));
-  const __half2 ca = __half2half2(__int2half_rn(-288 * sa)), cb = __half2half2(__int2half_rn(-288 * sb));
+// The stage's four int8 scales are one word (bytes 8n + 2j0 .. + 3): each
+// byte s + 128 beside 0x64 is fp16 1024 + s + 128, less 1152 it is s, and
+// 4 s and -288 s are exact in fp16.  `raw` is 2-byte aligned inside the
+// column's 16-byte span; ALIGNED4 when it is 4-byte aligned (the same for
+// every row of a unit), else the byte runs are read as shifted words.
+template <bool ALIGNED4>
+__device__ __forceinline__ void q6k_stage(const uint8_t* raw, int q, uint4 (&ch)[8]) {
+  const int n = q >> 1, j0 = 2 * (q & 1), sh = 4 * (q & 1);
+  uint32_t la[8], lb[8], hh[8], scw;
+  if constexpr (ALIGNED4) {
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(raw);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      la[i] = w[16 * n + i];
+      lb[i] = w[16 * n + 8 + i];
+      hh[i] = w[32 + 8 * n + i];
+    }
+    scw = w[48 + 2 * n + (j0 >> 1)];
+  } else {
+    uint32_t sw1[1];
+    ld_words_unaligned<8>(raw + 64 * n, la);
+    ld_words_unaligned<8>(raw + 64 * n + 32, lb);
+    ld_words_unaligned<8>(raw + 128 + 32 * n, hh);
+    ld_words_unaligned<1>(raw + 192 + 8 * n + 2 * j0, sw1);
+    scw = sw1[0];
+  }
+  const uint32_t sb = scw ^ 0x80808080u;
+  const __half2 k1152 = __float2half2_rn(1152.f);
+  const __half2 sA = __hsub2(magic2(sb, 0x64646464u, 0x4140), k1152);  // group j0: l < 16, l >= 16
+  const __half2 sB = __hsub2(magic2(sb, 0x64646464u, 0x4342), k1152);  // group j0 + 1
+  const __half2 s4A = __hmul2(sA, __float2half2_rn(4.f)), s4B = __hmul2(sB, __float2half2_rn(4.f));
+  const __half2 cA = __hmul2(sA, __float2half2_rn(-288.f)), cB = __hmul2(sB, __float2half2_rn(-288.f));
   const uint32_t K54 = 0x54545454u;
 #pragma unroll
-  for (int i = 0; i < 2; ++i) {
+  for (int w = 0; w < 8; ++w) {  // elements 4w .. 4w + 3 of both groups
+    const __half2 ma = w < 4 ? __low2half2(s4A) : __high2half2(s4A), ca = w < 4 ? __low2half2(cA) : __high2half2(cA);
+    const __half2 mb = w < 4 ? __low2half2(s4B) : __high2half2(s4B), cb = w < 4 ? __low2half2(cB) : __high2half2(cB);
     // 4q as bytes: ((ql >> shift) & 15) << 2 | ((qh >> 2j) & 3) << 6
-    const uint32_t qa = (((la[i] >> ql_shift) & 0x0F0F0F0Fu) << 2) | (((h[i] >> (2 * j0)) & 0x03030303u) << 6);
-    const uint32_t qb = (((lb[i] >> ql_shift) & 0x0F0F0F0Fu) << 2) | (((h[i] >> (2 * j0 + 2)) & 0x03030303u) << 6);
-    const uint32_t a01 = h2_bits(__hfma2(magic2(qa, K54, 0x4140), s4a, ca));
-    const uint32_t a23 = h2_bits(__hfma2(magic2(qa, K54, 0x4342), s4a, ca));
-    const uint32_t b01 = h2_bits(__hfma2(magic2(qb, K54, 0x4140), s4b, cb));
-    const uint32_t b23 = h2_bits(__hfma2(magic2(qb, K54, 0x4342), s4b, cb));
-    if (i == 0) {
-      c0.x = a01; c0.y = a23; c1.x = b01; c1.y = b23;
+    const uint32_t qa = (((la[w] >> sh) & 0x0F0F0F0Fu) << 2) | (((hh[w] >> (2 * j0)) & 0x03030303u) << 6);
+    const uint32_t qb = (((lb[w] >> sh) & 0x0F0F0F0Fu) << 2) | (((hh[w] >> (2 * j0 + 2)) & 0x03030303u) << 6);
+    const uint32_t a01 = h2_bits(__hfma2(magic2(qa, K54, 0x4140), ma, ca));
+    const uint32_t a23 = h2_bits(__hfma2(magic2(qa, K54, 0x4342), ma, ca));
+    const uint32_t b01 = h2_bits(__hfma2(magic2(qb, K54, 0x4140), mb, cb));
+    const uint32_t b23 = h2_bits(__hfma2(magic2(qb, K54, 0x4342), mb, cb));
+    if (w & 1) {
+      ch[w >> 1].z = a01; ch[w >> 1].w = a23; ch[4 + (w >> 1)].z = b01; ch[4 + (w >> 1)].w = b23;
     } else {
-      c0.z = a01; c0.w = a23; c1.z = b01; c1.w = b23;
+      ch[w >> 1].x = a01; ch[w >> 1].y = a23; ch[4 + (w >> 1)].x = b01; ch[4 + (w >> 1)].y = b23;
     }
   }
 }
@@ -511,8 +531,8 @@ __device__ __forceinline__ void tc_stage(int code, const uint8_t* raw, int q, in
   } else if (code == kTcQ6KG) {
     if (HM) *reinterpret_cast<uint32_t*>(a2row + ((a2c ^ sw) << 4) + 4 * q) = 0u;
     if (q == 0) *dsc_row = make_float2(h2f((uint16_t)ld_u16(raw + 208)), 0.f);
-#pragma unroll
-    for (int pp = 0; pp < 4; ++pp) q6k_pair(raw, q, pp, 4 * (q & 1), ch[pp], ch[pp + 4], off16);
+    if ((off16 & 3) == 0) q6k_stage<true>(raw, q, ch);
+    else q6k_stage<false>(raw, q, ch);
   } else if (code == kTcQ6KN) {
     if (HM) *reinterpret_cast<uint32_t*>(a2row + ((a2c ^ sw) << 4) + 4 * q) = 0u;
     if (q == 0) *dsc_row = make_float2(h2f((uint16_t)ld_u16(raw + 208)) * 0.015625f, 0.f);
