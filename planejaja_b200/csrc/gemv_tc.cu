@@ -506,18 +506,20 @@ __device__ __forceinline__ void tc_stage(int code, const uint8_t* raw, int q, in
   if (code == kTcQ4K || code == kTcQ5KG || code == kTcQ5KN) {
     // Q4_K and Q5_K share the header: d, dmin, the packed 6-bit scales and mins
     const uint4 hdr = *reinterpret_cast<const uint4*>(raw);
-    const uint32_t sm0 = q4k_scale_min(hdr.y, hdr.z, hdr.w, 2 * q);
-    const uint32_t sm1 = q4k_scale_min(hdr.y, hdr.z, hdr.w, 2 * q + 1);
-    *reinterpret_cast<uint32_t*>(a2row + ((a2c ^ sw) << 4) + 4 * q) =
-        h2_bits(__halves2half2(__uint2half_rn(sm0 >> 8), __uint2half_rn(sm1 >> 8)));
+    // bytes sc_2q, m_2q, sc_2q+1, m_2q+1 (each below 64): fp16 1024 + byte
+    // less 1024 gives each exactly
+    const uint32_t smw = q4k_scale_min(hdr.y, hdr.z, hdr.w, 2 * q) | (q4k_scale_min(hdr.y, hdr.z, hdr.w, 2 * q + 1) << 16);
+    const __half2 k1024 = __float2half2_rn(1024.f);
+    const __half2 scs = __hsub2(magic2(smw, 0x64646464u, 0x4240), k1024);
+    const __half2 mns = __hsub2(magic2(smw, 0x64646464u, 0x4341), k1024);
+    *reinterpret_cast<uint32_t*>(a2row + ((a2c ^ sw) << 4) + 4 * q) = h2_bits(mns);
     if (q == 0) {
       const float d = h2f((uint16_t)(hdr.x & 0xFFFF)), dmin = h2f((uint16_t)(hdr.x >> 16));
       *dsc_row = make_float2(d, 32.0f * dmin);
     }
-    const __half h0 = __uint2half_rn(sm0 & 0xFF), h1 = __uint2half_rn(sm1 & 0xFF);
-    const __half2 s0 = __half2half2(h0), s1 = __half2half2(h1);
-    const __half2 b0 = __half2half2(__hmul(h0, __float2half_rn(-1024.f)));
-    const __half2 b1 = __half2half2(__hmul(h1, __float2half_rn(-1024.f)));
+    const __half2 s0 = __low2half2(scs), s1 = __high2half2(scs);
+    const __half2 bb = __hmul2(scs, __float2half2_rn(-1024.f));
+    const __half2 b0 = __low2half2(bb), b1 = __high2half2(bb);
     if (code == kTcQ4K) {
 #pragma unroll
       for (int pp = 0; pp < 4; ++pp) q4k_pair(raw, q, pp, s0, b0, s1, b1, ch[pp], ch[pp + 4]);
