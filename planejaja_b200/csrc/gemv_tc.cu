@@ -450,8 +450,9 @@ __device__ __forceinline__ void q6kn_stage(const uint8_t* raw, int q, uint4 (&ch
 struct TcCursor {
   int sg = 0, tl = 0, c = 0, t = 0;
   __device__ void init(const TcParams& p, int64_t u) {
-    t = (int)(u / p.NSB);
-    c = (int)(u - (int64_t)t * p.NSB);
+    // 32-bit: the host keeps U * (G + 1) below 2^32
+    t = (int)((uint32_t)u / (uint32_t)p.NSB);
+    c = (int)((uint32_t)u - (uint32_t)t * (uint32_t)p.NSB);
     sg = 0;
     while (sg + 1 < p.nseg && t >= p.seg[sg + 1].tile0) ++sg;
     tl = t - p.seg[sg].tile0;
@@ -491,8 +492,14 @@ __device__ __forceinline__ void tc_store_y(const TcParams& p, const TcSeg& S, in
   }
 }
 
-// CTA index owning unit u (unit ranges [U i / G, U (i+1) / G)).
-__device__ __forceinline__ int tc_owner(int64_t u, int64_t U, int G) { return (int)(((u + 1) * G - 1) / U); }
+// First unit of CTA i, and the CTA owning unit u (unit ranges [U i / G,
+// U (i+1) / G)), in 32-bit arithmetic: the host keeps U * (G + 1) below 2^32.
+__device__ __forceinline__ int64_t tc_first(int64_t U, int i, int G) {
+  return (int64_t)(((uint32_t)U * (uint32_t)i) / (uint32_t)G);
+}
+__device__ __forceinline__ int tc_owner(int64_t u, int64_t U, int G) {
+  return (int)(((uint32_t)(u + 1) * (uint32_t)G - 1u) / (uint32_t)U);
+}
 
 // One row's K stage q (64 weights) of a unit: the fp16 A chunks in natural K
 // order (chunk k8 = K 8 k8 .. 8 k8 + 7 of the stage), word q of the row's
@@ -589,7 +596,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = (int)gridDim.x;
-  const int64_t u0 = p.U * blockIdx.x / G, u1 = p.U * (blockIdx.x + 1) / G;
+  const int64_t u0 = tc_first(p.U, (int)blockIdx.x, G), u1 = tc_first(p.U, (int)blockIdx.x + 1, G);
   const int nunits = (int)(u1 - u0);
 
   // ---- raw producer (thread 0): per unit one 2-D TMA box [128 rows x one
@@ -957,7 +964,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
               for (int t = 0; t < TC_BN; ++t) sum[t] += acc[t];
               continue;
             }
-            const int64_t ui0 = p.U * i / G;
+            const int64_t ui0 = tc_first(p.U, i, G);
             const int sl = 2 * i + ((i == i_first && ui0 < ut0) ? 1 : 0);
             const float4* src = reinterpret_cast<const float4*>(p.ws_part + ((int64_t)sl * TC_BM + row) * TC_BN);
 #pragma unroll
@@ -1173,6 +1180,7 @@ int run_gemv_tc(const nsq_segment* segs, int nseg, const float* x, int64_t M, in
   int G = num_sms > 0 ? num_sms : 148;
   if (G > TC_GMAX) G = TC_GMAX;
   if ((int64_t)G > p.U) G = (int)p.U;
+  if (p.U * (G + 1) >= ((int64_t)1 << 32)) return -1;  // the unit arithmetic is 32-bit
   // activations -> fp16 B tiles, min-term tiles, scales; counters zeroed
   {
     cudaLaunchConfig_t cfg = {};
