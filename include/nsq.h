@@ -125,10 +125,10 @@ int nsq_dequant(const void *w, int ggml_type, int q6k_layout, int out_dtype, voi
  * not needed); the GEMV accumulates exact integer dot products per 16 or 32
  * weights and combines them in fp32.
  *
- * For 5..16 tokens over Q4_K, ggml-layout Q6_K, Q4_0 and Q8_0 (K % 256 == 0)
- * the GEMV runs on the tcgen05 tensor cores: the 6-bit sub-scales folded into
- * fp16 weight operands (exact products; Q4_0 / Q8_0 fold their block scale,
- * rounded once to fp16), x as fp16 hi + lo parts (22 bits), fp32
+ * For 5..16 tokens over every format and layout (K % 256 == 0) the GEMV runs
+ * on the tcgen05 tensor cores: the 6-bit sub-scales folded into fp16 weight
+ * operands held in tensor memory (exact products; Q4_0 / Q8_0 fold their
+ * block scale, rounded once to fp16), x as fp16 hi + lo parts (22 bits), fp32
  * accumulation, one fp32 epilogue per 256 weights.  Its workspace (fp16
  * activation tiles and split-tile partial sums, about 21 KB per 256 of K
  * plus 4 MiB) is what nsq_gemv_workspace_size returns for M >= 2; with a
