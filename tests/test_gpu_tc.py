@@ -7,7 +7,9 @@ Covered beside the parity suites (which run it as their "tc" kernel):
     the same bits;
   * Q6_K scales whose products sc * (q - 32) exceed 2048 (fp16 then rounds
     them to even integers): still within the GEMV tolerance of the oracle;
-  * mixed q|k|v segments (Q4_K, Q4_K, Q6_K) in one launch.
+  * mixed q|k|v segments (Q4_K, Q4_K, Q6_K) in one launch;
+  * every format and layout with the fp16 weight operand in tensor memory (the
+    default) and in shared memory (NSQ_TC_A=0).
 """
 import numpy as np
 import pytest
